@@ -1,0 +1,638 @@
+// Grouped (per-expert) GEMM for the MoE expert FFN on B200 tensor cores.
+//
+//   out[r, :] = x[r, :] @ W[widx(g)]^T     for every row r of group g
+//
+// x is [rows, K] bf16 (K contiguous), W is [num_w, N, K] bf16 ("[out,in]",
+// K contiguous), i.e. both operands are K-major, which is the native operand
+// form of tcgen05.mma. The reference computes the same thing as a Python loop
+// of torch.mm over uniform splits (kernel_cases/case03_moe_grouped_gemm_fc1_fwd
+// .py:57-64, case04_moe_grouped_gemm_fc2_fwd.py:57-64); here the groups are
+// ragged and described by a device-side table, so no host sync is needed.
+//
+// Kernel structure (one persistent CTA per SM, 192 threads):
+//   warp 0      TMA producer: 128x64 A tile + 2 x 128x64 B half-tiles per
+//               stage, 128-byte swizzle, 4-stage mbarrier ring.
+//   warp 1      TMEM owner (512 columns = two 128x256 fp32 accumulators) and
+//               single-thread tcgen05.mma issuer (M=128, N=256, K=16).
+//   warps 2-5   epilogue: tcgen05.ld (32 lanes x 32 columns), bf16 convert
+//               (or SwiGLU for fc1), predicated 16-byte global stores.
+// Two accumulators let the epilogue of tile i overlap the mainloop of i+1.
+// Tiles are walked group by group; inside a group, super-rows of 16 M-tiles
+// sweep all N-tiles so that concurrently running CTAs share both the weight
+// slab and the activation rows in L2.
+//
+// Every wait is bounded (2 s); on timeout the kernel records an error word in
+// the workspace, drains its own in-flight copies and MMAs, frees TMEM and
+// returns. No TMA multicast and no cluster launch are used.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "moe_common.cuh"
+#include "swiglu.cuh"
+
+namespace moe {
+namespace gg {
+
+constexpr int BM = 128;
+constexpr int BN = 256;
+constexpr int BK = 64;
+constexpr int kStages = 4;
+constexpr int kSuperRow = 16;  // M-tiles per raster super-row
+constexpr int kThreads = 192;
+constexpr uint32_t kABytes = BM * BK * 2;           // 16 KB
+constexpr uint32_t kBHalfBytes = 128 * BK * 2;      // 16 KB
+constexpr uint32_t kBBytes = BN * BK * 2;           // 32 KB
+constexpr uint32_t kStageBytes = kABytes + kBBytes;  // 48 KB
+constexpr uint32_t kTmemCols = 2 * BN;              // 512
+constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + 256;
+
+// Device error codes written to the workspace error word.
+constexpr int kErrTimeoutProducer = 1;
+constexpr int kErrTimeoutMma = 2;
+constexpr int kErrTimeoutEpilogue = 3;
+
+struct Params {
+  const int32_t* row_start;
+  const int32_t* rows;
+  const int32_t* widx;
+  int32_t* err;
+  __nv_bfloat16* out;
+  int64_t x_rows;
+  int G;
+  int n_w;     // rows of one weight matrix (N)
+  int n_out;   // output columns (N, or N/2 for SwiGLU)
+  int f_half;  // N/2 (SwiGLU up-row offset)
+  int num_kb;
+  int n_tiles;
+  int epilogue;
+};
+
+struct Tile {
+  int g;
+  int m_idx;
+  int n_idx;
+};
+
+// Maps a linear tile index to (group, m-tile, n-tile). Tile indices handed to
+// one CTA increase monotonically, so the walker only moves forward.
+struct Walker {
+  const int32_t* rows;
+  int G;
+  int n_tiles;
+  int g = 0;
+  int mt = -1;
+  long long base = 0;
+
+  __device__ bool locate(long long t, Tile& tile) {
+    while (g < G) {
+      if (mt < 0) mt = (max(rows[g], 0) + BM - 1) / BM;
+      const long long cnt = static_cast<long long>(mt) * n_tiles;
+      if (t < base + cnt) break;
+      base += cnt;
+      ++g;
+      mt = -1;
+    }
+    if (g >= G) return false;
+    const long long local = t - base;
+    const long long sr_tiles = static_cast<long long>(kSuperRow) * n_tiles;
+    const int sr = static_cast<int>(local / sr_tiles);
+    const int within = static_cast<int>(local - sr * sr_tiles);
+    const int mg = min(kSuperRow, mt - sr * kSuperRow);
+    tile.g = g;
+    tile.n_idx = within / mg;
+    tile.m_idx = sr * kSuperRow + within % mg;
+    return true;
+  }
+};
+
+MOE_DEVICE bool wait_drain(uint32_t bar, uint32_t parity) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity)) {
+    if (globaltimer_ns() - t0 > kWaitTimeoutNs) return false;
+  }
+  return true;
+}
+
+MOE_DEVICE void raise_abort(volatile int* abort_flag, int32_t* err, int code) {
+  atomicCAS(err, 0, code);
+  *abort_flag = 1;
+  __threadfence_block();
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                        const __grid_constant__ CUtensorMap tmap_b, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw_addr);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base_ptr + kStages * kStageBytes);
+  const uint32_t bar0 = smem_u32(bars);
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (kStages + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * kStages + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * kStages + 2 + a); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * kStages + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  Walker walker{p.rows, p.G, p.n_tiles};
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol_a = l2_policy_evict_normal();
+      const uint64_t pol_b = l2_policy_evict_normal();
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued[kStages];
+#pragma unroll
+      for (int s = 0; s < kStages; ++s) issued[s] = -1;
+      bool ok = true;
+      for (long long t = blockIdx.x; ok; t += gridDim.x) {
+        Tile tile;
+        if (!walker.locate(t, tile)) break;
+        const int row0 = p.row_start[tile.g] + tile.m_idx * BM;
+        const int wbase = p.widx[tile.g] * p.n_w;
+        int b0, b1;
+        if (p.epilogue == 1) {
+          b0 = wbase + tile.n_idx * 128;
+          b1 = b0 + p.f_half;
+        } else {
+          b0 = wbase + tile.n_idx * BN;
+          b1 = b0 + 128;
+        }
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = base + stage * kStageBytes;
+          const uint32_t sb = sa + kABytes;
+          mbar_arrive_expect_tx(full_bar(stage), kStageBytes);
+          tma_load_2d(sa, &tmap_a, kb * BK, row0, full_bar(stage), pol_a);
+          tma_load_2d(sb, &tmap_b, kb * BK, b0, full_bar(stage), pol_b);
+          tma_load_2d(sb + kBHalfBytes, &tmap_b, kb * BK, b1, full_bar(stage), pol_b);
+          issued[stage] = static_cast<int>(phase);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        raise_abort(abort_flag, p.err, kErrTimeoutProducer);
+        // Let every copy this thread started land before shared memory goes away.
+        for (int s = 0; s < kStages; ++s)
+          if (issued[s] >= 0) wait_drain(full_bar(s), static_cast<uint32_t>(issued[s]));
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16_f32(BM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (long long t = blockIdx.x; ok; t += gridDim.x) {
+        Tile tile;
+        if (!walker.locate(t, tile)) break;
+        const int acc = it & 1;
+        const uint32_t aph = static_cast<uint32_t>((it >> 1) & 1);
+        if (!mbar_wait(tempty_bar(acc), aph ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = base + stage * kStageBytes;
+          const uint32_t sb = sa + kABytes;
+          const uint64_t ad = umma_desc_k_sw128(sa);
+          const uint64_t bd = umma_desc_k_sw128(sb);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            // +32 bytes along K inside the 128-byte swizzle atom = +2 in the
+            // 16-byte-unit start-address field.
+            umma_bf16(d_tmem, ad + 2ull * k, bd + 2ull * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          }
+          issued_any = true;
+          umma_commit(empty_bar(stage));
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar(acc));
+        ++it;
+      }
+      if (!ok) {
+        raise_abort(abort_flag, p.err, kErrTimeoutMma);
+        if (issued_any) {
+          umma_commit(drain_bar);
+          wait_drain(drain_bar, 0);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;  // TMEM lanes this warp may access: 32*quad ..
+    const int r_in_tile = quad * 32 + lane;
+    int it = 0;
+    bool ok = true;
+    for (long long t = blockIdx.x;; t += gridDim.x) {
+      Tile tile;
+      if (!walker.locate(t, tile)) break;
+      const int acc = it & 1;
+      const uint32_t aph = static_cast<uint32_t>((it >> 1) & 1);
+      if (!mbar_wait(tfull_bar(acc), aph, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int m_local = tile.m_idx * BM + r_in_tile;
+      const int64_t row = static_cast<int64_t>(p.row_start[tile.g]) + m_local;
+      const bool rvalid = m_local < p.rows[tile.g] && row < p.x_rows;
+      const uint32_t tbase =
+          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      if (p.epilogue == 0) {
+        const int n0 = tile.n_idx * BN;
+        __nv_bfloat16* orow = p.out + row * p.n_out;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, r);
+          tmem_ld_wait();
+          if (rvalid) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const int col = n0 + c * 32 + v * 8;
+              if (col + 8 <= p.n_out) {
+                uint4 o;
+                o.x = pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
+                o.y = pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
+                o.z = pack_bf16x2(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
+                o.w = pack_bf16x2(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
+                *reinterpret_cast<uint4*>(orow + col) = o;
+              }
+            }
+          }
+        }
+      } else {
+        const int n0 = tile.n_idx * 128;
+        __nv_bfloat16* orow = p.out + row * p.n_out;
+#pragma unroll 1
+        for (int c = 0; c < 128 / 32; ++c) {
+          uint32_t gr[32], ur[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, gr);
+          tmem_ld_32x32b_x32(tbase + 128 + c * 32, ur);
+          tmem_ld_wait();
+          if (rvalid) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const int col = n0 + c * 32 + v * 8;
+              if (col + 8 <= p.n_out) {
+                uint32_t o[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const int j = v * 8 + 2 * q;
+                  const float h0 = swiglu_f32(round_bf16(__uint_as_float(gr[j])),
+                                              round_bf16(__uint_as_float(ur[j])));
+                  const float h1 = swiglu_f32(round_bf16(__uint_as_float(gr[j + 1])),
+                                              round_bf16(__uint_as_float(ur[j + 1])));
+                  o[q] = pack_bf16x2(h0, h1);
+                }
+                *reinterpret_cast<uint4*>(orow + col) = make_uint4(o[0], o[1], o[2], o[3]);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(acc));
+      ++it;
+    }
+    if (!ok && lane == 0) raise_abort(abort_flag, p.err, kErrTimeoutEpilogue);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// Group-table construction (single block).
+// mode 0: contiguous groups from splits, group g starts at the padded prefix.
+// mode 1: expert-parallel receive layout, see moe_grouped_gemm_plan_ep.
+// ---------------------------------------------------------------------------
+__global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ counts, int n,
+                                                    int mode, int num_src, int num_w,
+                                                    int64_t align, int32_t* __restrict__ err,
+                                                    int32_t* __restrict__ row_start,
+                                                    int32_t* __restrict__ rows,
+                                                    int32_t* __restrict__ widx,
+                                                    int32_t* __restrict__ tmp) {
+  __shared__ int64_t warp_sums[32];
+  __shared__ int64_t carry_s;
+  const int lane = lane_id(), wid = warp_id();
+  if (threadIdx.x == 0) {
+    *err = 0;
+    carry_s = 0;
+  }
+  __syncthreads();
+  for (int i0 = 0; i0 < n; i0 += 1024) {
+    const int i = i0 + threadIdx.x;
+    int64_t padded = 0;
+    if (i < n) {
+      const int64_t c = max(counts[i], 0);
+      padded = (align > 1) ? ((c + align - 1) / align) * align : c;
+    }
+    int64_t incl = padded;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int64_t y = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += y;
+    }
+    if (lane == 31) warp_sums[wid] = incl;
+    __syncthreads();
+    if (wid == 0) {
+      const int64_t ws = warp_sums[lane];
+      int64_t wincl = ws;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int64_t y = __shfl_up_sync(0xffffffffu, wincl, off);
+        if (lane >= off) wincl += y;
+      }
+      warp_sums[lane] = wincl - ws;
+    }
+    __syncthreads();
+    const int64_t cbase = carry_s;
+    if (i < n) tmp[i] = static_cast<int32_t>(cbase + warp_sums[wid] + incl - padded);
+    __syncthreads();
+    if (threadIdx.x == 1023) carry_s = cbase + warp_sums[wid] + incl;
+    __syncthreads();
+  }
+  for (int g = threadIdx.x; g < n; g += 1024) {
+    int f = g, w = g;
+    if (mode == 1) {
+      const int e = g / num_src, s = g - e * num_src;
+      f = s * num_w + e;
+      w = e;
+    }
+    row_start[g] = tmp[f];
+    rows[g] = max(counts[f], 0);
+    widx[g] = w;
+  }
+}
+
+struct WsLayout {
+  int32_t* err;
+  int32_t* row_start;
+  int32_t* rows;
+  int32_t* widx;
+  int32_t* tmp;
+};
+
+size_t ws_array_bytes(int64_t G) {
+  return (static_cast<size_t>(G) * 4 + 255) & ~static_cast<size_t>(255);
+}
+size_t ws_bytes(int64_t G) { return 256 + 4 * ws_array_bytes(G); }
+
+WsLayout ws_layout(const void* ws, int64_t G) {
+  char* b = static_cast<char*>(const_cast<void*>(ws));
+  const size_t a = ws_array_bytes(G);
+  WsLayout l;
+  l.err = reinterpret_cast<int32_t*>(b);
+  l.row_start = reinterpret_cast<int32_t*>(b + 256);
+  l.rows = reinterpret_cast<int32_t*>(b + 256 + a);
+  l.widx = reinterpret_cast<int32_t*>(b + 256 + 2 * a);
+  l.tmp = reinterpret_cast<int32_t*>(b + 256 + 3 * a);
+  return l;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// 2-D bf16 tensor map over a row-major [outer, inner] matrix, box 64 x 128,
+// 128-byte swizzle (one box row = one 128-byte swizzle row).
+int make_tmap(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer) {
+  auto encode = get_encode_fn();
+  if (encode == nullptr) {
+    set_last_error("grouped_gemm: cuTensorMapEncodeTiled unavailable");
+    return MOE_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), 128u};
+  cuuint32_t estr[2] = {1u, 1u};
+  const CUresult r = encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
+                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_last_error("grouped_gemm: cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return MOE_ERR_CUDA;
+  }
+  return MOE_OK;
+}
+
+int ensure_smem_attr() {
+  int dev = 0;
+  MOE_CUDA_CALL(cudaGetDevice(&dev), "cudaGetDevice");
+  static std::mutex mu;
+  static bool done[64] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 64 && done[dev]) return MOE_OK;
+  MOE_CUDA_CALL(cudaFuncSetAttribute(grouped_gemm_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(kSmemBytes)),
+                "cudaFuncSetAttribute(grouped_gemm)");
+  if (dev < 64) done[dev] = true;
+  return MOE_OK;
+}
+
+}  // namespace gg
+}  // namespace moe
+
+using namespace moe;
+
+extern "C" int moe_grouped_gemm_workspace_size(int64_t G, size_t* bytes) {
+  MOE_REQUIRE(bytes != nullptr, "grouped_gemm_workspace_size: null output");
+  MOE_REQUIRE(G >= 1 && G <= (1 << 24), "grouped_gemm: G=%lld out of range", (long long)G);
+  *bytes = gg::ws_bytes(G);
+  return MOE_OK;
+}
+
+static int check_ws(const void* ws, size_t bytes, int64_t G) {
+  MOE_REQUIRE(ws != nullptr && bytes >= gg::ws_bytes(G),
+              "grouped_gemm: workspace too small (%zu < %zu)", bytes, gg::ws_bytes(G));
+  MOE_REQUIRE((reinterpret_cast<uintptr_t>(ws) & 255) == 0,
+              "grouped_gemm: workspace must be 256-byte aligned");
+  return MOE_OK;
+}
+
+extern "C" int moe_grouped_gemm_plan_splits(const int32_t* m_splits, int64_t G, int64_t align,
+                                            void* workspace, size_t workspace_bytes,
+                                            moe_stream_t stream) {
+  MOE_REQUIRE(G >= 1 && G <= (1 << 24), "grouped_gemm_plan: G=%lld out of range", (long long)G);
+  MOE_REQUIRE(align >= 1 && align <= 4096, "grouped_gemm_plan: align=%lld out of [1,4096]",
+              (long long)align);
+  MOE_REQUIRE(m_splits != nullptr, "grouped_gemm_plan: null m_splits");
+  int st = check_ws(workspace, workspace_bytes, G);
+  if (st) return st;
+  gg::WsLayout l = gg::ws_layout(workspace, G);
+  gg::plan_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      m_splits, static_cast<int>(G), 0, 1, static_cast<int>(G), align, l.err, l.row_start, l.rows,
+      l.widx, l.tmp);
+  MOE_CUDA_CHECK_LAUNCH("grouped_gemm plan");
+  return MOE_OK;
+}
+
+extern "C" int moe_grouped_gemm_plan_ep(const int32_t* counts, int64_t num_src, int64_t num_w,
+                                        void* workspace, size_t workspace_bytes,
+                                        moe_stream_t stream) {
+  MOE_REQUIRE(num_src >= 1 && num_w >= 1 && num_src * num_w <= (1 << 24),
+              "grouped_gemm_plan_ep: bad num_src=%lld num_w=%lld", (long long)num_src,
+              (long long)num_w);
+  MOE_REQUIRE(counts != nullptr, "grouped_gemm_plan_ep: null counts");
+  const int64_t G = num_src * num_w;
+  int st = check_ws(workspace, workspace_bytes, G);
+  if (st) return st;
+  gg::WsLayout l = gg::ws_layout(workspace, G);
+  gg::plan_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
+      counts, static_cast<int>(G), 1, static_cast<int>(num_src), static_cast<int>(num_w), 1,
+      l.err, l.row_start, l.rows, l.widx, l.tmp);
+  MOE_CUDA_CHECK_LAUNCH("grouped_gemm plan_ep");
+  return MOE_OK;
+}
+
+extern "C" int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t x_rows, int64_t G,
+                                int64_t num_w, int64_t N, int64_t K, int32_t epilogue,
+                                const void* workspace, size_t workspace_bytes,
+                                moe_stream_t stream) {
+  MOE_REQUIRE(epilogue == 0 || epilogue == 1, "grouped_gemm: epilogue must be 0 or 1");
+  MOE_REQUIRE(G >= 1 && num_w >= 1, "grouped_gemm: G=%lld num_w=%lld", (long long)G,
+              (long long)num_w);
+  MOE_REQUIRE(x_rows >= 0 && x_rows < (1ll << 31), "grouped_gemm: x_rows=%lld out of range",
+              (long long)x_rows);
+  MOE_REQUIRE(K >= 8 && K % 8 == 0, "grouped_gemm: K=%lld must be a positive multiple of 8",
+              (long long)K);
+  MOE_REQUIRE(N >= 8 && N % 8 == 0, "grouped_gemm: N=%lld must be a positive multiple of 8",
+              (long long)N);
+  MOE_REQUIRE(epilogue == 0 || N % 16 == 0, "grouped_gemm: SwiGLU needs N=2F with F %% 8 == 0");
+  MOE_REQUIRE(num_w * N < (1ll << 31), "grouped_gemm: num_w*N too large");
+  int st = check_ws(workspace, workspace_bytes, G);
+  if (st) return st;
+  if (x_rows == 0) return MOE_OK;
+  MOE_REQUIRE(x && w && out, "grouped_gemm: null pointer");
+  MOE_REQUIRE(((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(w) |
+                reinterpret_cast<uintptr_t>(out)) & 15) == 0,
+              "grouped_gemm: x, w and out must be 16-byte aligned");
+  st = gg::ensure_smem_attr();
+  if (st) return st;
+
+  CUtensorMap ta, tb;
+  st = gg::make_tmap(&ta, x, static_cast<uint64_t>(K), static_cast<uint64_t>(x_rows));
+  if (st) return st;
+  st = gg::make_tmap(&tb, w, static_cast<uint64_t>(K), static_cast<uint64_t>(num_w * N));
+  if (st) return st;
+
+  gg::WsLayout l = gg::ws_layout(workspace, G);
+  gg::Params p;
+  p.row_start = l.row_start;
+  p.rows = l.rows;
+  p.widx = l.widx;
+  p.err = l.err;
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.x_rows = x_rows;
+  p.G = static_cast<int>(G);
+  p.n_w = static_cast<int>(N);
+  p.epilogue = epilogue;
+  if (epilogue == 1) {
+    p.f_half = static_cast<int>(N / 2);
+    p.n_out = p.f_half;
+    p.n_tiles = (p.f_half + 127) / 128;
+  } else {
+    p.f_half = 0;
+    p.n_out = static_cast<int>(N);
+    p.n_tiles = static_cast<int>((N + gg::BN - 1) / gg::BN);
+  }
+  p.num_kb = static_cast<int>((K + gg::BK - 1) / gg::BK);
+
+  int dev = 0;
+  MOE_CUDA_CALL(cudaGetDevice(&dev), "cudaGetDevice");
+  const int grid = num_sms(dev);
+  gg::grouped_gemm_kernel<<<grid, gg::kThreads, gg::kSmemBytes,
+                            reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, p);
+  MOE_CUDA_CHECK_LAUNCH("grouped_gemm launch");
+  return MOE_OK;
+}
+
+extern "C" int moe_grouped_gemm_check(const void* workspace, size_t workspace_bytes,
+                                      moe_stream_t stream, int32_t* device_error) {
+  MOE_REQUIRE(device_error != nullptr, "grouped_gemm_check: null output");
+  MOE_REQUIRE(workspace != nullptr && workspace_bytes >= 256, "grouped_gemm_check: bad workspace");
+  int32_t v = 0;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  MOE_CUDA_CALL(cudaMemcpyAsync(&v, workspace, sizeof(v), cudaMemcpyDeviceToHost, s),
+                "grouped_gemm_check copy");
+  MOE_CUDA_CALL(cudaStreamSynchronize(s), "grouped_gemm_check sync");
+  *device_error = v;
+  return v == 0 ? MOE_OK : MOE_ERR_DEVICE;
+}

@@ -1,0 +1,249 @@
+// Shared device helpers for the B200 MoE expert-layer kernels (sm_100a only).
+//
+// Everything here is plain CUDA C++ or hand-written PTX for Blackwell:
+// mbarriers with bounded waits, TMA tile loads (no cluster multicast anywhere
+// in this library), tcgen05 (UMMA + TMEM) wrappers, and bf16 helpers.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <cuda_bf16.h>
+#include <stdint.h>
+
+#include "../../include/moe_b200.h"
+
+#define MOE_DEVICE __device__ __forceinline__
+
+// ---------------------------------------------------------------------------
+// Host-side error plumbing shared by every entry point.
+// ---------------------------------------------------------------------------
+namespace moe {
+
+void set_last_error(const char* fmt, ...);
+
+#define MOE_REQUIRE(cond, ...)                        \
+  do {                                                \
+    if (!(cond)) {                                    \
+      ::moe::set_last_error(__VA_ARGS__);             \
+      return MOE_ERR_INVALID;                         \
+    }                                                 \
+  } while (0)
+
+#define MOE_CUDA_CHECK_LAUNCH(what)                                        \
+  do {                                                                     \
+    cudaError_t _e = cudaGetLastError();                                   \
+    if (_e != cudaSuccess) {                                               \
+      ::moe::set_last_error("%s: %s", what, cudaGetErrorString(_e));       \
+      return MOE_ERR_CUDA;                                                 \
+    }                                                                      \
+  } while (0)
+
+#define MOE_CUDA_CALL(call, what)                                          \
+  do {                                                                     \
+    cudaError_t _e = (call);                                               \
+    if (_e != cudaSuccess) {                                               \
+      ::moe::set_last_error("%s: %s", what, cudaGetErrorString(_e));       \
+      return MOE_ERR_CUDA;                                                 \
+    }                                                                      \
+  } while (0)
+
+int num_sms(int device);
+
+// ---------------------------------------------------------------------------
+// bf16 helpers. Conversions use the CUDA intrinsics (round-to-nearest-even),
+// the same rounding torch applies for .to(torch.bfloat16).
+// ---------------------------------------------------------------------------
+MOE_DEVICE float bf16_lo(uint32_t packed) { return __uint_as_float(packed << 16); }
+MOE_DEVICE float bf16_hi(uint32_t packed) { return __uint_as_float(packed & 0xFFFF0000u); }
+MOE_DEVICE uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+MOE_DEVICE float round_bf16(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+// ---------------------------------------------------------------------------
+// Timers and bounded waits. Every spin in this library gives up after
+// kWaitTimeoutNs of wall time, records an error and lets the kernel unwind.
+// ---------------------------------------------------------------------------
+constexpr unsigned long long kWaitTimeoutNs = 2000000000ull;  // 2 s
+
+MOE_DEVICE unsigned long long globaltimer_ns() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
+
+MOE_DEVICE uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+MOE_DEVICE void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+
+MOE_DEVICE void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+MOE_DEVICE bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the phase with the given parity. Returns false (and leaves the
+// barrier alone) when *abort_flag becomes non-zero or the wait exceeds
+// kWaitTimeoutNs; the caller then unwinds.
+MOE_DEVICE bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((it & 31u) == 0u) {
+      if (*abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitTimeoutNs) return false;
+    }
+  }
+}
+
+MOE_DEVICE void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+
+MOE_DEVICE void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+
+// ---------------------------------------------------------------------------
+// TMA (tensor tile copies). Loads only, CTA-local destination, no multicast.
+// ---------------------------------------------------------------------------
+MOE_DEVICE void tma_prefetch_desc(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+
+MOE_DEVICE void tma_load_2d(uint32_t dst, const void* tmap, int32_t x, int32_t y, uint32_t bar,
+                            uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint"
+      " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar), "l"(policy)
+      : "memory");
+}
+
+MOE_DEVICE uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+MOE_DEVICE uint64_t l2_policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+MOE_DEVICE uint64_t l2_policy_evict_normal() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_normal.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+// ---------------------------------------------------------------------------
+// tcgen05: TMEM allocation, UMMA issue, commit, TMEM loads.
+// ---------------------------------------------------------------------------
+MOE_DEVICE void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+MOE_DEVICE void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+MOE_DEVICE void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+MOE_DEVICE void tc_fence_before() {
+  asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory");
+}
+MOE_DEVICE void tc_fence_after() {
+  asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory");
+}
+
+// D[tmem] (+)= A[smem] * B[smem]^T, kind::f16 (bf16 inputs, fp32 accumulate).
+MOE_DEVICE void umma_bf16(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                          uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+// Arrives once on the mbarrier when all previously issued tcgen05.mma of this
+// thread have completed (which also releases their shared-memory operands).
+MOE_DEVICE void umma_commit(uint32_t bar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
+                   bar)
+               : "memory");
+}
+
+// 32 lanes x 32 consecutive fp32 columns: thread i of the warp receives row
+// (lane_base + i), columns [col, col + 32).
+MOE_DEVICE void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 "
+      "{%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, %15, "
+      "%16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]),
+        "=r"(r[7]), "=r"(r[8]), "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]),
+        "=r"(r[14]), "=r"(r[15]), "=r"(r[16]), "=r"(r[17]), "=r"(r[18]), "=r"(r[19]),
+        "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]), "=r"(r[25]),
+        "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr)
+      : "memory");
+}
+MOE_DEVICE void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// UMMA shared-memory matrix descriptor for a K-major operand tile staged by a
+// 128-byte-swizzled TMA load: rows of 128 bytes (64 bf16 along K), 8-row
+// swizzle atoms 1024 bytes apart (stride byte offset), descriptor version 1.
+MOE_DEVICE uint64_t umma_desc_k_sw128(uint32_t smem_addr) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);  // start address
+  d |= static_cast<uint64_t>(1u) << 16;                     // leading byte offset (unused, 16 B)
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;             // stride byte offset
+  d |= static_cast<uint64_t>(1u) << 46;                     // version (sm_100)
+  d |= static_cast<uint64_t>(2u) << 61;                     // SWIZZLE_128B
+  return d;
+}
+
+// Instruction descriptor, kind::f16: D fp32, A/B bf16, both K-major.
+__host__ __device__ constexpr uint32_t umma_idesc_bf16_f32(int m, int n) {
+  return (1u << 4)                                 // D format: f32
+         | (1u << 7)                               // A format: bf16
+         | (1u << 10)                              // B format: bf16
+         | (static_cast<uint32_t>(n >> 3) << 17)   // N / 8
+         | (static_cast<uint32_t>(m >> 4) << 24);  // M / 16
+}
+
+MOE_DEVICE int warp_id() { return static_cast<int>(threadIdx.x >> 5); }
+MOE_DEVICE int lane_id() { return static_cast<int>(threadIdx.x & 31); }
+
+MOE_DEVICE bool elect_one() {
+  uint32_t pred = 0;
+  asm volatile(
+      "{\n\t.reg .b32 rx;\n\t.reg .pred px;\n\t"
+      "elect.sync rx|px, 0xffffffff;\n\t"
+      "selp.b32 %0, 1, 0, px;\n\t}"
+      : "=r"(pred));
+  return pred != 0;
+}
+
+}  // namespace moe

@@ -1,0 +1,421 @@
+// Token permute / unpermute (dispatch / combine) for the MoE expert layer.
+//
+// Both directions are row copies of H bf16 values driven by a row-id map:
+//   permute   out[row[t,e]] = x[t]                (+ permuted probs)
+//   unpermute out[t] = bf16(sum_e w(t,e) * pin[row[e,t]])
+// They are HBM-bound. One 128-thread CTA owns one token: the map entries of
+// the token are read once, compacted in ascending expert order through a
+// warp ballot, and the H-element row moves as 16-byte vectors held in
+// registers (VPT vectors per thread), so every global access is a coalesced
+// 16-byte access and each source row is read exactly once.
+//
+// Reference behaviour: kernel_cases/case17_moe_permute_with_mask_map.py:58-71,
+// kernel_cases/case22_ref_moe_permute_mask_kernel_true.py:47-69,
+// kernel_cases/case15_moe_unpermute_mask_fwd.py:58-64,
+// kernel_cases/case24_ref_moe_unpermute_mask_kernel_false.py:45-68.
+#include "moe_common.cuh"
+#include "swiglu.cuh"
+
+namespace moe {
+namespace {
+
+constexpr int kRowThreads = 128;
+constexpr int kRowWarps = kRowThreads / 32;
+
+template <typename IdxT, bool kTrans>
+MOE_DEVICE int64_t load_map(const IdxT* map, int64_t T, int E, int64_t t, int e) {
+  return kTrans ? static_cast<int64_t>(__ldg(map + static_cast<int64_t>(e) * T + t))
+                : static_cast<int64_t>(__ldg(map + t * E + e));
+}
+
+// Ordered compaction of one window of up to 128 map entries: valid entries are
+// written to s_idx[0..n) in ascending thread (= expert) order. Returns n.
+MOE_DEVICE int compact_window(bool valid, int* s_wcnt, int& pos) {
+  const int lane = lane_id(), wid = warp_id();
+  const unsigned b = __ballot_sync(0xffffffffu, valid);
+  if (lane == 0) s_wcnt[wid] = __popc(b);
+  __syncthreads();
+  int before = 0, total = 0;
+#pragma unroll
+  for (int w = 0; w < kRowWarps; ++w) {
+    const int c = s_wcnt[w];
+    before += (w < wid) ? c : 0;
+    total += c;
+  }
+  pos = before + __popc(b & ((1u << lane) - 1u));
+  return total;
+}
+
+template <int VPT, bool kTrans, typename IdxT, typename V>
+__global__ void __launch_bounds__(kRowThreads) permute_kernel(
+    const V* __restrict__ x, const IdxT* __restrict__ map, const float* __restrict__ probs,
+    V* __restrict__ out, float* __restrict__ pp, int64_t T, int E, int nvec,
+    int64_t num_out) {
+  __shared__ int64_t s_dst[kRowThreads];
+  __shared__ float s_p[kRowThreads];
+  __shared__ int s_wcnt[kRowWarps];
+  const int64_t t = blockIdx.x;
+  const int tid = threadIdx.x;
+  const V* src = x + t * nvec;
+
+  V r[VPT > 0 ? VPT : 1];
+  if constexpr (VPT > 0) {
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const int i = tid + v * kRowThreads;
+      if (i < nvec) r[v] = __ldg(src + i);
+    }
+  }
+
+  for (int e0 = 0; e0 < E; e0 += kRowThreads) {
+    const int e = e0 + tid;
+    int64_t d = -1;
+    if (e < E) d = load_map<IdxT, kTrans>(map, T, E, t, e);
+    const bool valid = d >= 0 && d < num_out;
+    int pos;
+    const int total = compact_window(valid, s_wcnt, pos);
+    if (valid) {
+      s_dst[pos] = d;
+      if (probs) s_p[pos] = __ldg(probs + t * E + e);
+    }
+    __syncthreads();
+    for (int j = 0; j < total; ++j) {
+      const int64_t dd = s_dst[j];
+      V* o = out + dd * nvec;
+      if constexpr (VPT > 0) {
+#pragma unroll
+        for (int v = 0; v < VPT; ++v) {
+          const int i = tid + v * kRowThreads;
+          if (i < nvec) o[i] = r[v];
+        }
+      } else {
+        for (int i = tid; i < nvec; i += kRowThreads) o[i] = __ldg(src + i);
+      }
+      if (pp != nullptr && tid == 0) pp[dd] = s_p[j];
+    }
+    __syncthreads();
+  }
+}
+
+// A row moves as vectors V of 8 (uint4), 2 (uint32_t) or 1 (uint16_t) bf16
+// values; the widest one that the row length and pointer alignment allow.
+template <typename V>
+struct VecTraits;
+template <>
+struct VecTraits<uint4> {
+  static constexpr int kElems = 8;
+  MOE_DEVICE static void unpack(const uint4& q, float (&f)[8]) {
+    const uint32_t u[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      f[2 * i] = bf16_lo(u[i]);
+      f[2 * i + 1] = bf16_hi(u[i]);
+    }
+  }
+  MOE_DEVICE static uint4 pack(const float (&f)[8]) {
+    return make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                      pack_bf16x2(f[6], f[7]));
+  }
+};
+template <>
+struct VecTraits<uint32_t> {
+  static constexpr int kElems = 2;
+  MOE_DEVICE static void unpack(const uint32_t& q, float (&f)[2]) {
+    f[0] = bf16_lo(q);
+    f[1] = bf16_hi(q);
+  }
+  MOE_DEVICE static uint32_t pack(const float (&f)[2]) { return pack_bf16x2(f[0], f[1]); }
+};
+template <>
+struct VecTraits<uint16_t> {
+  static constexpr int kElems = 1;
+  MOE_DEVICE static void unpack(const uint16_t& q, float (&f)[1]) {
+    f[0] = __uint_as_float(static_cast<uint32_t>(q) << 16);
+  }
+  MOE_DEVICE static uint16_t pack(const float (&f)[1]) {
+    return static_cast<uint16_t>(pack_bf16x2(f[0], 0.f) & 0xFFFFu);
+  }
+};
+
+template <typename V>
+MOE_DEVICE void accum_vec(float (&acc)[VecTraits<V>::kElems], const V& q, float w, bool weighted) {
+  constexpr int kE = VecTraits<V>::kElems;
+  float f[kE];
+  VecTraits<V>::unpack(q, f);
+#pragma unroll
+  for (int i = 0; i < kE; ++i)
+    acc[i] = weighted ? __fadd_rn(acc[i], __fmul_rn(w, f[i])) : __fadd_rn(acc[i], f[i]);
+}
+
+// probs_mode: -1 unweighted, 0 probs[t*E+e], 1 probs[src row].
+template <int VPT, typename IdxT, typename V>
+__global__ void __launch_bounds__(kRowThreads) unpermute_kernel(
+    const V* __restrict__ pin, const IdxT* __restrict__ map, const float* __restrict__ probs,
+    int probs_mode, V* __restrict__ out, float* __restrict__ acc_out, int64_t T, int E,
+    int nvec, int64_t num_rows) {
+  constexpr int kE = VecTraits<V>::kElems;
+  __shared__ int64_t s_src[kRowThreads];
+  __shared__ float s_w[kRowThreads];
+  __shared__ int s_wcnt[kRowWarps];
+  const int64_t t = blockIdx.x;
+  const int tid = threadIdx.x;
+  const bool weighted = probs_mode >= 0;
+
+  float acc[VPT][kE];
+#pragma unroll
+  for (int v = 0; v < VPT; ++v)
+#pragma unroll
+    for (int i = 0; i < kE; ++i) acc[v][i] = 0.f;
+
+  for (int e0 = 0; e0 < E; e0 += kRowThreads) {
+    const int e = e0 + tid;
+    int64_t s = -1;
+    if (e < E) s = load_map<IdxT, true>(map, T, E, t, e);
+    const bool valid = s >= 0 && s < num_rows;
+    int pos;
+    const int total = compact_window(valid, s_wcnt, pos);
+    if (valid) {
+      s_src[pos] = s;
+      float w = 1.f;
+      if (probs_mode == 0) w = __ldg(probs + t * E + e);
+      else if (probs_mode == 1) w = __ldg(probs + s);
+      s_w[pos] = w;
+    }
+    __syncthreads();
+    int j = 0;
+    // Two source rows in flight per step; accumulation order stays ascending.
+    for (; j + 1 < total; j += 2) {
+      const V* a = pin + s_src[j] * nvec;
+      const V* b = pin + s_src[j + 1] * nvec;
+      const float wa = s_w[j], wb = s_w[j + 1];
+      V qa[VPT], qb[VPT];
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        const int i = tid + v * kRowThreads;
+        if (i < nvec) {
+          qa[v] = a[i];
+          qb[v] = b[i];
+        }
+      }
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        const int i = tid + v * kRowThreads;
+        if (i < nvec) {
+          accum_vec<V>(acc[v], qa[v], wa, weighted);
+          accum_vec<V>(acc[v], qb[v], wb, weighted);
+        }
+      }
+    }
+    if (j < total) {
+      const V* a = pin + s_src[j] * nvec;
+      const float wa = s_w[j];
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        const int i = tid + v * kRowThreads;
+        if (i < nvec) accum_vec<V>(acc[v], a[i], wa, weighted);
+      }
+    }
+    __syncthreads();
+  }
+
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int i = tid + v * kRowThreads;
+    if (i < nvec) {
+      out[t * nvec + i] = VecTraits<V>::pack(acc[v]);
+      if (acc_out) {
+        float* ao = acc_out + (t * nvec + i) * kE;
+#pragma unroll
+        for (int q = 0; q < kE; ++q) ao[q] = acc[v][q];
+      }
+    }
+  }
+}
+
+__global__ void swiglu_kernel(const uint4* __restrict__ y, uint4* __restrict__ h, int64_t M,
+                              int fvec) {
+  const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= M * fvec) return;
+  const int64_t m = i / fvec;
+  const int c = static_cast<int>(i - m * fvec);
+  const uint4 g = __ldg(y + m * 2 * fvec + c);
+  const uint4 u = __ldg(y + m * 2 * fvec + fvec + c);
+  const uint32_t gg[4] = {g.x, g.y, g.z, g.w}, uu[4] = {u.x, u.y, u.z, u.w};
+  uint32_t o[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k)
+    o[k] = pack_bf16x2(swiglu_f32(bf16_lo(gg[k]), bf16_lo(uu[k])),
+                       swiglu_f32(bf16_hi(gg[k]), bf16_hi(uu[k])));
+  h[i] = make_uint4(o[0], o[1], o[2], o[3]);
+}
+
+template <bool kTrans, typename IdxT, typename V>
+int launch_permute_v(const void* x, const IdxT* map, const float* probs, void* out, float* pp,
+                     int64_t T, int64_t H, int64_t E, int64_t num_out, cudaStream_t s) {
+  const int nvec = static_cast<int>(H / VecTraits<V>::kElems);
+  const int vpt = (nvec + kRowThreads - 1) / kRowThreads;
+  const V* xv = static_cast<const V*>(x);
+  V* ov = static_cast<V*>(out);
+  const unsigned grid = static_cast<unsigned>(T);
+#define MOE_PERMUTE_CASE(VP)                                                                 \
+  permute_kernel<VP, kTrans, IdxT, V><<<grid, kRowThreads, 0, s>>>(xv, map, probs, ov, pp, T, \
+                                                                   (int)E, nvec, num_out)
+  if (vpt <= 1) MOE_PERMUTE_CASE(1);
+  else if (vpt <= 2) MOE_PERMUTE_CASE(2);
+  else if (vpt <= 4) MOE_PERMUTE_CASE(4);
+  else if (vpt <= 8) MOE_PERMUTE_CASE(8);
+  else MOE_PERMUTE_CASE(0);
+#undef MOE_PERMUTE_CASE
+  MOE_CUDA_CHECK_LAUNCH("permute launch");
+  return MOE_OK;
+}
+
+template <typename IdxT, typename V>
+int launch_unpermute_v(const void* pin, const IdxT* map, const float* probs, int probs_mode,
+                       void* out, float* acc_out, int64_t T, int64_t H, int64_t E,
+                       int64_t num_rows, cudaStream_t s) {
+  const int nvec = static_cast<int>(H / VecTraits<V>::kElems);
+  const int vpt = (nvec + kRowThreads - 1) / kRowThreads;
+  const V* pv = static_cast<const V*>(pin);
+  V* ov = static_cast<V*>(out);
+  const unsigned grid = static_cast<unsigned>(T);
+#define MOE_UNPERMUTE_CASE(VP)                                                           \
+  unpermute_kernel<VP, IdxT, V><<<grid, kRowThreads, 0, s>>>(pv, map, probs, probs_mode, ov, \
+                                                             acc_out, T, (int)E, nvec, num_rows)
+  if (vpt <= 1) MOE_UNPERMUTE_CASE(1);
+  else if (vpt <= 2) MOE_UNPERMUTE_CASE(2);
+  else if (vpt <= 4) MOE_UNPERMUTE_CASE(4);
+  else if (vpt <= 8) MOE_UNPERMUTE_CASE(8);
+  else if (vpt <= 16) MOE_UNPERMUTE_CASE(16);
+  else {
+    set_last_error("unpermute: H=%lld exceeds this build (H <= %d for this row alignment)",
+                   (long long)H, 16 * kRowThreads * VecTraits<V>::kElems);
+    return MOE_ERR_UNSUPPORTED;
+  }
+#undef MOE_UNPERMUTE_CASE
+  MOE_CUDA_CHECK_LAUNCH("unpermute launch");
+  return MOE_OK;
+}
+
+// Widest vector the row length and both row pointers allow: 16, 4 or 2 bytes.
+int vec_bytes(const void* a, const void* b, int64_t H) {
+  const uintptr_t m = reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b);
+  if (H % 8 == 0 && (m & 15) == 0) return 16;
+  if (H % 2 == 0 && (m & 3) == 0) return 4;
+  return 2;
+}
+
+template <bool kTrans, typename IdxT>
+int launch_permute(const void* x, const IdxT* map, const float* probs, void* out, float* pp,
+                   int64_t T, int64_t H, int64_t E, int64_t num_out, cudaStream_t s) {
+  switch (vec_bytes(x, out, H)) {
+    case 16: return launch_permute_v<kTrans, IdxT, uint4>(x, map, probs, out, pp, T, H, E, num_out, s);
+    case 4: return launch_permute_v<kTrans, IdxT, uint32_t>(x, map, probs, out, pp, T, H, E, num_out, s);
+    default: return launch_permute_v<kTrans, IdxT, uint16_t>(x, map, probs, out, pp, T, H, E, num_out, s);
+  }
+}
+
+template <typename IdxT>
+int launch_unpermute(const void* pin, const IdxT* map, const float* probs, int probs_mode,
+                     void* out, float* acc_out, int64_t T, int64_t H, int64_t E, int64_t num_rows,
+                     cudaStream_t s) {
+  switch (vec_bytes(pin, out, H)) {
+    case 16:
+      return launch_unpermute_v<IdxT, uint4>(pin, map, probs, probs_mode, out, acc_out, T, H, E,
+                                             num_rows, s);
+    case 4:
+      return launch_unpermute_v<IdxT, uint32_t>(pin, map, probs, probs_mode, out, acc_out, T, H,
+                                                E, num_rows, s);
+    default:
+      return launch_unpermute_v<IdxT, uint16_t>(pin, map, probs, probs_mode, out, acc_out, T, H,
+                                                E, num_rows, s);
+  }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+int check_row_args(const char* op, const void* a, const void* b, int64_t T, int64_t H, int64_t E) {
+  MOE_REQUIRE(T >= 0 && H >= 0 && E >= 1, "%s: bad shape T=%lld H=%lld E=%lld", op,
+              (long long)T, (long long)H, (long long)E);
+  MOE_REQUIRE(T <= 0x7fffffff && H <= 0x7fffffff && E <= 0x7fffffff, "%s: size too large", op);
+  MOE_REQUIRE(((reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b)) & 1) == 0,
+              "%s: row pointers must be 2-byte aligned", op);
+  return MOE_OK;
+}
+
+}  // namespace
+}  // namespace moe
+
+using namespace moe;
+
+extern "C" int moe_permute_mask_map(const void* x, const int64_t* row_id_map_te, const float* probs,
+                                    void* out, float* permuted_probs, int64_t T, int64_t H,
+                                    int64_t E, int64_t num_out, moe_stream_t stream) {
+  int st = check_row_args("permute", x, out, T, H, E);
+  if (st) return st;
+  MOE_REQUIRE(num_out >= 0, "permute: num_out=%lld < 0", (long long)num_out);
+  if (T == 0 || H == 0 || num_out == 0) return MOE_OK;
+  MOE_REQUIRE((probs == nullptr) == (permuted_probs == nullptr),
+              "permute: probs and permuted_probs must both be given or both be null");
+  MOE_REQUIRE(x && out && row_id_map_te, "permute: null pointer");
+  return launch_permute<false, int64_t>(x, row_id_map_te, probs, out, permuted_probs, T, H, E,
+                                        num_out, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int moe_permute_mask_map_trans(const void* x, const void* row_id_map_et,
+                                          int32_t idx_bits, const float* probs, void* out,
+                                          float* permuted_probs, int64_t T, int64_t H, int64_t E,
+                                          int64_t num_out, moe_stream_t stream) {
+  int st = check_row_args("permute_trans", x, out, T, H, E);
+  if (st) return st;
+  MOE_REQUIRE(idx_bits == 32 || idx_bits == 64, "permute_trans: idx_bits must be 32 or 64");
+  MOE_REQUIRE(num_out >= 0, "permute_trans: num_out=%lld < 0", (long long)num_out);
+  if (T == 0 || H == 0 || num_out == 0) return MOE_OK;
+  MOE_REQUIRE((probs == nullptr) == (permuted_probs == nullptr),
+              "permute_trans: probs and permuted_probs must both be given or both be null");
+  MOE_REQUIRE(x && out && row_id_map_et, "permute_trans: null pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (idx_bits == 64)
+    return launch_permute<true, int64_t>(x, static_cast<const int64_t*>(row_id_map_et), probs, out,
+                                         permuted_probs, T, H, E, num_out, s);
+  return launch_permute<true, int32_t>(x, static_cast<const int32_t*>(row_id_map_et), probs, out,
+                                       permuted_probs, T, H, E, num_out, s);
+}
+
+extern "C" int moe_unpermute_mask(const void* pin, const void* row_id_map_et, int32_t idx_bits,
+                                  const float* probs, int32_t probs_mode, void* out,
+                                  float* acc_out, int64_t T, int64_t H, int64_t E,
+                                  int64_t num_rows, moe_stream_t stream) {
+  int st = check_row_args("unpermute", pin, out, T, H, E);
+  if (st) return st;
+  MOE_REQUIRE(idx_bits == 32 || idx_bits == 64, "unpermute: idx_bits must be 32 or 64");
+  MOE_REQUIRE(probs == nullptr || probs_mode == 0 || probs_mode == 1,
+              "unpermute: probs_mode must be 0 ([T,E]) or 1 (permuted)");
+  MOE_REQUIRE(num_rows >= 0, "unpermute: num_rows=%lld < 0", (long long)num_rows);
+  MOE_REQUIRE(acc_out == nullptr || (reinterpret_cast<uintptr_t>(acc_out) & 3) == 0,
+              "unpermute: acc_out must be 4-byte aligned");
+  if (T == 0 || H == 0) return MOE_OK;
+  MOE_REQUIRE(out && row_id_map_et && (pin || num_rows == 0), "unpermute: null pointer");
+  const int mode = probs ? probs_mode : -1;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (idx_bits == 64)
+    return launch_unpermute<int64_t>(pin, static_cast<const int64_t*>(row_id_map_et), probs, mode,
+                                     out, acc_out, T, H, E, num_rows, s);
+  return launch_unpermute<int32_t>(pin, static_cast<const int32_t*>(row_id_map_et), probs, mode,
+                                   out, acc_out, T, H, E, num_rows, s);
+}
+
+extern "C" int moe_swiglu(const void* y, void* h, int64_t M, int64_t F, moe_stream_t stream) {
+  MOE_REQUIRE(M >= 0 && F >= 0 && F % 8 == 0, "swiglu: F=%lld must be a multiple of 8",
+              (long long)F);
+  if (M == 0 || F == 0) return MOE_OK;
+  MOE_REQUIRE(y && h && aligned16(y) && aligned16(h), "swiglu: null or misaligned pointer");
+  const int fvec = static_cast<int>(F / 8);
+  const int64_t n = M * fvec;
+  const int threads = 256;
+  swiglu_kernel<<<static_cast<unsigned>((n + threads - 1) / threads), threads, 0,
+                  reinterpret_cast<cudaStream_t>(stream)>>>(static_cast<const uint4*>(y),
+                                                            static_cast<uint4*>(h), M, fvec);
+  MOE_CUDA_CHECK_LAUNCH("swiglu launch");
+  return MOE_OK;
+}

@@ -1,0 +1,17 @@
+"""B200-native MoE expert-layer forward path (sm_100a CUDA behind a C ABI).
+
+Public API (torch tensors on a CUDA device; no CPU fallback):
+  topk, router_topk, row_id_map, permute, permute_trans, unpermute,
+  grouped_gemm, swiglu, MoELayer, MoEWeights
+The reference-style ``kernel_function`` entry points live in ``bundles/``.
+"""
+from ._lib import MoeError, load as load_library
+from .ops import (GroupedGemmPlan, RouterOutput, RowIdMap, grouped_gemm, permute, permute_trans,
+                  router_topk, row_id_map, swiglu, topk, unpermute)
+from .layer import MoELayer, MoEWeights
+
+__all__ = [
+    "MoeError", "load_library", "GroupedGemmPlan", "RouterOutput", "RowIdMap", "grouped_gemm",
+    "permute", "permute_trans", "router_topk", "row_id_map", "swiglu", "topk", "unpermute",
+    "MoELayer", "MoEWeights",
+]

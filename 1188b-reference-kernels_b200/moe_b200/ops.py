@@ -1,0 +1,361 @@
+"""Torch-facing wrappers of the C ABI: one function per hot-path operator.
+
+Each wrapper validates shapes and dtypes, allocates outputs with torch (the
+caller's device and current stream), and calls the sm_100a kernel through
+``_lib.call``. Inputs must be CUDA tensors: there is no CPU path.
+
+Reference interfaces mirrored (kernel_results/<case>/binding.cpp):
+  topk            <- case23_aten_topk/binding.cpp:6-26 (topk_forward)
+  row_id_map      <- case12_moe_row_id_map_pass2/binding.cpp:13-36
+  permute         <- case17_moe_permute_with_mask_map/binding.cpp:8-32
+  unpermute       <- case15_moe_unpermute_mask_fwd/binding.cpp:11-22
+"""
+from __future__ import annotations
+
+from ctypes import byref, c_int32, c_size_t
+from typing import NamedTuple, Optional, Sequence, Union
+
+import torch
+
+from . import _lib
+
+__all__ = [
+    "topk", "router_topk", "RouterOutput", "row_id_map", "RowIdMap", "permute",
+    "permute_trans", "unpermute", "grouped_gemm", "GroupedGemmPlan", "swiglu",
+]
+
+
+def _stream(dev: torch.device) -> int:
+    return torch.cuda.current_stream(dev).cuda_stream
+
+
+def _p(t: Optional[torch.Tensor]):
+    return None if t is None else t.data_ptr()
+
+
+def _need_cuda(name: str, t: Optional[torch.Tensor]) -> None:
+    if t is not None and not t.is_cuda:
+        raise ValueError(f"{name} must be a CUDA tensor (the MoE B200 ops have no CPU path)")
+
+
+def _need_dtype(name: str, t: torch.Tensor, *dtypes: torch.dtype) -> None:
+    if t.dtype not in dtypes:
+        raise ValueError(f"{name} must be {' or '.join(map(str, dtypes))}, got {t.dtype}")
+
+
+def _workspace(nbytes: int, dev: torch.device) -> torch.Tensor:
+    # The caching allocator returns blocks aligned to at least 512 bytes.
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=dev)
+
+
+# --------------------------------------------------------------------------- a1
+def topk(input: torch.Tensor, k: int = 8):
+    """Row-wise top-k (largest, sorted, ties -> lower index) of fp32 [M,N].
+
+    Same contract as kernel_cases/case23_ref_aten_topk.py:47-62 (reference_topk).
+    Returns (values fp32 [M,k], indices int64 [M,k]).
+    """
+    _need_cuda("input", input)
+    _need_dtype("input", input, torch.float32)
+    if input.dim() != 2:
+        raise ValueError(f"expected 2D input, got {input.dim()}D")
+    x = input.contiguous()
+    m, n = x.shape
+    values = torch.empty((m, k), dtype=torch.float32, device=x.device)
+    indices = torch.empty((m, k), dtype=torch.int64, device=x.device)
+    _lib.call("moe_topk_f32", _p(x), _p(values), _p(indices), m, n, int(k), _stream(x.device))
+    return values, indices
+
+
+class RouterOutput(NamedTuple):
+    topk_vals: torch.Tensor    # [T,k] fp32 gate weights in selection order
+    topk_idx: torch.Tensor     # [T,k] int64 expert ids
+    routing_map: torch.Tensor  # [T,E] bool
+    probs: torch.Tensor        # [T,E] fp32, gate at routed pairs, 0 elsewhere
+
+
+def router_topk(logits: torch.Tensor, k: int, score: str = "softmax", renorm: bool = True,
+                bias: Optional[torch.Tensor] = None, outputs: str = "all") -> RouterOutput:
+    """Fused router: (logits + bias) -> top-k -> gates -> routing map + probs.
+
+    score="softmax": gates are softmax probabilities (renormalised over the k
+    selected experts when renorm). score="logits": gates are the raw logits
+    (case23 semantics). The selection follows the logits, which orders the
+    experts exactly as their softmax probabilities do.
+    outputs="all" or "maps" (skip topk_vals/topk_idx).
+    """
+    _need_cuda("logits", logits)
+    _need_dtype("logits", logits, torch.float32)
+    if logits.dim() != 2:
+        raise ValueError("logits must be [T,E]")
+    if score not in ("softmax", "logits"):
+        raise ValueError("score must be 'softmax' or 'logits'")
+    lg = logits.contiguous()
+    t, e = lg.shape
+    dev = lg.device
+    if bias is not None:
+        _need_cuda("bias", bias)
+        _need_dtype("bias", bias, torch.float32)
+        if bias.shape != (e,):
+            raise ValueError(f"bias must be [{e}]")
+        bias = bias.contiguous()
+    tv = ti = None
+    if outputs == "all":
+        tv = torch.empty((t, k), dtype=torch.float32, device=dev)
+        ti = torch.empty((t, k), dtype=torch.int64, device=dev)
+    rmap = torch.empty((t, e), dtype=torch.bool, device=dev)
+    probs = torch.empty((t, e), dtype=torch.float32, device=dev)
+    _lib.call("moe_router_topk", _p(lg), _p(bias), t, e, int(k), 1 if score == "softmax" else 0,
+              1 if renorm else 0, _p(tv), _p(ti), _p(rmap), _p(probs), _stream(dev))
+    return RouterOutput(tv, ti, rmap, probs)
+
+
+# --------------------------------------------------------------------------- a3
+class RowIdMap(NamedTuple):
+    map_et: Optional[torch.Tensor]  # [E,T] int64
+    map_te: Optional[torch.Tensor]  # [T,E] int64
+    counts: torch.Tensor            # [E] int32 tokens per expert
+    num_out: torch.Tensor           # [1] int64 total (padded) rows, on device
+
+
+def row_id_map(routing_map: torch.Tensor, align: int = 1, want_et: bool = True,
+               want_te: bool = True) -> RowIdMap:
+    """routing_map [T,E] bool -> expert-major row-id maps (both layouts).
+
+    align=1 reproduces kernel_cases/case12_moe_row_id_map_pass2.py:43-50
+    exactly; align>1 starts every expert segment on a multiple of align.
+    """
+    _need_cuda("routing_map", routing_map)
+    _need_dtype("routing_map", routing_map, torch.bool, torch.uint8)
+    if routing_map.dim() != 2:
+        raise ValueError("routing_map must be [T,E]")
+    rm = routing_map.contiguous()
+    t, e = rm.shape
+    dev = rm.device
+    ws_bytes = c_size_t(0)
+    _lib.call("moe_row_id_map_workspace_size", t, e, byref(ws_bytes))
+    ws = _workspace(ws_bytes.value, dev)
+    map_et = torch.empty((e, t), dtype=torch.int64, device=dev) if want_et else None
+    map_te = torch.empty((t, e), dtype=torch.int64, device=dev) if want_te else None
+    counts = torch.empty((e,), dtype=torch.int32, device=dev)
+    num_out = torch.empty((1,), dtype=torch.int64, device=dev)
+    _lib.call("moe_row_id_map", _p(rm), t, e, int(align), _p(map_et), _p(map_te), _p(counts),
+              _p(num_out), _p(ws), ws_bytes.value, _stream(dev))
+    return RowIdMap(map_et, map_te, counts, num_out)
+
+
+# --------------------------------------------------------------------------- a4/a5
+def _map_stats(row_id_map: torch.Tensor):
+    """(max+1, number of valid entries) with one device->host sync."""
+    valid = row_id_map >= 0
+    stats = torch.stack([row_id_map.max().to(torch.int64) + 1, valid.sum().to(torch.int64)])
+    r, n = (int(v) for v in stats.cpu())
+    return max(r, 0), n
+
+
+def _permute_outputs(x, probs, num_out, dense):
+    alloc = torch.empty if dense else torch.zeros
+    out = alloc((num_out, x.shape[1]), dtype=x.dtype, device=x.device)
+    pp = None
+    if probs is not None:
+        pp = alloc((num_out,), dtype=torch.float32, device=x.device)
+    return out, pp
+
+
+def permute(x: torch.Tensor, row_id_map: torch.Tensor, probs: Optional[torch.Tensor] = None,
+            num_out: Optional[int] = None):
+    """out[row_id_map[t,e]] = x[t]; permuted_probs[row_id_map[t,e]] = probs[t,e].
+
+    row_id_map is the token-major [T,E] int64 map (case17). When num_out is
+    None it is max(row_id_map)+1, found with one host sync as the reference
+    binding does (kernel_results/case17_moe_permute_with_mask_map/binding.cpp:24).
+    Returns (out [num_out,H], permuted_probs [num_out] or None).
+    """
+    for n_, t_ in (("x", x), ("row_id_map", row_id_map), ("probs", probs)):
+        _need_cuda(n_, t_)
+    if x.dim() != 2 or row_id_map.dim() != 2 or row_id_map.shape[0] != x.shape[0]:
+        raise ValueError(f"shapes x {tuple(x.shape)} row_id_map {tuple(row_id_map.shape)}")
+    if x.element_size() != 2:
+        raise ValueError("x must be a 2-byte type (bf16/fp16)")
+    _need_dtype("row_id_map", row_id_map, torch.int64)
+    t, e = row_id_map.shape
+    xc = x.contiguous()
+    mc = row_id_map.contiguous()
+    pc = None
+    if probs is not None:
+        if probs.shape != (t, e):
+            raise ValueError(f"probs {tuple(probs.shape)} expected {(t, e)}")
+        pc = probs.contiguous().to(torch.float32)
+    dense = True
+    if num_out is None:
+        num_out, nvalid = _map_stats(mc) if mc.numel() else (0, 0)
+        dense = nvalid >= num_out
+    out, pp = _permute_outputs(xc, pc, int(num_out), dense)
+    _lib.call("moe_permute_mask_map", _p(xc), _p(mc), _p(pc), _p(out), _p(pp), t, xc.shape[1], e,
+              int(num_out), _stream(xc.device))
+    return out, pp
+
+
+def permute_trans(x: torch.Tensor, row_id_map: torch.Tensor, probs: Optional[torch.Tensor] = None,
+                  num_out: Optional[int] = None):
+    """Permute with the expert-major [E,T] map (int64 or int32), case22/21/30."""
+    for n_, t_ in (("x", x), ("row_id_map", row_id_map), ("probs", probs)):
+        _need_cuda(n_, t_)
+    if row_id_map.dim() != 2 or x.dim() != 2 or row_id_map.shape[1] != x.shape[0]:
+        raise ValueError(f"shapes inp {tuple(x.shape)} row_id_map {tuple(row_id_map.shape)}")
+    if x.element_size() != 2:
+        raise ValueError("x must be a 2-byte type (bf16/fp16)")
+    _need_dtype("row_id_map", row_id_map, torch.int64, torch.int32)
+    e, t = row_id_map.shape
+    xc = x.contiguous()
+    mc = row_id_map.contiguous()
+    pc = None
+    if probs is not None:
+        if probs.shape != (t, e):
+            raise ValueError(f"probs {tuple(probs.shape)} expected {(t, e)}")
+        pc = probs.contiguous().to(torch.float32)
+    dense = True
+    if num_out is None:
+        num_out, nvalid = _map_stats(mc) if mc.numel() else (0, 0)
+        dense = nvalid >= num_out
+    out, pp = _permute_outputs(xc, pc, int(num_out), dense)
+    bits = 64 if mc.dtype == torch.int64 else 32
+    _lib.call("moe_permute_mask_map_trans", _p(xc), _p(mc), bits, _p(pc), _p(out), _p(pp), t,
+              xc.shape[1], e, int(num_out), _stream(xc.device))
+    return out, pp
+
+
+# --------------------------------------------------------------------------- a6-a8
+def unpermute(pin: torch.Tensor, row_id_map: torch.Tensor, probs: Optional[torch.Tensor] = None,
+              probs_mode: str = "dense", return_acc: bool = False):
+    """out[t] = bf16(sum over e ascending of w * pin[row_id_map[e,t]]), fp32 accumulation.
+
+    w = 1 without probs (case15 / case24); w = probs[t,e] for probs_mode
+    "dense" ([T,E]); w = probs[row] for probs_mode "permuted" ([rows]).
+    Returns out (and the fp32 accumulator when return_acc).
+    """
+    for n_, t_ in (("pin", pin), ("row_id_map", row_id_map), ("probs", probs)):
+        _need_cuda(n_, t_)
+    if row_id_map.dim() != 2 or pin.dim() != 2:
+        raise ValueError(f"shapes pin {tuple(pin.shape)} row_id_map {tuple(row_id_map.shape)}")
+    _need_dtype("pin", pin, torch.bfloat16)
+    _need_dtype("row_id_map", row_id_map, torch.int64, torch.int32)
+    e, t = row_id_map.shape
+    pc = pin.contiguous()
+    mc = row_id_map.contiguous()
+    mode = -1
+    prc = None
+    if probs is not None:
+        prc = probs.contiguous().to(torch.float32)
+        if probs_mode == "dense":
+            if prc.shape != (t, e):
+                raise ValueError(f"probs {tuple(prc.shape)} expected {(t, e)}")
+            mode = 0
+        elif probs_mode == "permuted":
+            if prc.shape != (pc.shape[0],):
+                raise ValueError(f"permuted probs must be [{pc.shape[0]}]")
+            mode = 1
+        else:
+            raise ValueError("probs_mode must be 'dense' or 'permuted'")
+    out = torch.empty((t, pc.shape[1]), dtype=pc.dtype, device=pc.device)
+    acc = torch.empty((t, pc.shape[1]), dtype=torch.float32, device=pc.device) if return_acc else None
+    bits = 64 if mc.dtype == torch.int64 else 32
+    _lib.call("moe_unpermute_mask", _p(pc), _p(mc), bits, _p(prc), mode if mode >= 0 else 0,
+              _p(out), _p(acc), t, pc.shape[1], e, pc.shape[0], _stream(pc.device))
+    return (out, acc) if return_acc else out
+
+
+# --------------------------------------------------------------------------- a9-a11
+class GroupedGemmPlan:
+    """Device-side group table for moe_grouped_gemm (reusable across calls)."""
+
+    def __init__(self, num_groups: int, device: torch.device):
+        self.num_groups = int(num_groups)
+        nb = c_size_t(0)
+        _lib.call("moe_grouped_gemm_workspace_size", self.num_groups, byref(nb))
+        self.nbytes = nb.value
+        self.workspace = _workspace(self.nbytes, device)
+        self.device = device
+
+    def from_splits(self, m_splits: torch.Tensor, align: int = 1) -> "GroupedGemmPlan":
+        ms = m_splits.to(device=self.device, dtype=torch.int32).contiguous()
+        if ms.numel() != self.num_groups:
+            raise ValueError(f"m_splits has {ms.numel()} entries, plan has {self.num_groups}")
+        self._keep = ms
+        _lib.call("moe_grouped_gemm_plan_splits", _p(ms), self.num_groups, int(align),
+                  _p(self.workspace), self.nbytes, _stream(self.device))
+        return self
+
+    def from_ep_counts(self, counts: torch.Tensor, num_src: int, num_w: int) -> "GroupedGemmPlan":
+        c = counts.to(device=self.device, dtype=torch.int32).contiguous()
+        if c.numel() != num_src * num_w or num_src * num_w != self.num_groups:
+            raise ValueError("counts must be [num_src * num_w]")
+        self._keep = c
+        _lib.call("moe_grouped_gemm_plan_ep", _p(c), int(num_src), int(num_w),
+                  _p(self.workspace), self.nbytes, _stream(self.device))
+        return self
+
+    def device_error(self) -> int:
+        v = c_int32(0)
+        lib = _lib.load()
+        lib.moe_grouped_gemm_check(_p(self.workspace), self.nbytes, _stream(self.device), byref(v))
+        return int(v.value)
+
+
+def grouped_gemm(x: torch.Tensor, w: torch.Tensor,
+                 m_splits: Union[None, Sequence[int], torch.Tensor] = None,
+                 epilogue: str = "none", align: int = 1,
+                 plan: Optional[GroupedGemmPlan] = None,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out = cat_g(x[seg_g] @ w[g].T) on tcgen05 tensor cores (bf16, fp32 accumulate).
+
+    x [rows,K] bf16, w [G,N,K] bf16 ("[out,in]" as in case03/case04). With
+    epilogue="swiglu", w holds [gate|up] (N=2F) and the result is
+    silu(gate)*up, [rows,F]. m_splits defaults to the uniform split of
+    kernel_cases/case03_moe_grouped_gemm_fc1_fwd.py:43-46. A prebuilt plan
+    (device group table) skips the planning launch.
+    """
+    for n_, t_ in (("x", x), ("w", w)):
+        _need_cuda(n_, t_)
+        _need_dtype(n_, t_, torch.bfloat16)
+    if x.dim() != 2 or w.dim() != 3 or x.shape[1] != w.shape[2]:
+        raise ValueError(f"shapes x {tuple(x.shape)} w {tuple(w.shape)}")
+    if epilogue not in ("none", "swiglu"):
+        raise ValueError("epilogue must be 'none' or 'swiglu'")
+    xc = x.contiguous()
+    wc = w.contiguous()
+    rows, k = xc.shape
+    g, n, _ = wc.shape
+    dev = xc.device
+    if plan is None:
+        if m_splits is None:
+            base, rem = divmod(rows, g)
+            m_splits = [base + (1 if i < rem else 0) for i in range(g)]
+        if isinstance(m_splits, torch.Tensor):
+            ms = m_splits
+        else:
+            if len(m_splits) != g:
+                raise ValueError(f"m_splits has {len(m_splits)} entries for {g} groups")
+            if align == 1 and sum(int(v) for v in m_splits) > rows:
+                raise ValueError("sum(m_splits) exceeds x rows")
+            ms = torch.tensor([int(v) for v in m_splits], dtype=torch.int32)
+        plan = GroupedGemmPlan(g, dev).from_splits(ms, align)
+    n_out = n // 2 if epilogue == "swiglu" else n
+    if out is None:
+        out = torch.empty((rows, n_out), dtype=torch.bfloat16, device=dev)
+    _lib.call("moe_grouped_gemm", _p(xc), _p(wc), _p(out), rows, plan.num_groups, g, n, k,
+              1 if epilogue == "swiglu" else 0, _p(plan.workspace), plan.nbytes, _stream(dev))
+    return out
+
+
+def swiglu(y: torch.Tensor) -> torch.Tensor:
+    """h = silu(y[:, :F]) * y[:, F:] for y [M,2F] bf16 (gate|up order)."""
+    _need_cuda("y", y)
+    _need_dtype("y", y, torch.bfloat16)
+    if y.dim() != 2 or y.shape[1] % 2:
+        raise ValueError("y must be [M,2F]")
+    yc = y.contiguous()
+    m, f2 = yc.shape
+    h = torch.empty((m, f2 // 2), dtype=yc.dtype, device=yc.device)
+    _lib.call("moe_swiglu", _p(yc), _p(h), m, f2 // 2, _stream(yc.device))
+    return h

@@ -1,0 +1,387 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 MoE expert-layer forward (tokens/s).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl b200|reference]
+
+N=1: the full single-GPU layer (T=16384 tokens, H=7168, E=256 experts, top-8,
+ffn=2048 SwiGLU, Zipf-skewed router logits). N>1 (launched by torchrun, one
+rank per GPU): the expert-parallel layer, T=16384 tokens per GPU, experts
+split evenly, NCCL all-to-all dispatch/combine. Prints one JSON line on rank 0.
+
+  value  tokens/s of the whole job, inputs resident in HBM, CUDA-event timed
+         (max over ranks), weak scaling;
+  e2e    the same through the public layer API with host buffers: pinned
+         H2D of x and logits and D2H of the output inside every timed step;
+  roofline  the dominant kernel (fc1 grouped GEMM, tcgen05) against the
+         measured bf16 peak; stages  per-stage device times;
+  cpu_baseline  the numpy restatement of the same layer (oracle/) on this
+         host's cores over a bounded token sample (rank 0, N=1 only).
+--impl reference times that CPU restatement alone (the reference's own path
+is PyTorch-on-CPU code that cannot run without its sources).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "1188b-reference-kernels_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "MoE-layer fwd tokens/s"
+UNIT = "tokens/s"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
+    ap.add_argument("--tokens", type=int, default=16384, help="tokens per GPU")
+    ap.add_argument("--hidden", type=int, default=7168)
+    ap.add_argument("--experts", type=int, default=256)
+    ap.add_argument("--ffn", type=int, default=2048)
+    ap.add_argument("--topk", type=int, default=8)
+    ap.add_argument("--routing", choices=["zipf", "uniform"], default="zipf")
+    ap.add_argument("--cpu-tokens", type=int, default=1024,
+                    help="token sample of the CPU baseline (per step for --impl reference)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true")
+    return ap.parse_args()
+
+
+def load_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+def config_dict(a, world):
+    return {"workload": "moe_layer_fwd" if world == 1 else "moe_layer_fwd_ep",
+            "tokens_per_gpu": a.tokens, "hidden": a.hidden, "experts": a.experts,
+            "topk": a.topk, "ffn": a.ffn, "routing": a.routing,
+            "parallelism": f"ep{world}" if world > 1 else "single",
+            "l2": "no flush: every step streams >22 GB of expert weights and 0.25 GB of "
+                  "activations, both larger than the 126 MB L2"}
+
+
+def zipf_bias(e, routing):
+    import torch
+    if routing != "zipf":
+        return torch.zeros(e)
+    g = torch.Generator().manual_seed(7)
+    r = torch.randperm(e, generator=g).float() + 1.0
+    return -1.5 * torch.log(r)
+
+
+# --------------------------------------------------------------------------- clocks
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, bus_id):
+        self.bus_id = bus_id
+        self.proc = None
+        self.path = None
+
+    def start(self):
+        try:
+            fd, self.path = tempfile.mkstemp(suffix=".csv")
+            os.close(fd)
+            cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                   "-lms", "200"]
+            if self.bus_id:
+                cmd += ["-i", self.bus_id]
+            self.proc = subprocess.Popen(cmd, stdout=open(self.path, "w"),
+                                         stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        time.sleep(0.25)
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except Exception:
+            self.proc.kill()
+        rows = []
+        for line in Path(self.path).read_text().splitlines():
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) >= 9:
+                rows.append(parts)
+        os.unlink(self.path)
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v == "Active"})
+        pw = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+                "samples": len(rows), "power_w_max": max(pw) if pw else None}
+
+
+# --------------------------------------------------------------------------- CPU port
+def cpu_layer_sample(a, tokens, seed=0):
+    """Times the numpy restatement of the layer on `tokens` tokens with the
+    bench's shapes. Expert weights come from a pool of 8 fp32 matrices (the
+    per-token work is unchanged; 256 distinct fp32 experts would need 45 GB of
+    host memory). Returns (seconds, tokens)."""
+    import numpy as np
+    from oracle import moe_oracle as orc
+    rng = np.random.default_rng(seed)
+    h, e, f, k = a.hidden, a.experts, a.ffn, a.topk
+    x = orc.f32_to_bf16(rng.standard_normal((tokens, h), dtype=np.float32))
+    bias = zipf_bias(e, a.routing).numpy()
+    lg = rng.standard_normal((tokens, e), dtype=np.float32)
+    pool = 8
+    w1p = [(rng.standard_normal((2 * f, h), dtype=np.float32) * 0.02) for _ in range(pool)]
+    w2p = [(rng.standard_normal((h, f), dtype=np.float32) * 0.02) for _ in range(pool)]
+    w1 = [w1p[i % pool] for i in range(e)]
+    w2 = [w2p[i % pool] for i in range(e)]
+    t0 = time.perf_counter()
+    _, _, rmap, probs = orc.router(lg, k, bias, "softmax", True)
+    map_et, map_te, counts, n = orc.row_id_map(rmap)
+    xp, _ = orc.permute(x, map_te, None, n)
+    hmid = orc.grouped_gemm(xp, w1, counts, "swiglu")
+    y = orc.grouped_gemm(hmid, w2, counts)
+    orc.unpermute(y, map_et, probs, "dense")
+    return time.perf_counter() - t0, tokens
+
+
+def cpu_threads():
+    try:
+        from threadpoolctl import threadpool_info
+        n = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
+        if n:
+            return int(max(n))
+    except Exception:
+        pass
+    return os.cpu_count() or 1
+
+
+def run_reference_arm(a, world, rank):
+    if rank != 0:
+        return
+    for _ in range(a.warmup):
+        cpu_layer_sample(a, a.cpu_tokens, seed=1)
+    times = []
+    for s in range(a.steps):
+        dt, n = cpu_layer_sample(a, a.cpu_tokens, seed=2 + s)
+        times.append(dt)
+    total = sum(times)
+    value = a.cpu_tokens * a.steps / total
+    sample = (f"{a.cpu_tokens} tokens per step of the {a.tokens}-token layer (same H/E/F/top-k, "
+              f"{a.routing} routing), numpy restatement, expert weights from an fp32 pool of 8")
+    line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": 1e3 * total / a.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "impl": "reference", "config": config_dict(a, world),
+            "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------- GPU arm
+def read_traffic():
+    p = ROOT / "profiles" / "grouped_gemm_fc1_layer.txt"
+    if not p.exists():
+        return None
+    for line in p.read_text().splitlines():
+        if line.startswith("dram_bytes_per_launch_full:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def main():
+    a = parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.impl == "reference":
+        run_reference_arm(a, world, rank)
+        return
+
+    import torch
+    import torch.distributed as dist
+    import moe_b200
+    from moe_b200 import _lib
+
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=dev)
+    moe_b200.load_library()
+
+    t, h, e, f, k = a.tokens, a.hidden, a.experts, a.ffn, a.topk
+    e_loc = e // world
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    x = torch.randn(t, h, device=dev, generator=g).to(torch.bfloat16)
+    logits = torch.randn(t, e, device=dev, generator=g)
+    bias = zipf_bias(e, a.routing).to(dev)
+    w = moe_b200.MoEWeights.random(e_loc, h, f, dev, seed=77 + rank)
+    if world == 1:
+        layer = moe_b200.MoELayer(w, topk=k, expert_bias=bias)
+        stage_names = ["start", "routing", "permute", "fc1", "fc2", "combine"]
+    else:
+        from moe_b200.ep import MoELayerEP
+        layer = MoELayerEP(w, e, topk=k, expert_bias=bias)
+        stage_names = ["start", "local_dispatch", "a2a_dispatch", "fc1", "fc2", "a2a_combine",
+                       "combine"]
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+
+    for _ in range(a.warmup):
+        layer(x, logits)
+    torch.cuda.synchronize()
+    assert layer.plan.device_error() == 0, "grouped GEMM reported a device error"
+
+    # ---- device-timed region: inputs resident in HBM
+    events = [{n: torch.cuda.Event(enable_timing=True) for n in stage_names}
+              for _ in range(a.steps)]
+    bus = None
+    try:
+        bus = torch.cuda.get_device_properties(dev).pci_bus_id
+    except Exception:
+        bus = str(local_rank)
+    sampler = ClockSampler(bus)
+    barrier()
+    torch.cuda.synchronize()
+    sampler.start()
+    time.sleep(0.3)
+    launches0 = _lib.launch_count
+    t_start = torch.cuda.Event(enable_timing=True)
+    t_end = torch.cuda.Event(enable_timing=True)
+    t_start.record()
+    for s in range(a.steps):
+        layer.events = events[s]
+        layer(x, logits)
+    t_end.record()
+    torch.cuda.synchronize()
+    barrier()
+    launches = _lib.launch_count - launches0
+    clocks = sampler.stop()
+    layer.events = None
+    ms_total = t_start.elapsed_time(t_end)
+    stage_ms = {}
+    for i in range(1, len(stage_names)):
+        n0, n1 = stage_names[i - 1], stage_names[i]
+        stage_ms[n1] = sum(ev[n0].elapsed_time(ev[n1]) for ev in events) / a.steps
+    fc1_ms = stage_ms["fc1"]
+    fc1_rows = t * k if world == 1 else int(layer.plan._keep.sum().item())
+    fc2_ms = stage_ms["fc2"]
+
+    ms_step = ms_total / a.steps
+    if world > 1:
+        v = torch.tensor([ms_step], device=dev)
+        dist.all_reduce(v, op=dist.ReduceOp.MAX)
+        ms_step = float(v.item())
+    value = world * t / (ms_step / 1e3)
+
+    # ---- end-to-end through the public API with host buffers
+    e2e = None
+    if not a.no_e2e:
+        x_h = x.cpu().pin_memory()
+        lg_h = logits.cpu().pin_memory()
+        out_h = torch.empty((t, h), dtype=torch.bfloat16).pin_memory()
+        x_d = torch.empty_like(x)
+        lg_d = torch.empty_like(logits)
+        for _ in range(2):
+            x_d.copy_(x_h, non_blocking=True)
+            lg_d.copy_(lg_h, non_blocking=True)
+            out_h.copy_(layer(x_d, lg_d), non_blocking=True)
+        barrier()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            x_d.copy_(x_h, non_blocking=True)
+            lg_d.copy_(lg_h, non_blocking=True)
+            out_h.copy_(layer(x_d, lg_d), non_blocking=True)
+        e1.record()
+        torch.cuda.synchronize()
+        barrier()
+        e2e_ms = e0.elapsed_time(e1) / a.steps
+        if world > 1:
+            v = torch.tensor([e2e_ms], device=dev)
+            dist.all_reduce(v, op=dist.ReduceOp.MAX)
+            e2e_ms = float(v.item())
+        e2e = {"value": world * t / (e2e_ms / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": x.numel() * 2 + logits.numel() * 4,
+               "d2h_bytes_per_step": t * h * 2, "ms_per_step": e2e_ms}
+
+    peaks, peak_kind = load_peaks()
+    fc1_flops = 2.0 * fc1_rows * (2 * f) * h
+    fc2_flops = 2.0 * fc1_rows * h * f
+    achieved = fc1_flops / (fc1_ms / 1e3) / 1e12
+    peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    traffic = read_traffic()
+    rows = fc1_rows
+    perm_bytes = t * h * 2 + rows * h * 2 + t * e * 8
+    comb_bytes = rows * h * 2 + t * h * 2 + t * e * 8 + t * e * 4
+    stages = {n: round(ms, 4) for n, ms in stage_ms.items()}
+    extra = {
+        "stages_ms": stages,
+        "fc1_tflops": round(achieved, 1),
+        "fc2_tflops": round(fc2_flops / (fc2_ms / 1e3) / 1e12, 1),
+        "gemm_frac_of_peak": round((fc1_flops + fc2_flops) / ((fc1_ms + fc2_ms) / 1e3) / 1e12 / peak, 4),
+        "peak_kind": f"bf16 sustained, of {peak_kind}",
+        "hbm_peak_gbs": hbm,
+    }
+    if world == 1:
+        extra["permute_gbs"] = round(perm_bytes / (stage_ms["permute"] / 1e3) / 1e9, 1)
+        extra["combine_gbs"] = round(comb_bytes / (stage_ms["combine"] / 1e3) / 1e9, 1)
+
+    cpu = None
+    if world == 1 and rank == 0 and not a.no_cpu_baseline:
+        dt, n = cpu_layer_sample(a, a.cpu_tokens)
+        cpu = {"value": n / dt, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+               "sample": f"{n} tokens of the {t}-token layer (same H/E/F/top-k, {a.routing} "
+                         f"routing), numpy restatement, expert weights from an fp32 pool of 8"}
+
+    if rank == 0:
+        line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+                "steps": a.steps, "warmup": a.warmup, "ms_per_step": ms_step,
+                "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                "dtype": "bf16", "data": "synthetic (seeded N(0,1) activations/logits, "
+                "N(0,0.02) weights, Zipf expert bias)",
+                "config": config_dict(a, world),
+                "roofline": {"bound": "tensor", "kernel": "grouped_gemm fc1 (tcgen05, fused SwiGLU)",
+                             "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                             "frac": round(achieved / peak, 4), "traffic": traffic},
+                "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks}
+        line.update(extra)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,163 @@
+/*
+ * moe_b200.h - C ABI of the B200 (sm_100a) MoE expert-layer forward path.
+ *
+ * Every entry point takes plain device pointers, sizes and a cudaStream_t,
+ * launches asynchronously on that stream and returns a moe_status. On a
+ * non-zero status, moe_b200_last_error() returns a message for the calling
+ * thread. Outputs are caller-allocated; inputs are only read. No entry point
+ * synchronises the stream or allocates device memory; the ones that need
+ * scratch take a caller-provided workspace whose size the matching
+ * *_workspace_size function reports.
+ *
+ * Each function names the reference interface it replaces. The reference
+ * binds its kernels through pybind functions that take torch tensors and call
+ * a raw-pointer launcher on the default stream; this header is the raw-pointer
+ * layer, with an explicit stream and a status code added.
+ *
+ * Row-id maps follow the reference convention: entry >= 0 is a destination
+ * (permute) or source (unpermute) row of the expert-major permuted buffer,
+ * -1 means "token not routed to this expert".
+ */
+#ifndef MOE_B200_H
+#define MOE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* moe_stream_t; /* == cudaStream_t */
+
+typedef enum {
+  MOE_OK = 0,
+  MOE_ERR_INVALID = 1,     /* bad argument: null pointer, size, alignment, dtype code */
+  MOE_ERR_UNSUPPORTED = 2, /* valid but outside what this build supports (e.g. k > 32) */
+  MOE_ERR_CUDA = 3,        /* a CUDA runtime/driver call or launch failed */
+  MOE_ERR_DEVICE = 4       /* a kernel reported an error word (see moe_grouped_gemm) */
+} moe_status;
+
+/* Message for the last failing call on this host thread ("" if none). */
+const char* moe_b200_last_error(void);
+/* ABI version: bumped on any signature change. */
+int moe_b200_abi_version(void);
+
+/* ------------------------------------------------------------------------ */
+/* a1  Row-wise top-k, largest, sorted, ties -> lower column index.          */
+/* Replaces kernel_results/case23_aten_topk/binding.cpp:4 (launch_topk) and  */
+/* matches kernel_cases/case23_ref_aten_topk.py:47-62 (reference_topk).      */
+/* input [M,N] fp32 row-major; values [M,k] fp32; indices [M,k] int64.       */
+/* 1 <= k <= min(N, 32); N <= 4096.                                          */
+int moe_topk_f32(const float* input, float* values, int64_t* indices, int64_t M, int64_t N,
+                 int32_t k, moe_stream_t stream);
+
+/* a1+a2  Fused router: score -> top-k -> gate weights -> routing map.       */
+/* score_mode 0: select on the raw logits, gate = logit.                     */
+/* score_mode 1: softmax over the row, gate = softmax prob; with renorm != 0 */
+/*               the k selected probs are rescaled to sum to 1.              */
+/* Selection order is the logits' (softmax is monotone); ties -> lower index.*/
+/* bias (nullable, [E] fp32) is added to the logits before everything.       */
+/* Outputs (each nullable): topk_vals [T,k] fp32, topk_idx [T,k] int64,      */
+/* routing_map [T,E] uint8/bool, probs [T,E] fp32 (gate at selected, else 0).*/
+/* The routing map and dense probs are the inputs the reference builds with  */
+/* scatter_ (kernel_cases/case12_moe_row_id_map_pass2.py:30-40,              */
+/* kernel_cases/case17_moe_permute_with_mask_map.py:78-90).                  */
+int moe_router_topk(const float* logits, const float* bias, int64_t T, int64_t E, int32_t k,
+                    int32_t score_mode, int32_t renorm, float* topk_vals, int64_t* topk_idx,
+                    uint8_t* routing_map, float* probs, moe_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* a3  routing_map [T,E] bool -> row_id_map, expert-major destinations:      */
+/*   row[t,e] = base[e] + #{t' <= t : map[t',e]} - 1 if map[t,e] else -1     */
+/* base[e] = sum over e' < e of roundup(count[e'], align) (align = 1 is the  */
+/* reference's make_row_id_map, kernel_cases/case12_moe_row_id_map_pass2.py: */
+/* 43-50; larger aligns pad every expert segment for tile-aligned GEMMs).    */
+/* Replaces the five launchers of kernel_results/case12_moe_row_id_map_pass2 */
+/* /binding.cpp:7-11. Outputs (nullable except one of the maps):             */
+/*   row_id_map_et [E,T] int64, row_id_map_te [T,E] int64,                   */
+/*   expert_counts [E] int32, num_out [1] int64 (padded total rows).          */
+int moe_row_id_map_workspace_size(int64_t T, int64_t E, size_t* bytes);
+int moe_row_id_map(const uint8_t* routing_map, int64_t T, int64_t E, int64_t align,
+                   int64_t* row_id_map_et, int64_t* row_id_map_te, int32_t* expert_counts,
+                   int64_t* num_out, void* workspace, size_t workspace_bytes,
+                   moe_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* a4  Permute with a [T,E] map: out[row[t,e]] = x[t], pp[row[t,e]] =        */
+/* probs[t,e]. Replaces kernel_results/case17_moe_permute_with_mask_map/     */
+/* binding.cpp:5-6 (permute_rt_launcher); semantics of kernel_cases/case17_  */
+/* moe_permute_with_mask_map.py:58-71. x/out bf16 (any 2-byte type: pure     */
+/* copy), H % 8 == 0, pointers 16-byte aligned. probs / permuted_probs       */
+/* nullable together. Rows of out no map entry points at are left untouched. */
+/* Map entries must lie in [-1, num_out).                                    */
+int moe_permute_mask_map(const void* x, const int64_t* row_id_map_te, const float* probs,
+                         void* out, float* permuted_probs, int64_t T, int64_t H, int64_t E,
+                         int64_t num_out, moe_stream_t stream);
+
+/* a5  Same with an expert-major [E,T] map of int64 (idx_bits 64) or int32   */
+/* (idx_bits 32): kernel_cases/case22_ref_moe_permute_mask_kernel_true.py:   */
+/* 47-69, case21_ref_permute_with_mask_map_trans.py:52-68,                   */
+/* case30_ref_moe_permute_mask_kernel.py:44-58 (probs null).                 */
+int moe_permute_mask_map_trans(const void* x, const void* row_id_map_et, int32_t idx_bits,
+                               const float* probs, void* out, float* permuted_probs, int64_t T,
+                               int64_t H, int64_t E, int64_t num_out, moe_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* a6/a7/a8  Unpermute (combine) with an expert-major [E,T] map:             */
+/*   acc[t] = sum over e ascending of w(t,e) * float(pin[row[e,t]])          */
+/*   out[t] = bf16_rne(acc[t]); acc_out (nullable, [T,H] fp32) = acc.         */
+/* w = 1 when probs is null (kernel_results/case15_moe_unpermute_mask_fwd/   */
+/* binding.cpp:5-8, kernel_cases/case15_moe_unpermute_mask_fwd.py:58-64,    */
+/* case24_ref_moe_unpermute_mask_kernel_false.py:45-68); otherwise           */
+/* w = probs[t,e] ([T,E] fp32, probs_mode 0) or w = probs[row[e,t]]          */
+/* (permuted [num_rows] fp32, probs_mode 1). Products and sums are separate  */
+/* fp32 roundings (no FMA), accumulated in ascending expert order.           */
+int moe_unpermute_mask(const void* pin, const void* row_id_map_et, int32_t idx_bits,
+                       const float* probs, int32_t probs_mode, void* out, float* acc_out,
+                       int64_t T, int64_t H, int64_t E, int64_t num_rows, moe_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* a9/a10/a11  Grouped GEMM on tcgen05 tensor cores (bf16 in, fp32 acc).     */
+/* out[r, :] = x[r, :] @ w[widx(g)]^T for the rows r of group g, where       */
+/* w is [num_w, N, K] ("[out,in]" as in kernel_cases/case03_moe_grouped_gemm */
+/* _fc1_fwd.py:57-64 and case04_moe_grouped_gemm_fc2_fwd.py:57-64).          */
+/* Groups are described on the device by a group table built with            */
+/* moe_grouped_gemm_plan_* below, so no host synchronisation is needed.      */
+/* epilogue 0: out [rows, N] bf16.                                           */
+/* epilogue 1 (SwiGLU, fc1): N = 2F with rows [0,F) = gate, [F,2F) = up;     */
+/*   out [rows, F] bf16 = silu(g) * u with g, u the bf16-rounded GEMM        */
+/*   outputs (the unfused chain fc1 -> bf16 -> silu(gate)*up).               */
+/* x [x_rows, K] bf16, K % 8 == 0, N % 8 == 0 (F % 8 for SwiGLU).            */
+/* workspace: moe_grouped_gemm_workspace_size(G) bytes, 256-byte aligned.    */
+int moe_grouped_gemm_workspace_size(int64_t G, size_t* bytes);
+
+/* Plan from per-group row counts (device int32 [G], contiguous groups in    */
+/* order; each group's first row rounded up to `align`): widx(g) = g.        */
+int moe_grouped_gemm_plan_splits(const int32_t* m_splits, int64_t G, int64_t align,
+                                 void* workspace, size_t workspace_bytes, moe_stream_t stream);
+
+/* Plan for expert-parallel receive buffers: rows arrive as num_src blocks   */
+/* (one per source rank) of num_w expert segments each, counts[s*num_w + e]. */
+/* Groups are ordered expert-major (all sources of expert 0, then expert 1), */
+/* so each weight matrix is streamed once; widx(g) = e.                      */
+int moe_grouped_gemm_plan_ep(const int32_t* counts, int64_t num_src, int64_t num_w,
+                             void* workspace, size_t workspace_bytes, moe_stream_t stream);
+
+int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t x_rows, int64_t G,
+                     int64_t num_w, int64_t N, int64_t K, int32_t epilogue,
+                     const void* workspace, size_t workspace_bytes, moe_stream_t stream);
+
+/* Reads the device error word a previous moe_grouped_gemm left in the       */
+/* workspace (0 = none; blocking: synchronises the stream).                  */
+int moe_grouped_gemm_check(const void* workspace, size_t workspace_bytes, moe_stream_t stream,
+                           int32_t* device_error);
+
+/* a11 standalone: h[M,F] = bf16(silu(y[:, :F]) * y[:, F:]) for y [M,2F].    */
+int moe_swiglu(const void* y, void* h, int64_t M, int64_t F, moe_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* MOE_B200_H */

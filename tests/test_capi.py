@@ -1,0 +1,87 @@
+"""CPU checks of the C ABI: the library loads, exports every symbol that
+include/moe_b200.h declares, and rejects bad arguments before touching a GPU.
+No kernel is launched here."""
+import ctypes
+import re
+from ctypes import byref, c_size_t
+
+import pytest
+
+from conftest import PKG, ROOT
+
+
+@pytest.fixture(scope="module")
+def lib():
+    import moe_b200
+    from moe_b200 import build
+    build.build()
+    return moe_b200.load_library()
+
+
+def header_symbols():
+    text = (ROOT / "include" / "moe_b200.h").read_text()
+    return set(re.findall(r"^\s*(?:int|const char\*)\s+(moe_\w+)\s*\(", text, re.M))
+
+
+def test_header_symbols_exported(lib):
+    syms = header_symbols()
+    assert len(syms) >= 15
+    for s in syms:
+        assert hasattr(lib, s), s
+    from moe_b200 import _lib
+    assert syms == set(_lib.EXPORTED)
+
+
+def test_abi_version(lib):
+    assert lib.moe_b200_abi_version() == 1
+
+
+def test_workspace_sizes(lib):
+    n = c_size_t(0)
+    assert lib.moe_row_id_map_workspace_size(16384, 256, byref(n)) == 0
+    assert n.value >= 256 * 256 * 4 and n.value % 256 == 0
+    assert lib.moe_grouped_gemm_workspace_size(256, byref(n)) == 0
+    assert n.value >= 256 + 4 * 256 * 4
+    assert lib.moe_grouped_gemm_workspace_size(0, byref(n)) == 1
+    assert b"out of range" in lib.moe_b200_last_error()
+
+
+def test_invalid_arguments_are_rejected_without_launch(lib):
+    # odd row pointer (rows move in 2-byte units at least)
+    assert lib.moe_permute_mask_map(17, 16, None, 32, None, 4, 12, 2, 4, None) == 1
+    assert b"aligned" in lib.moe_b200_last_error()
+    # null rows
+    assert lib.moe_permute_mask_map(None, None, None, None, None, 4, 12, 2, 4, None) == 1
+    assert b"null" in lib.moe_b200_last_error()
+    # probs without permuted_probs
+    assert lib.moe_permute_mask_map(16, 16, 16, 16, None, 4, 8, 2, 4, None) == 1
+    assert b"both" in lib.moe_b200_last_error()
+    # bad idx_bits
+    assert lib.moe_unpermute_mask(None, None, 16, None, 0, None, None, 4, 8, 2, 4, None) == 1
+    # k beyond this build
+    assert lib.moe_topk_f32(16, 16, 16, 4, 64, 17, None) == 2
+    # empty shapes are no-ops that succeed without a device
+    assert lib.moe_permute_mask_map(None, None, None, None, None, 0, 8, 2, 0, None) == 0
+    assert lib.moe_topk_f32(16, 16, 16, 0, 64, 8, None) == 0
+    # GEMM argument checks
+    assert lib.moe_grouped_gemm(None, None, None, 10, 4, 4, 256, 12, 0, None, 0, None) == 1
+    assert lib.moe_grouped_gemm(None, None, None, 10, 4, 4, 256, 64, 2, None, 0, None) == 1
+
+
+def test_ops_refuse_cpu_tensors():
+    import torch
+    import moe_b200
+    with pytest.raises(ValueError):
+        moe_b200.topk(torch.randn(4, 8), 2)
+    with pytest.raises(ValueError):
+        moe_b200.permute(torch.zeros(4, 8, dtype=torch.bfloat16),
+                         torch.zeros(4, 2, dtype=torch.int64))
+    with pytest.raises(ValueError):
+        moe_b200.grouped_gemm(torch.zeros(4, 8, dtype=torch.bfloat16),
+                              torch.zeros(1, 8, 8, dtype=torch.bfloat16))
+
+
+def test_product_package_does_not_import_oracle():
+    pat = re.compile(r"^\s*(from\s+oracle\b|import\s+oracle\b)|moe_oracle", re.M)
+    for p in PKG.rglob("*.py"):
+        assert not pat.search(p.read_text()), p

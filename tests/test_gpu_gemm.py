@@ -1,0 +1,206 @@
+"""GPU parity of the tcgen05 grouped GEMM (fc1 / fc2) and the SwiGLU epilogue.
+
+Tolerance: rtol 2e-2 / atol 1e-2 against the fp32-accumulated oracle (the
+north-star bar for GEMM outputs), plus the reference's own bf16 GEMM rule
+(kernel_cases/case35_...:66-75: fail only if max_rel > 2e-2 and
+max_abs > 2e-1). Both sides accumulate in fp32; they differ only in
+summation order, so almost every output matches to the last bf16 bit.
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import from_u16, load_bundle, u16
+from oracle import moe_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+RTOL, ATOL = 2e-2, 1e-2
+
+
+def assert_gemm_close(got_bf16: torch.Tensor, ref_f32: np.ndarray, tag="", ulp_frac=0.999):
+    assert tuple(got_bf16.shape) == ref_f32.shape, tag
+    if ref_f32.size == 0:
+        return
+    got = orc.bf16_to_f32(u16(got_bf16))
+    np.testing.assert_allclose(got, ref_f32, rtol=RTOL, atol=ATOL, err_msg=tag)
+    diff = np.abs(got - ref_f32)
+    max_rel = (diff / np.maximum(np.abs(ref_f32), 1.0)).max()
+    assert not (max_rel > 2e-2 and diff.max() > 2e-1), tag
+    # summation order only: nearly all elements within one bf16 ulp
+    # (SwiGLU rounds its two GEMM inputs to bf16 first, so a 1-ulp input flip
+    # can move the output by slightly more; its bar is 0.995.)
+    ulp_ok = diff <= np.abs(ref_f32) * 2.0 ** -7 + 1e-6
+    assert ulp_ok.mean() > ulp_frac, (tag, ulp_ok.mean())
+
+
+def fp32_ref(x_u16, w_u16, splits, row_starts=None, swiglu=False, widx=None):
+    """Unrounded per-group fp32 products (rounded to bf16 first for SwiGLU)."""
+    n = w_u16.shape[1]
+    out = np.zeros((x_u16.shape[0], n // 2 if swiglu else n), np.float32)
+    off = 0
+    for g, m in enumerate(splits):
+        s = off if row_starts is None else row_starts[g]
+        if m:
+            wi = g if widx is None else widx[g]
+            y = orc.bf16_to_f32(x_u16[s:s + m]) @ orc.bf16_to_f32(w_u16[wi]).T
+            if swiglu:
+                yb = orc.bf16_to_f32(orc.f32_to_bf16(y))
+                y = orc.swiglu_f32(yb[:, :n // 2], yb[:, n // 2:])
+            out[s:s + m] = y
+        off = s + m
+    return out
+
+
+def test_reference_models_golden(cuda_dev, golden):
+    z = golden("gemm_swiglu.npz")
+    for tag, case in (("c03", "case03_moe_grouped_gemm_fc1_fwd"),
+                      ("c04", "case04_moe_grouped_gemm_fc2_fwd"),
+                      ("c10", "case03_moe_grouped_gemm_fc1_fwd")):
+        y = load_bundle(case).kernel_function(from_u16(z[f"{tag}_x"], cuda_dev),
+                                              from_u16(z[f"{tag}_w"], cuda_dev))
+        assert y.dtype == torch.bfloat16 and y.shape == z[f"{tag}_y"].shape
+        assert_gemm_close(y, orc.bf16_to_f32(z[f"{tag}_y"]), tag)
+        assert_gemm_close(y, fp32_ref(z[f"{tag}_x"], z[f"{tag}_w"], z[f"{tag}_splits"]), tag)
+
+
+def test_single_expert_fp32_golden(cuda_dev, golden):
+    z = golden("gemm_swiglu.npz")
+    y = load_bundle("case35_bf16_gemm_nt").kernel_function(from_u16(z["c35_x"], cuda_dev),
+                                                           from_u16(z["c35_w"], cuda_dev))
+    assert_gemm_close(y, z["c35_y"], "c35")
+
+
+def _rand_bf16(g, *shape, std=1.0):
+    return (torch.randn(*shape, generator=g) * std).to(torch.bfloat16)
+
+
+@pytest.mark.parametrize("splits,n,k", [
+    ([0, 1, 127, 128, 129, 300, 0, 5], 256, 128),
+    ([512, 77, 1000], 512, 7168),
+    ([64] * 16, 768, 2048),
+    ([3000], 4096, 512),
+    ([10, 0, 0, 250], 200, 72),         # N, K not multiples of the tile
+    ([0, 0, 0], 256, 64),               # no rows at all
+])
+def test_ragged_vs_oracle(cuda_dev, splits, n, k):
+    import moe_b200
+    g = torch.Generator().manual_seed(sum(splits) + n + k)
+    rows = max(sum(splits), 1)
+    x = _rand_bf16(g, rows, k)
+    w = _rand_bf16(g, len(splits), n, k, std=0.05)
+    y = moe_b200.grouped_gemm(x.to(cuda_dev), w.to(cuda_dev), splits)
+    ref = fp32_ref(u16(x), u16(w), splits)
+    assert_gemm_close(y[:sum(splits)], ref[:sum(splits)], str(splits))
+
+
+@pytest.mark.parametrize("splits,f,k", [([5, 200, 0, 129, 64], 128, 256), ([1024, 300], 2048, 7168),
+                                        ([40, 8], 72, 64)])
+def test_swiglu_epilogue_vs_oracle(cuda_dev, splits, f, k):
+    import moe_b200
+    g = torch.Generator().manual_seed(f + k)
+    rows = sum(splits)
+    x = _rand_bf16(g, rows, k)
+    w = _rand_bf16(g, len(splits), 2 * f, k, std=0.05)
+    h = moe_b200.grouped_gemm(x.to(cuda_dev), w.to(cuda_dev), splits, epilogue="swiglu")
+    ref = fp32_ref(u16(x), u16(w), splits, swiglu=True)
+    assert_gemm_close(h, ref, "swiglu", ulp_frac=0.995)
+    # fused == unfused chain (GEMM -> bf16 -> SwiGLU kernel), bit for bit
+    y = moe_b200.grouped_gemm(x.to(cuda_dev), w.to(cuda_dev), splits)
+    h2 = moe_b200.swiglu(y)
+    assert torch.equal(h, h2)
+
+
+def test_standalone_swiglu_golden(cuda_dev, golden):
+    import moe_b200
+    z = golden("gemm_swiglu.npz")
+    h = moe_b200.swiglu(from_u16(z["swiglu_y"], cuda_dev))
+    ref = orc.bf16_to_f32(z["swiglu_h"])
+    got = orc.bf16_to_f32(u16(h))
+    assert (np.abs(got - ref) <= np.abs(ref) * 2 ** -8 + 1e-6).all()
+    np.testing.assert_array_equal(u16(h), orc.swiglu(z["swiglu_y"]))
+
+
+def test_aligned_segments(cuda_dev):
+    """Groups starting on 128-row boundaries (padded permute layout)."""
+    import moe_b200
+    g = torch.Generator().manual_seed(11)
+    splits = [100, 0, 300, 1]
+    starts, off = [], 0
+    for m in splits:
+        starts.append(off)
+        off += -(-m // 128) * 128
+    x = _rand_bf16(g, off, 256)
+    w = _rand_bf16(g, 4, 256, 256, std=0.05)
+    y = moe_b200.grouped_gemm(x.to(cuda_dev), w.to(cuda_dev), splits, align=128)
+    ref = fp32_ref(u16(x), u16(w), splits, row_starts=starts)
+    for s, m in zip(starts, splits):
+        assert_gemm_close(y[s:s + m], ref[s:s + m], "aligned")
+
+
+def test_ep_plan_expert_major_groups(cuda_dev):
+    """Receive buffer of 3 source ranks x 4 local experts, groups walked expert-major."""
+    import moe_b200
+    g = torch.Generator().manual_seed(5)
+    num_src, num_w, n, k = 3, 4, 256, 128
+    counts = torch.randint(0, 90, (num_src * num_w,), generator=g, dtype=torch.int32)
+    counts[5] = 0
+    rows = int(counts.sum())
+    x = _rand_bf16(g, rows, k)
+    w = _rand_bf16(g, num_w, n, k, std=0.05)
+    plan = moe_b200.GroupedGemmPlan(num_src * num_w, cuda_dev).from_ep_counts(
+        counts.to(cuda_dev), num_src, num_w)
+    y = moe_b200.grouped_gemm(x.to(cuda_dev), w.to(cuda_dev), plan=plan)
+    # reference: segment (s,e) at its flat offset uses w[e]
+    c = counts.numpy()
+    starts = np.concatenate([[0], np.cumsum(c)[:-1]])
+    widx = [i % num_w for i in range(num_src * num_w)]
+    ref = fp32_ref(u16(x), u16(w), c, row_starts=starts, widx=widx)
+    assert_gemm_close(y, ref, "ep")
+    assert plan.device_error() == 0
+
+
+def test_full_fc1_fc2_shapes_spot_check(cuda_dev):
+    """BASELINE cfg3 shapes (T=8192 top-8 routing -> 65536 rows, E=256, H=7168,
+    F=2048) checked on sampled rows of sampled experts."""
+    import moe_b200
+    t, e, h, f, topk = 8192, 256, 7168, 2048, 8
+    gc = torch.Generator().manual_seed(3)
+    lg = torch.randn(t, e, generator=gc)
+    r = moe_b200.router_topk(lg.to(cuda_dev), topk, "softmax", renorm=True, outputs="maps")
+    m = moe_b200.row_id_map(r.routing_map)
+    counts = m.counts.cpu().numpy()
+    rows = t * topk
+    gd = torch.Generator(device=cuda_dev).manual_seed(3)
+    x = torch.randn(rows, h, device=cuda_dev, generator=gd).to(torch.bfloat16)
+    w1 = (torch.randn(e, 2 * f, h, device=cuda_dev, generator=gd) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(e, h, f, device=cuda_dev, generator=gd) * 0.02).to(torch.bfloat16)
+    plan = moe_b200.GroupedGemmPlan(e, cuda_dev).from_splits(m.counts)
+    hmid = moe_b200.grouped_gemm(x, w1, epilogue="swiglu", plan=plan)
+    y = moe_b200.grouped_gemm(hmid, w2, plan=plan)
+    assert plan.device_error() == 0
+    starts = np.concatenate([[0], np.cumsum(counts)[:-1]])
+    rng = np.random.default_rng(0)
+    for gidx in [0, 1, e // 2, e - 1] + list(rng.integers(0, e, 4)):
+        cnt = int(counts[gidx])
+        if cnt == 0:
+            continue
+        sel = np.unique(np.concatenate([[0, cnt - 1], rng.integers(0, cnt, 6)]))
+        rr = starts[gidx] + sel
+        xs = u16(x[torch.as_tensor(rr, device=cuda_dev)])
+        hs = fp32_ref(xs, u16(w1[gidx:gidx + 1]), [len(rr)], swiglu=True)
+        assert_gemm_close(hmid[torch.as_tensor(rr, device=cuda_dev)], hs, f"fc1 g{gidx}",
+                          ulp_frac=0.995)
+        ys = fp32_ref(u16(hmid[torch.as_tensor(rr, device=cuda_dev)]), u16(w2[gidx:gidx + 1]),
+                      [len(rr)])
+        assert_gemm_close(y[torch.as_tensor(rr, device=cuda_dev)], ys, f"fc2 g{gidx}")
+
+
+def test_bad_arguments(cuda_dev):
+    import moe_b200
+    x = torch.zeros(8, 20, dtype=torch.bfloat16, device=cuda_dev)  # K % 8 != 0
+    w = torch.zeros(1, 16, 20, dtype=torch.bfloat16, device=cuda_dev)
+    with pytest.raises(moe_b200.MoeError):
+        moe_b200.grouped_gemm(x, w, [8])
+    with pytest.raises(ValueError):
+        moe_b200.grouped_gemm(x.float(), w, [8])
