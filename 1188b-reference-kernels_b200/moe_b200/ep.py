@@ -61,23 +61,49 @@ class EPDispatcher:
         recv_splits = [int(v) for v in both[1]]
         return send_splits, recv_splits, recv
 
+    def _rows_a2a(self, src: torch.Tensor, in_splits: List[int], out_splits: List[int],
+                  out: Optional[torch.Tensor]) -> torch.Tensor:
+        if src.dim() != 2 or src.shape[0] != sum(in_splits):
+            raise ValueError(f"rows {tuple(src.shape)} do not match split sizes {in_splits}")
+        if out is None:
+            out = src.new_empty((sum(out_splits), src.shape[1]))
+        # Rows travel as raw bytes: every backend moves uint8, and the copy is
+        # bit-exact whatever the element type.
+        dist.all_to_all_single(out.view(torch.uint8), src.contiguous().view(torch.uint8),
+                               output_split_sizes=out_splits, input_split_sizes=in_splits,
+                               group=self.group)
+        return out
+
     def dispatch(self, xp: torch.Tensor, send_splits: List[int], recv_splits: List[int],
                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
-        if out is None:
-            out = xp.new_empty((sum(recv_splits),) + tuple(xp.shape[1:]))
-        dist.all_to_all_single(out, xp, output_split_sizes=recv_splits,
-                               input_split_sizes=send_splits, group=self.group)
-        return out
+        """Sends each destination rank its block of expert-major rows."""
+        return self._rows_a2a(xp, send_splits, recv_splits, out)
 
     def combine(self, y: torch.Tensor, send_splits: List[int], recv_splits: List[int],
                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Inverse of dispatch: returns rows to their source ranks, in the
         source's original (expert-major) order."""
-        if out is None:
-            out = y.new_empty((sum(send_splits),) + tuple(y.shape[1:]))
-        dist.all_to_all_single(out, y, output_split_sizes=send_splits,
-                               input_split_sizes=recv_splits, group=self.group)
-        return out
+        return self._rows_a2a(y, recv_splits, send_splits, out)
+
+
+def ep_group_table(recv_counts, num_src: int, num_w: int):
+    """Host restatement of the device group table for a receive buffer of
+    (source rank, local expert) segments, groups ordered expert-major:
+    returns (row_start, rows, widx) lists. The device planner
+    (moe_grouped_gemm_plan_ep) builds the same table on the GPU."""
+    c = [int(v) for v in recv_counts]
+    pos, acc = [], 0
+    for v in c:
+        pos.append(acc)
+        acc += v
+    starts, rows, widx = [], [], []
+    for e in range(num_w):
+        for s in range(num_src):
+            f = s * num_w + e
+            starts.append(pos[f])
+            rows.append(c[f])
+            widx.append(e)
+    return starts, rows, widx
 
 
 class MoELayerEP:

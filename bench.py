@@ -88,32 +88,44 @@ def zipf_bias(e, routing):
 
 # --------------------------------------------------------------------------- clocks
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi clock/throttle sampling (50 ms) around the measurement.
+
+    Samples are time-stamped on the host; the summary uses the samples that
+    fall inside the device-timed window, or, when that window is shorter than
+    the sampling period, the whole measurement (warm-up + timed + e2e steps).
+    """
+    FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
 
-    def __init__(self, bus_id):
-        self.bus_id = bus_id
+    def __init__(self, device_index):
+        self.device_index = device_index
         self.proc = None
         self.path = None
+        self.window = None
 
     def start(self):
         try:
             fd, self.path = tempfile.mkstemp(suffix=".csv")
             os.close(fd)
             cmd = ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                   "-lms", "200"]
-            if self.bus_id:
-                cmd += ["-i", self.bus_id]
+                   "-lms", "50", "-i", str(self.device_index)]
             self.proc = subprocess.Popen(cmd, stdout=open(self.path, "w"),
                                          stderr=subprocess.DEVNULL)
+            t0 = time.time()
+            while time.time() - t0 < 10 and Path(self.path).stat().st_size == 0:
+                time.sleep(0.05)
         except Exception:
             self.proc = None
+
+    def mark(self, t0, t1):
+        self.window = (t0, t1)
 
     def stop(self):
         if self.proc is None:
             return None
-        time.sleep(0.25)
+        time.sleep(0.2)
         self.proc.terminate()
         try:
             self.proc.wait(timeout=5)
@@ -122,19 +134,37 @@ class ClockSampler:
         rows = []
         for line in Path(self.path).read_text().splitlines():
             parts = [p.strip() for p in line.split(",")]
-            if len(parts) >= 9:
-                rows.append(parts)
+            if len(parts) < 9:
+                continue
+            try:
+                ts = time.mktime(time.strptime(parts[0].split(".")[0], "%Y/%m/%d %H:%M:%S"))
+                ts += float("0." + parts[0].split(".")[1]) if "." in parts[0] else 0.0
+            except Exception:
+                ts = None
+            rows.append((ts, parts))
         os.unlink(self.path)
         if not rows:
             return None
-        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({n for r in rows for n, v in zip(names, r[5:9]) if v == "Active"})
-        pw = [float(r[3]) for r in rows if r[3].replace(".", "").isdigit()]
+        scope = "bench run"
+        if self.window:
+            inside = [r for r in rows if r[0] is not None and
+                      self.window[0] - 0.05 <= r[0] <= self.window[1] + 0.05]
+            if inside:
+                rows, scope = inside, "timed window"
+
+        def num(v):
+            try:
+                return float(v)
+            except ValueError:
+                return None
+        sm = [v for v in (num(p[1]) for _, p in rows) if v is not None]
+        mx = [v for v in (num(p[2]) for _, p in rows) if v is not None]
+        pw = [v for v in (num(p[3]) for _, p in rows) if v is not None]
+        reasons = sorted({n for _, p in rows for n, v in zip(self.NAMES, p[5:9]) if v == "Active"})
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows), "power_w_max": max(pw) if pw else None}
+                "samples": len(rows), "scope": scope,
+                "power_w_max": max(pw) if pw else None}
 
 
 # --------------------------------------------------------------------------- CPU port
@@ -255,6 +285,10 @@ def main():
         if world > 1:
             dist.barrier(device_ids=[local_rank])
 
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    smi_index = vis.split(",")[local_rank] if vis else str(local_rank)
+    sampler = ClockSampler(smi_index)
+    sampler.start()
     for _ in range(a.warmup):
         layer(x, logits)
     torch.cuda.synchronize()
@@ -263,17 +297,10 @@ def main():
     # ---- device-timed region: inputs resident in HBM
     events = [{n: torch.cuda.Event(enable_timing=True) for n in stage_names}
               for _ in range(a.steps)]
-    bus = None
-    try:
-        bus = torch.cuda.get_device_properties(dev).pci_bus_id
-    except Exception:
-        bus = str(local_rank)
-    sampler = ClockSampler(bus)
     barrier()
     torch.cuda.synchronize()
-    sampler.start()
-    time.sleep(0.3)
     launches0 = _lib.launch_count
+    wall0 = time.time()
     t_start = torch.cuda.Event(enable_timing=True)
     t_end = torch.cuda.Event(enable_timing=True)
     t_start.record()
@@ -282,9 +309,9 @@ def main():
         layer(x, logits)
     t_end.record()
     torch.cuda.synchronize()
+    sampler.mark(wall0, time.time())
     barrier()
     launches = _lib.launch_count - launches0
-    clocks = sampler.stop()
     layer.events = None
     ms_total = t_start.elapsed_time(t_end)
     stage_ms = {}
@@ -335,6 +362,7 @@ def main():
                "h2d_bytes_per_step": x.numel() * 2 + logits.numel() * 4,
                "d2h_bytes_per_step": t * h * 2, "ms_per_step": e2e_ms}
 
+    clocks = sampler.stop()
     peaks, peak_kind = load_peaks()
     fc1_flops = 2.0 * fc1_rows * (2 * f) * h
     fc2_flops = 2.0 * fc1_rows * h * f
