@@ -425,3 +425,96 @@ extern "C" int moe_row_id_map(const uint8_t* routing_map, int64_t T, int64_t E, 
   }
   return MOE_OK;
 }
+
+// ---------------------------------------------------------------------------
+// row_id_map without a caller-provided workspace.
+//
+// Some callers cannot allocate device memory at the point where they build
+// the routing maps: for example a serving runtime that hands each request a
+// fixed, pre-partitioned slice of HBM and forbids further cudaMalloc, or a
+// latency-critical loop where cudaMalloc's implicit synchronisation is not
+// acceptable. For them the scratch lives in a file-scope device array of
+// kRimStaticScratchBytes (1 MiB): it is part of this library's device image,
+// so every GPU that loads the library holds it until the process exits.
+//
+// Host code cannot pass the array's name to a kernel (on the host it is only
+// a stand-in symbol, not a device address), so the first call on each device
+// looks up the real address with cudaGetSymbolAddress, with that device
+// current, and caches it. That first call should therefore happen before any
+// stream capture.
+//
+// All calls on a device share the one array and it keeps whatever the last
+// call left there. Nothing in it needs to start at zero: the count kernel
+// writes every count slot and the scan writes every offset before anything
+// reads them. Calls whose kernels overlap on the GPU (different streams, or
+// different host threads without ordering) race on the array; serialise them.
+// ---------------------------------------------------------------------------
+#include <mutex>
+#include <vector>
+
+namespace {
+constexpr size_t kRimStaticScratchBytes = size_t(1) << 20;
+static __device__ __align__(256) unsigned char g_rim_static_scratch[kRimStaticScratchBytes];
+
+std::mutex g_rim_static_mu;
+std::vector<void*> g_rim_static_addr;  // per device, filled on first use
+
+int rim_static_scratch_address(void** out) {
+  int dev = 0;
+  MOE_CUDA_CALL(cudaGetDevice(&dev), "row_id_map_static_scratch: cudaGetDevice");
+  std::lock_guard<std::mutex> lock(g_rim_static_mu);
+  if (static_cast<size_t>(dev) >= g_rim_static_addr.size())
+    g_rim_static_addr.resize(static_cast<size_t>(dev) + 1, nullptr);
+  if (g_rim_static_addr[dev] == nullptr) {
+    void* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(&p, g_rim_static_scratch);
+    if (e != cudaSuccess || p == nullptr) {
+      moe::set_last_error("row_id_map_static_scratch: cudaGetSymbolAddress failed on device %d: %s",
+                          dev, cudaGetErrorString(e));
+      return MOE_ERR_CUDA;
+    }
+    g_rim_static_addr[dev] = p;
+  }
+  *out = g_rim_static_addr[dev];
+  return MOE_OK;
+}
+}  // namespace
+
+extern "C" int moe_row_id_map_static_scratch(const uint8_t* routing_map, int64_t T, int64_t E,
+                                             int64_t align, int64_t* row_id_map_et,
+                                             int64_t* row_id_map_te, int32_t* expert_counts,
+                                             int64_t* num_out, moe_stream_t stream) {
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  MOE_REQUIRE(T >= 0 && E >= 1 && E <= 65536, "row_id_map_static_scratch: bad shape T=%lld E=%lld",
+              (long long)T, (long long)E);
+  MOE_REQUIRE(align >= 1 && align <= 4096,
+              "row_id_map_static_scratch: align=%lld out of [1,4096]", (long long)align);
+  MOE_REQUIRE(T * E < (int64_t)0x7fffffff,
+              "row_id_map_static_scratch: T*E=%lld must stay below 2^31", (long long)(T * E));
+  const size_t need = rim_ws_bytes(T, E);
+  MOE_REQUIRE(need <= kRimStaticScratchBytes,
+              "row_id_map_static_scratch: T=%lld E=%lld needs %zu bytes of scratch, more than the "
+              "%zu-byte static array; use moe_row_id_map with a workspace",
+              (long long)T, (long long)E, need, kRimStaticScratchBytes);
+  MOE_REQUIRE(T == 0 || routing_map != nullptr, "row_id_map_static_scratch: null routing_map");
+  void* scratch = nullptr;
+  int st = rim_static_scratch_address(&scratch);
+  if (st) return st;
+  const int C = static_cast<int>((T + kRimChunk - 1) / kRimChunk);
+  int32_t* counts = static_cast<int32_t*>(scratch);
+  const size_t counts_bytes = (static_cast<size_t>(E) * C * 4 + 255) & ~static_cast<size_t>(255);
+  int64_t* offs = reinterpret_cast<int64_t*>(static_cast<char*>(scratch) + counts_bytes);
+  const int eblocks = static_cast<int>((E + kRimThreads - 1) / kRimThreads);
+  if (C > 0) {
+    rim_count_kernel<<<dim3(C, eblocks), kRimThreads, 0, s>>>(routing_map, T, (int)E, C, counts);
+    MOE_CUDA_CHECK_LAUNCH("row_id_map_static_scratch count");
+  }
+  rim_scan_kernel<<<1, 1024, 0, s>>>(counts, (int)E, C, align, offs, expert_counts, num_out);
+  MOE_CUDA_CHECK_LAUNCH("row_id_map_static_scratch scan");
+  if (C > 0 && (row_id_map_et != nullptr || row_id_map_te != nullptr)) {
+    rim_fill_kernel<<<dim3(C, eblocks), kRimThreads, 0, s>>>(routing_map, T, (int)E, C, counts,
+                                                             row_id_map_et, row_id_map_te);
+    MOE_CUDA_CHECK_LAUNCH("row_id_map_static_scratch fill");
+  }
+  return MOE_OK;
+}

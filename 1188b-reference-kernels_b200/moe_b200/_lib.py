@@ -44,6 +44,8 @@ _SIGNATURES = {
     "moe_row_id_map_workspace_size": [c_int64, c_int64, POINTER(c_size_t)],
     "moe_row_id_map": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                        c_void_p, c_void_p, c_size_t, c_void_p],
+    "moe_row_id_map_static_scratch": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p,
+                                      c_void_p, c_void_p, c_void_p],
     "moe_permute_mask_map": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int64,
                              c_int64, c_int64, c_void_p],
     "moe_permute_mask_map_trans": [c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_void_p,
@@ -64,6 +66,7 @@ EXPORTED = tuple(_SIGNATURES)
 
 # Kernels each successful call launches (for the bench's launch count).
 _LAUNCHES = {"moe_topk_f32": 1, "moe_router_topk": 1, "moe_row_id_map": 3,
+             "moe_row_id_map_static_scratch": 3,
              "moe_permute_mask_map": 1, "moe_permute_mask_map_trans": 1, "moe_unpermute_mask": 1,
              "moe_grouped_gemm_plan_splits": 1, "moe_grouped_gemm_plan_ep": 1,
              "moe_grouped_gemm": 1, "moe_swiglu": 1}

@@ -83,6 +83,18 @@ int moe_row_id_map(const uint8_t* routing_map, int64_t T, int64_t E, int64_t ali
                    int64_t* num_out, void* workspace, size_t workspace_bytes,
                    moe_stream_t stream);
 
+/* Same maps as moe_row_id_map, for callers that may not allocate device     */
+/* memory (a runtime that owns a fixed HBM budget, or a path where          */
+/* cudaMalloc's implicit synchronisation is not allowed). No counterpart in  */
+/* the reference. Its scratch is a 1 MiB file-scope device array held by     */
+/* every GPU that loads the library; sizes needing more are rejected with    */
+/* MOE_ERR_INVALID (at E=256 that is T > about 63000 tokens). The first call */
+/* on a device looks the array's address up (do it before any stream         */
+/* capture). Calls share the array: calls that overlap on the GPU race.      */
+int moe_row_id_map_static_scratch(const uint8_t* routing_map, int64_t T, int64_t E,
+                                  int64_t align, int64_t* row_id_map_et, int64_t* row_id_map_te,
+                                  int32_t* expert_counts, int64_t* num_out, moe_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* a4  Permute with a [T,E] map: out[row[t,e]] = x[t], pp[row[t,e]] =        */
 /* probs[t,e]. Replaces kernel_results/case17_moe_permute_with_mask_map/     */
