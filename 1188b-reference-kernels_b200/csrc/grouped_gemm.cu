@@ -23,9 +23,11 @@
 //
 // Every wait is bounded (2 s); on timeout the kernel records an error word in
 // the workspace, drains its own in-flight copies and MMAs, frees TMEM and
-// returns. No TMA multicast and no cluster launch are used.
+// returns. Every CTA loads only its own tiles.
 #include <cuda.h>
 #include <cudaTypedefs.h>
+
+#include <stdlib.h>
 
 #include <mutex>
 
@@ -76,8 +78,11 @@ struct Tile {
 };
 
 // Maps a linear tile index to (group, m-tile, n-tile). Tile indices handed to
-// one CTA increase monotonically, so the walker only moves forward.
-struct Walker {
+// one CTA (or CTA pair) increase monotonically, so the walker only moves
+// forward. kTileM rows per M-tile; inside a group, super-rows of kRaster
+// M-tiles sweep all N-tiles.
+template <int kTileM, int kRaster>
+struct WalkerT {
   const int32_t* rows;
   int G;
   int n_tiles;
@@ -87,7 +92,7 @@ struct Walker {
 
   __device__ bool locate(long long t, Tile& tile) {
     while (g < G) {
-      if (mt < 0) mt = (max(rows[g], 0) + BM - 1) / BM;
+      if (mt < 0) mt = (max(rows[g], 0) + kTileM - 1) / kTileM;
       const long long cnt = static_cast<long long>(mt) * n_tiles;
       if (t < base + cnt) break;
       base += cnt;
@@ -96,16 +101,17 @@ struct Walker {
     }
     if (g >= G) return false;
     const long long local = t - base;
-    const long long sr_tiles = static_cast<long long>(kSuperRow) * n_tiles;
+    const long long sr_tiles = static_cast<long long>(kRaster) * n_tiles;
     const int sr = static_cast<int>(local / sr_tiles);
     const int within = static_cast<int>(local - sr * sr_tiles);
-    const int mg = min(kSuperRow, mt - sr * kSuperRow);
+    const int mg = min(kRaster, mt - sr * kRaster);
     tile.g = g;
     tile.n_idx = within / mg;
-    tile.m_idx = sr * kSuperRow + within % mg;
+    tile.m_idx = sr * kRaster + within % mg;
     return true;
   }
 };
+using Walker = WalkerT<BM, kSuperRow>;
 
 MOE_DEVICE bool wait_drain(uint32_t bar, uint32_t parity) {
   const unsigned long long t0 = globaltimer_ns();
@@ -366,6 +372,285 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// CTA-pair variant (tcgen05 cta_group::2), launched as clusters of 2 CTAs.
+//
+// A pair owns a 256-row x 256-column output tile. Each CTA stages only its own
+// 128 A rows and its half of the B rows (128 of 256) per k-block, 32 KB a
+// stage instead of 48 KB, so per SM the L2->shared traffic and the shared
+// memory operand reads are a third lower than the single-CTA kernel's. The
+// leader CTA (rank 0) issues M=256, N=256 MMAs that read both CTAs' shared
+// memory and write both CTAs' TMEM; its commits arrive on the barrier at the
+// same offset in both CTAs. Both CTAs' TMA loads count their bytes on the
+// leader's full barrier; both CTAs' epilogue warps arrive on the leader's
+// accumulator-empty barrier. All waits are bounded as in the 1-CTA kernel,
+// and a cluster barrier precedes the pair TMEM release.
+// ---------------------------------------------------------------------------
+namespace pairk {
+constexpr int kPairTileM = 256;
+constexpr int kPairStages = 6;
+constexpr int kPairRaster = 8;                            // pair M-tiles per super-row
+constexpr uint32_t kPairABytes = 128 * BK * 2;            // 16 KB: this CTA's rows
+constexpr uint32_t kPairBBytes = 128 * BK * 2;            // 16 KB: this CTA's half of B
+constexpr uint32_t kPairStageBytes = kPairABytes + kPairBBytes;   // 32 KB
+constexpr uint32_t kPairTxBytes = 2 * kPairStageBytes;    // both CTAs, on the leader's barrier
+constexpr size_t kPairSmemBytes = 1024 + kPairStages * kPairStageBytes + 256;
+}  // namespace pairk
+
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
+                             const __grid_constant__ CUtensorMap tmap_b, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw_addr);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base_ptr + pairk::kPairStages * pairk::kPairStageBytes);
+  const uint32_t bar0 = smem_u32(bars);
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (pairk::kPairStages + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * pairk::kPairStages + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * pairk::kPairStages + 2 + a); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * pairk::kPairStages + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * pairk::kPairStages + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const long long cid = cluster_id_x();
+  const long long ncl = num_clusters_x();
+  const int warp = warp_id();
+  const int lane = lane_id();
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < pairk::kPairStages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 8);  // 4 epilogue warps in each of the 2 CTAs
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_desc(&tmap_a);
+    tma_prefetch_desc(&tmap_b);
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  WalkerT<pairk::kPairTileM, pairk::kPairRaster> walker{p.rows, p.G, p.n_tiles};
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol_a = l2_policy_evict_normal();
+      const uint64_t pol_b = l2_policy_evict_normal();
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued[pairk::kPairStages];
+#pragma unroll
+      for (int s = 0; s < pairk::kPairStages; ++s) issued[s] = -1;
+      bool ok = true;
+      for (long long t = cid; ok; t += ncl) {
+        Tile tile;
+        if (!walker.locate(t, tile)) break;
+        const int row0 = p.row_start[tile.g] + tile.m_idx * pairk::kPairTileM + static_cast<int>(rank) * 128;
+        const int wbase = p.widx[tile.g] * p.n_w;
+        const int b0 = (p.epilogue == 1)
+                           ? wbase + tile.n_idx * 128 + static_cast<int>(rank) * p.f_half
+                           : wbase + tile.n_idx * BN + static_cast<int>(rank) * 128;
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = base + stage * pairk::kPairStageBytes;
+          const uint32_t sb = sa + pairk::kPairABytes;
+          const uint32_t leader_full = map_to_rank(full_bar(stage), 0);
+          if (leader) mbar_arrive_expect_tx(full_bar(stage), pairk::kPairTxBytes);
+          tma_load_2d_pair(sa, &tmap_a, kb * BK, row0, leader_full, pol_a);
+          tma_load_2d_pair(sb, &tmap_b, kb * BK, b0, leader_full, pol_b);
+          issued[stage] = static_cast<int>(phase);
+          if (++stage == pairk::kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (ok) {
+        // The pair's MMA releases every stage with a commit that lands in this
+        // CTA's shared memory; wait for the last ones before exiting.
+        for (int s = 0; s < pairk::kPairStages; ++s)
+          if (issued[s] >= 0) wait_drain(empty_bar(s), static_cast<uint32_t>(issued[s]));
+      } else {
+        raise_abort(abort_flag, p.err, kErrTimeoutProducer);
+        if (leader) {
+          for (int s = 0; s < pairk::kPairStages; ++s)
+            if (issued[s] >= 0) wait_drain(full_bar(s), static_cast<uint32_t>(issued[s]));
+        } else {
+          // Copies count on the leader's barrier; give them a bounded time to land.
+          const unsigned long long t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 200000ull) {
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader)
+    if (leader && lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16_f32(pairk::kPairTileM, BN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (long long t = cid; ok; t += ncl) {
+        Tile tile;
+        if (!walker.locate(t, tile)) break;
+        const int acc = it & 1;
+        const uint32_t aph = static_cast<uint32_t>((it >> 1) & 1);
+        if (!mbar_wait_cluster(tempty_bar(acc), aph ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        for (int kb = 0; kb < p.num_kb; ++kb) {
+          if (!mbar_wait_cluster(full_bar(stage), phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = base + stage * pairk::kPairStageBytes;
+          const uint32_t sb = sa + pairk::kPairABytes;
+          const uint64_t ad = umma_desc_k_sw128(sa);
+          const uint64_t bd = umma_desc_k_sw128(sb);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_bf16_pair(d_tmem, ad + 2ull * k, bd + 2ull * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          issued_any = true;
+          umma_commit_pair(empty_bar(stage), 0x3);
+          if (++stage == pairk::kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(tfull_bar(acc), 0x3);
+        ++it;
+      }
+      if (!ok) {
+        raise_abort(abort_flag, p.err, kErrTimeoutMma);
+        if (issued_any) {
+          umma_commit_pair(drain_bar, 0x1);
+          wait_drain(drain_bar, 0);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quad = warp & 3;  // TMEM lanes this warp may access: 32*quad ..
+    const int r_in_cta = quad * 32 + lane;
+    const uint32_t leader_tempty0 = map_to_rank(tempty_bar(0), 0);
+    const uint32_t leader_tempty1 = map_to_rank(tempty_bar(1), 0);
+    int it = 0;
+    bool ok = true;
+    for (long long t = cid;; t += ncl) {
+      Tile tile;
+      if (!walker.locate(t, tile)) break;
+      const int acc = it & 1;
+      const uint32_t aph = static_cast<uint32_t>((it >> 1) & 1);
+      if (!mbar_wait_cluster(tfull_bar(acc), aph, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int m_local = tile.m_idx * pairk::kPairTileM + static_cast<int>(rank) * 128 + r_in_cta;
+      const int64_t row = static_cast<int64_t>(p.row_start[tile.g]) + m_local;
+      const bool rvalid = m_local < p.rows[tile.g] && row < p.x_rows;
+      const uint32_t tbase =
+          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      __nv_bfloat16* orow = p.out + row * p.n_out;
+      if (p.epilogue == 0) {
+        const int n0 = tile.n_idx * BN;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, r);
+          tmem_ld_wait();
+          if (rvalid) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const int col = n0 + c * 32 + v * 8;
+              if (col + 8 <= p.n_out) {
+                uint4 o;
+                o.x = pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
+                o.y = pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
+                o.z = pack_bf16x2(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
+                o.w = pack_bf16x2(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
+                *reinterpret_cast<uint4*>(orow + col) = o;
+              }
+            }
+          }
+        }
+      } else {
+        const int n0 = tile.n_idx * 128;
+#pragma unroll 1
+        for (int c = 0; c < 128 / 32; ++c) {
+          uint32_t gr[32], ur[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, gr);
+          tmem_ld_32x32b_x32(tbase + 128 + c * 32, ur);
+          tmem_ld_wait();
+          if (rvalid) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) {
+              const int col = n0 + c * 32 + v * 8;
+              if (col + 8 <= p.n_out) {
+                uint32_t o[4];
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                  const int j = v * 8 + 2 * q;
+                  const float h0 = swiglu_f32(round_bf16(__uint_as_float(gr[j])),
+                                              round_bf16(__uint_as_float(ur[j])));
+                  const float h1 = swiglu_f32(round_bf16(__uint_as_float(gr[j + 1])),
+                                              round_bf16(__uint_as_float(ur[j + 1])));
+                  o[q] = pack_bf16x2(h0, h1);
+                }
+                *reinterpret_cast<uint4*>(orow + col) = make_uint4(o[0], o[1], o[2], o[3]);
+              }
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc == 0 ? leader_tempty0 : leader_tempty1);
+      ++it;
+    }
+    if (!ok && lane == 0) raise_abort(abort_flag, p.err, kErrTimeoutEpilogue);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its partner may still touch its memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // Group-table construction (single block).
 // mode 0: contiguous groups from splits, group g starts at the padded prefix.
 // mode 1: expert-parallel receive layout, see moe_grouped_gemm_plan_ep.
@@ -490,6 +775,46 @@ int make_tmap(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer) {
     return MOE_ERR_CUDA;
   }
   return MOE_OK;
+}
+
+// Clusters of 2 that can be resident at once (0 if the pair kernel cannot run).
+int pair_clusters(int dev) {
+  static std::mutex mu;
+  static int cache[64];
+  static bool init[64] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= 0 && dev < 64 && init[dev]) return cache[dev];
+  int n = 0;
+  if (cudaFuncSetAttribute(grouped_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(pairk::kPairSmemBytes)) == cudaSuccess) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * 74);
+    cfg.blockDim = dim3(kThreads);
+    cfg.dynamicSmemBytes = pairk::kPairSmemBytes;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    if (cudaOccupancyMaxActiveClusters(&n, grouped_gemm_pair_kernel, &cfg) != cudaSuccess) n = 0;
+  }
+  cudaGetLastError();  // clear a non-sticky error from an unsupported query
+  if (dev >= 0 && dev < 64) {
+    cache[dev] = n;
+    init[dev] = true;
+  }
+  return n;
+}
+
+bool pair_enabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("MOE_GEMM_PAIR");
+    v = (e != nullptr && e[0] == '0') ? 0 : 1;
+  }
+  return v == 1;
 }
 
 int ensure_smem_attr() {
@@ -617,6 +942,24 @@ extern "C" int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t
 
   int dev = 0;
   MOE_CUDA_CALL(cudaGetDevice(&dev), "cudaGetDevice");
+  const int clusters = gg::pair_enabled() ? gg::pair_clusters(dev) : 0;
+  if (clusters > 0) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2 * clusters);
+    cfg.blockDim = dim3(gg::kThreads);
+    cfg.dynamicSmemBytes = gg::pairk::kPairSmemBytes;
+    cfg.stream = reinterpret_cast<cudaStream_t>(stream);
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    MOE_CUDA_CALL(cudaLaunchKernelEx(&cfg, gg::grouped_gemm_pair_kernel, ta, tb, p),
+                  "grouped_gemm pair launch");
+    return MOE_OK;
+  }
   const int grid = num_sms(dev);
   gg::grouped_gemm_kernel<<<grid, gg::kThreads, gg::kSmemBytes,
                             reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, p);

@@ -1,8 +1,8 @@
 // Shared device helpers for the B200 MoE expert-layer kernels (sm_100a only).
 //
 // Everything here is plain CUDA C++ or hand-written PTX for Blackwell:
-// mbarriers with bounded waits, TMA tile loads (no cluster multicast anywhere
-// in this library), tcgen05 (UMMA + TMEM) wrappers, and bf16 helpers.
+// mbarriers with bounded waits, TMA tile loads (each CTA loads only into its
+// own shared memory), tcgen05 (UMMA + TMEM) wrappers, and bf16 helpers.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -122,7 +122,7 @@ MOE_DEVICE void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
 }
 
 // ---------------------------------------------------------------------------
-// TMA (tensor tile copies). Loads only, CTA-local destination, no multicast.
+// TMA (tensor tile copies). Loads only, into this CTA's own shared memory.
 // ---------------------------------------------------------------------------
 MOE_DEVICE void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
@@ -231,6 +231,105 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16_f32(int m, int n) {
          | (1u << 10)                              // B format: bf16
          | (static_cast<uint32_t>(n >> 3) << 17)   // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);  // M / 16
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair (cluster of 2) helpers for the cta_group::2 GEMM.
+// ---------------------------------------------------------------------------
+MOE_DEVICE uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+MOE_DEVICE uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+MOE_DEVICE uint32_t num_clusters_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+// Shared::cluster address of the same shared-memory offset in CTA `rank`.
+MOE_DEVICE uint32_t map_to_rank(uint32_t smem_addr, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_addr), "r"(rank));
+  return r;
+}
+MOE_DEVICE void cluster_sync() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" :::
+                   "memory");
+}
+MOE_DEVICE void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr)
+               : "memory");
+}
+MOE_DEVICE bool mbar_try_wait_cluster(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+// Bounded wait with cluster-scope acquire (for barriers other CTAs arrive on).
+MOE_DEVICE bool mbar_wait_cluster(uint32_t bar, uint32_t parity, volatile int* abort_flag) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer_ns();
+  for (uint32_t it = 1;; ++it) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if ((it & 31u) == 0u) {
+      if (abort_flag != nullptr && *abort_flag) return false;
+      if (globaltimer_ns() - t0 > kWaitTimeoutNs) return false;
+    }
+  }
+}
+// Tile load for the CTA pair: data lands in this CTA's shared memory, the
+// transaction bytes are counted on `bar_cluster`, which may be the leader
+// CTA's barrier. Each CTA of the pair loads its own tiles.
+MOE_DEVICE void tma_load_2d_pair(uint32_t dst, const void* tmap, int32_t x, int32_t y,
+                                 uint32_t bar_cluster, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      ".L2::cache_hint [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar_cluster), "l"(policy)
+      : "memory");
+}
+MOE_DEVICE void tmem_alloc_pair(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+MOE_DEVICE void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+MOE_DEVICE void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+// D[tmem of both CTAs] (+)= A * B^T over the CTA pair (M = 256 split by rows,
+// B split by N halves), issued by one thread of the leader CTA.
+MOE_DEVICE void umma_bf16_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                               uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// tcgen05.commit to both CTAs of the pair: arrives once on the barrier at
+// this offset in every CTA of cta_mask when the pair's issued MMAs complete.
+MOE_DEVICE void umma_commit_pair(uint32_t bar, uint16_t cta_mask) {
+  asm volatile(
+      "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64"
+      " [%0], %1;" ::"r"(bar),
+      "h"(cta_mask)
+      : "memory");
 }
 
 MOE_DEVICE int warp_id() { return static_cast<int>(threadIdx.x >> 5); }

@@ -8,10 +8,10 @@ The reference-style ``kernel_function`` entry points live in ``bundles/``.
 from ._lib import MoeError, load as load_library
 from .ops import (GroupedGemmPlan, RouterOutput, RowIdMap, grouped_gemm, permute, permute_trans,
                   router_topk, row_id_map, swiglu, topk, unpermute)
-from .layer import MoELayer, MoEWeights
+from .layer import HostPipeline, MoELayer, MoEWeights
 
 __all__ = [
     "MoeError", "load_library", "GroupedGemmPlan", "RouterOutput", "RowIdMap", "grouped_gemm",
     "permute", "permute_trans", "router_topk", "row_id_map", "swiglu", "topk", "unpermute",
-    "MoELayer", "MoEWeights",
+    "MoELayer", "MoEWeights", "HostPipeline",
 ]

@@ -101,3 +101,60 @@ class MoELayer:
         return out
 
     __call__ = forward
+
+
+class HostPipeline:
+    """Runs layer steps whose inputs and outputs live in pinned host memory.
+
+    Each submitted step copies its x and logits host->device on an upload
+    stream, runs the layer on the compute stream once its upload has landed,
+    and copies the output device->host on a download stream. Uploads of the
+    next step and the download of the previous one overlap the current step's
+    kernels (the copy engines are independent of the SMs), so a stream of
+    steps runs at the pace of the slowest of the three. `depth` device buffer
+    slots are cycled; a slot is reused only after the step that read it.
+    """
+
+    def __init__(self, layer, tokens: int, hidden: int, num_experts: int, device,
+                 depth: int = 2):
+        self.layer = layer
+        self.depth = depth
+        self.dev = torch.device(device)
+        self.x = [torch.empty((tokens, hidden), dtype=torch.bfloat16, device=self.dev)
+                  for _ in range(depth)]
+        self.lg = [torch.empty((tokens, num_experts), dtype=torch.float32, device=self.dev)
+                   for _ in range(depth)]
+        self.up = torch.cuda.Stream(self.dev)
+        self.down = torch.cuda.Stream(self.dev)
+        self.compute = torch.cuda.current_stream(self.dev)
+        self.uploaded = [torch.cuda.Event() for _ in range(depth)]
+        self.consumed = [torch.cuda.Event() for _ in range(depth)]
+        self.done = [torch.cuda.Event() for _ in range(depth)]
+        self._used = [False] * depth
+        self._n = 0
+
+    def submit(self, x_host: torch.Tensor, logits_host: torch.Tensor,
+               out_host: torch.Tensor) -> torch.cuda.Event:
+        """Enqueues one step; returns the event that marks its output on the host."""
+        s = self._n % self.depth
+        self._n += 1
+        with torch.cuda.stream(self.up):
+            if self._used[s]:
+                self.up.wait_event(self.consumed[s])
+            self.x[s].copy_(x_host, non_blocking=True)
+            self.lg[s].copy_(logits_host, non_blocking=True)
+            self.uploaded[s].record(self.up)
+        self._used[s] = True
+        with torch.cuda.stream(self.compute):
+            self.compute.wait_event(self.uploaded[s])
+            out = self.layer(self.x[s], self.lg[s])
+            self.consumed[s].record(self.compute)
+        with torch.cuda.stream(self.down):
+            self.down.wait_event(self.consumed[s])
+            out_host.copy_(out, non_blocking=True)
+            out.record_stream(self.down)
+            self.done[s].record(self.down)
+        return self.done[s]
+
+    def synchronize(self) -> None:
+        self.down.synchronize()

@@ -33,7 +33,7 @@ typedef struct CUstream_st* moe_stream_t; /* == cudaStream_t */
 typedef enum {
   MOE_OK = 0,
   MOE_ERR_INVALID = 1,     /* bad argument: null pointer, size, alignment, dtype code */
-  MOE_ERR_UNSUPPORTED = 2, /* valid but outside what this build supports (e.g. k > 32) */
+  MOE_ERR_UNSUPPORTED = 2, /* valid but outside what this build supports (e.g. k > 16) */
   MOE_ERR_CUDA = 3,        /* a CUDA runtime/driver call or launch failed */
   MOE_ERR_DEVICE = 4       /* a kernel reported an error word (see moe_grouped_gemm) */
 } moe_status;
@@ -48,7 +48,8 @@ int moe_b200_abi_version(void);
 /* Replaces kernel_results/case23_aten_topk/binding.cpp:4 (launch_topk) and  */
 /* matches kernel_cases/case23_ref_aten_topk.py:47-62 (reference_topk).      */
 /* input [M,N] fp32 row-major; values [M,k] fp32; indices [M,k] int64.       */
-/* 1 <= k <= min(N, 32); N <= 4096.                                          */
+/* 1 <= k <= min(N, 16) and N <= 2048, else MOE_ERR_UNSUPPORTED. NaN ranks   */
+/* first, as in torch.sort / torch.topk.                                     */
 int moe_topk_f32(const float* input, float* values, int64_t* indices, int64_t M, int64_t N,
                  int32_t k, moe_stream_t stream);
 
@@ -100,9 +101,10 @@ int moe_row_id_map_static_scratch(const uint8_t* routing_map, int64_t T, int64_t
 /* probs[t,e]. Replaces kernel_results/case17_moe_permute_with_mask_map/     */
 /* binding.cpp:5-6 (permute_rt_launcher); semantics of kernel_cases/case17_  */
 /* moe_permute_with_mask_map.py:58-71. x/out bf16 (any 2-byte type: pure     */
-/* copy), H % 8 == 0, pointers 16-byte aligned. probs / permuted_probs       */
-/* nullable together. Rows of out no map entry points at are left untouched. */
-/* Map entries must lie in [-1, num_out).                                    */
+/* copy), any H; rows move as 16-, 4- or 2-byte vectors depending on H and   */
+/* pointer alignment. probs / permuted_probs nullable together. Rows of out  */
+/* no map entry points at are left untouched; entries outside [0, num_out)   */
+/* are skipped.                                                              */
 int moe_permute_mask_map(const void* x, const int64_t* row_id_map_te, const float* probs,
                          void* out, float* permuted_probs, int64_t T, int64_t H, int64_t E,
                          int64_t num_out, moe_stream_t stream);
@@ -125,6 +127,7 @@ int moe_permute_mask_map_trans(const void* x, const void* row_id_map_et, int32_t
 /* w = probs[t,e] ([T,E] fp32, probs_mode 0) or w = probs[row[e,t]]          */
 /* (permuted [num_rows] fp32, probs_mode 1). Products and sums are separate  */
 /* fp32 roundings (no FMA), accumulated in ascending expert order.           */
+/* Any H up to 16384 (16-byte rows), 4096 (4-byte) or 2048 (2-byte).         */
 int moe_unpermute_mask(const void* pin, const void* row_id_map_et, int32_t idx_bits,
                        const float* probs, int32_t probs_mode, void* out, float* acc_out,
                        int64_t T, int64_t H, int64_t E, int64_t num_rows, moe_stream_t stream);

@@ -1,0 +1,96 @@
+"""Expert-parallel layer on 2 (or 4) GPUs over NCCL, against the single-GPU layer.
+
+Each output element is accumulated in the same K order by the same kernel on
+either path, and the combine adds experts in ascending order on both, so the
+EP result must equal the single-GPU result bit for bit. Needs >= 2 GPUs;
+skipped on single-GPU hosts.
+"""
+import os
+import socket
+import sys
+import traceback
+from datetime import timedelta
+
+import pytest
+import torch
+
+from conftest import GOLDEN, PKG, ROOT
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _problem(world, t, h, e, f, routing):
+    g = torch.Generator().manual_seed(11 + world)
+    x = torch.randn(world * t, h, generator=g).to(torch.bfloat16)
+    lg = torch.randn(world * t, e, generator=g)
+    bias = torch.zeros(e)
+    if routing == "zipf":
+        bias = -1.5 * torch.log(torch.randperm(e, generator=g).float() + 1)
+    w1 = (torch.randn(e, 2 * f, h, generator=g) * 0.03).to(torch.bfloat16)
+    w2 = (torch.randn(e, h, f, generator=g) * 0.03).to(torch.bfloat16)
+    return x, lg, bias, w1, w2
+
+
+def _worker(rank, world, port, routing, q):
+    for p in (str(PKG), str(ROOT), str(GOLDEN)):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    try:
+        import torch.distributed as dist
+        import moe_b200
+        from moe_b200.ep import MoELayerEP
+        dev = torch.device("cuda", rank)
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=timedelta(seconds=60), device_id=dev)
+        t, h, e, f, k = 256, 1024, 16, 256, 4
+        x, lg, bias, w1, w2 = _problem(world, t, h, e, f, routing)
+        el = e // world
+        sl = slice(rank * t, (rank + 1) * t)
+        local = moe_b200.MoEWeights(w1[rank * el:(rank + 1) * el].to(dev).contiguous(),
+                                    w2[rank * el:(rank + 1) * el].to(dev).contiguous())
+        layer = MoELayerEP(local, e, topk=k, expert_bias=bias.to(dev))
+        out = layer(x[sl].to(dev), lg[sl].to(dev))
+        outs = [torch.empty_like(out) for _ in range(world)]
+        dist.all_gather(outs, out)
+        err = layer.plan.device_error()
+        ok = None
+        if rank == 0:
+            full = moe_b200.MoELayer(moe_b200.MoEWeights(w1.to(dev), w2.to(dev)), topk=k,
+                                     expert_bias=bias.to(dev))
+            ref = full(x.to(dev), lg.to(dev))
+            ok = bool(torch.equal(torch.cat(outs), ref))
+        dist.barrier(device_ids=[rank])
+        dist.destroy_process_group()
+        q.put((rank, ok, err))
+    except Exception as exc:
+        q.put((rank, "error", f"{type(exc).__name__}: {exc}", traceback.format_exc()[-1500:]))
+
+
+@pytest.mark.parametrize("world,routing", [(2, "uniform"), (2, "zipf"), (4, "zipf")])
+def test_ep_equals_single_gpu(world, routing):
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test selected but no CUDA device is visible")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, routing, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted((q.get(timeout=300) for _ in range(world)), key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=120)
+    for r in res:
+        assert r[1] != "error", r
+        assert r[2] == 0, r
+    assert res[0][1] is True

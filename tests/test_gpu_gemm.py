@@ -204,3 +204,33 @@ def test_bad_arguments(cuda_dev):
         moe_b200.grouped_gemm(x, w, [8])
     with pytest.raises(ValueError):
         moe_b200.grouped_gemm(x.float(), w, [8])
+
+
+def test_single_cta_kernel_variant(cuda_dev):
+    """The single-CTA kernel (used when CTA pairs cannot be scheduled, or with
+    MOE_GEMM_PAIR=0) on ragged, SwiGLU and EP-style groups, in a fresh process."""
+    import os
+    import subprocess
+    import sys
+    from conftest import ROOT
+    code = r'''
+import sys, numpy as np, torch
+sys.path[:0] = [sys.argv[1], sys.argv[2], sys.argv[3]]
+import moe_b200
+from test_gpu_gemm import fp32_ref, assert_gemm_close, _rand_bf16
+from conftest import u16
+dev = torch.device("cuda", 0)
+g = torch.Generator().manual_seed(1)
+splits = [0, 1, 127, 128, 129, 300, 0, 5]
+x = _rand_bf16(g, sum(splits), 256); w = _rand_bf16(g, 8, 512, 256, std=0.05)
+y = moe_b200.grouped_gemm(x.to(dev), w.to(dev), splits)
+assert_gemm_close(y, fp32_ref(u16(x), u16(w), splits), "1cta plain")
+h = moe_b200.grouped_gemm(x.to(dev), w.to(dev), splits, epilogue="swiglu")
+assert_gemm_close(h, fp32_ref(u16(x), u16(w), splits, swiglu=True), "1cta swiglu", ulp_frac=0.995)
+print("OK")
+'''
+    env = dict(os.environ, MOE_GEMM_PAIR="0")
+    r = subprocess.run([sys.executable, "-c", code, str(ROOT / "1188b-reference-kernels_b200"),
+                        str(ROOT), str(ROOT / "tests")], env=env, capture_output=True, text=True,
+                       timeout=300)
+    assert r.returncode == 0 and "OK" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]

@@ -43,3 +43,23 @@ def test_layer_vs_oracle(cuda_dev, t, h, e, f, k, zipf):
                         None if bias is None else bias.numpy(), tokens=tokens)
     got = orc.bf16_to_f32(u16(out)[tokens])
     np.testing.assert_allclose(got, orc.bf16_to_f32(ref), rtol=2e-2, atol=1e-2)
+
+
+def test_host_pipeline_matches_direct_calls(cuda_dev):
+    """Overlapped host->device->host steps give the same outputs as direct calls."""
+    import moe_b200
+    t, h, e, f, k = 384, 512, 16, 256, 4
+    g = torch.Generator().manual_seed(9)
+    w1 = (torch.randn(e, 2 * f, h, generator=g) * 0.03).to(torch.bfloat16).to(cuda_dev)
+    w2 = (torch.randn(e, h, f, generator=g) * 0.03).to(torch.bfloat16).to(cuda_dev)
+    layer = moe_b200.MoELayer(moe_b200.MoEWeights(w1, w2), topk=k)
+    xs = [torch.randn(t, h, generator=g).to(torch.bfloat16).pin_memory() for _ in range(5)]
+    lgs = [torch.randn(t, e, generator=g).pin_memory() for _ in range(5)]
+    outs = [torch.empty(t, h, dtype=torch.bfloat16).pin_memory() for _ in range(5)]
+    pipe = moe_b200.HostPipeline(layer, t, h, e, cuda_dev, depth=2)
+    for i in range(5):
+        pipe.submit(xs[i], lgs[i], outs[i])
+    pipe.synchronize()
+    for i in range(5):
+        ref = layer(xs[i].to(cuda_dev), lgs[i].to(cuda_dev)).cpu()
+        assert torch.equal(outs[i], ref), i
