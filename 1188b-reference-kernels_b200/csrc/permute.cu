@@ -232,6 +232,78 @@ __global__ void __launch_bounds__(kRowThreads) unpermute_kernel(
   }
 }
 
+// Combine with the whole source list staged first (up to kCombineMaxE map
+// entries per token), then one pass over the row's column vectors that keeps
+// up to 8 source rows in flight per thread. Same arithmetic and the same
+// ascending-expert order as unpermute_kernel, so the results are identical;
+// it only hides memory latency better (few registers, many loads in flight).
+// kTrans: map is [E,T] (reference layout); otherwise token-major [T,E].
+constexpr int kCombineMaxE = 1024;
+
+template <bool kTrans, typename IdxT, typename V>
+__global__ void __launch_bounds__(kRowThreads) combine_kernel(
+    const V* __restrict__ pin, const IdxT* __restrict__ map, const float* __restrict__ probs,
+    int probs_mode, V* __restrict__ out, float* __restrict__ acc_out, int64_t T, int E,
+    int nvec, int64_t num_rows) {
+  constexpr int kE = VecTraits<V>::kElems;
+  __shared__ int64_t s_src[kCombineMaxE];
+  __shared__ float s_w[kCombineMaxE];
+  __shared__ int s_wcnt[kRowWarps];
+  __shared__ int s_n;
+  const int64_t t = blockIdx.x;
+  const int tid = threadIdx.x;
+  const bool weighted = probs_mode >= 0;
+  if (tid == 0) s_n = 0;
+  for (int e0 = 0; e0 < E; e0 += kRowThreads) {
+    const int e = e0 + tid;
+    int64_t s = -1;
+    if (e < E) s = load_map<IdxT, kTrans>(map, T, E, t, e);
+    const bool valid = s >= 0 && s < num_rows;
+    int pos;
+    const int total = compact_window(valid, s_wcnt, pos);  // contains a __syncthreads
+    const int base = s_n;
+    if (valid) {
+      s_src[base + pos] = s;
+      float w = 1.f;
+      if (probs_mode == 0) w = __ldg(probs + t * E + e);
+      else if (probs_mode == 1) w = __ldg(probs + s);
+      s_w[base + pos] = w;
+    }
+    __syncthreads();
+    if (tid == 0) s_n = base + total;
+  }
+  __syncthreads();
+  const int n = s_n;
+  for (int i = tid; i < nvec; i += kRowThreads) {
+    float acc[kE];
+#pragma unroll
+    for (int q = 0; q < kE; ++q) acc[q] = 0.f;
+    int j = 0;
+    for (; j + 8 <= n; j += 8) {
+      V v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = pin[s_src[j + u] * nvec + i];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) accum_vec<V>(acc, v[u], s_w[j + u], weighted);
+    }
+    if (j + 4 <= n) {
+      V v[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) v[u] = pin[s_src[j + u] * nvec + i];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) accum_vec<V>(acc, v[u], s_w[j + u], weighted);
+      j += 4;
+    }
+    for (; j < n; ++j) accum_vec<V>(acc, pin[s_src[j] * nvec + i], s_w[j], weighted);
+    out[t * nvec + i] = VecTraits<V>::pack(acc);
+    if (acc_out) {
+      float* ao = acc_out + (t * nvec + i) * kE;
+#pragma unroll
+      for (int q = 0; q < kE; ++q) ao[q] = acc[q];
+    }
+  }
+}
+
 __global__ void swiglu_kernel(const uint4* __restrict__ y, uint4* __restrict__ h, int64_t M,
                               int fvec) {
   const int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -315,10 +387,42 @@ int launch_permute(const void* x, const IdxT* map, const float* probs, void* out
   }
 }
 
+template <bool kTrans, typename IdxT, typename V>
+int launch_combine_v(const void* pin, const IdxT* map, const float* probs, int probs_mode,
+                     void* out, float* acc_out, int64_t T, int64_t H, int64_t E, int64_t num_rows,
+                     cudaStream_t s) {
+  const int nvec = static_cast<int>(H / VecTraits<V>::kElems);
+  combine_kernel<kTrans, IdxT, V><<<static_cast<unsigned>(T), kRowThreads, 0, s>>>(
+      static_cast<const V*>(pin), map, probs, probs_mode, static_cast<V*>(out), acc_out, T,
+      (int)E, nvec, num_rows);
+  MOE_CUDA_CHECK_LAUNCH("combine launch");
+  return MOE_OK;
+}
+
+template <bool kTrans, typename IdxT>
+int launch_combine(const void* pin, const IdxT* map, const float* probs, int probs_mode,
+                   void* out, float* acc_out, int64_t T, int64_t H, int64_t E, int64_t num_rows,
+                   cudaStream_t s) {
+  switch (vec_bytes(pin, out, H)) {
+    case 16:
+      return launch_combine_v<kTrans, IdxT, uint4>(pin, map, probs, probs_mode, out, acc_out, T,
+                                                   H, E, num_rows, s);
+    case 4:
+      return launch_combine_v<kTrans, IdxT, uint32_t>(pin, map, probs, probs_mode, out, acc_out,
+                                                      T, H, E, num_rows, s);
+    default:
+      return launch_combine_v<kTrans, IdxT, uint16_t>(pin, map, probs, probs_mode, out, acc_out,
+                                                      T, H, E, num_rows, s);
+  }
+}
+
 template <typename IdxT>
 int launch_unpermute(const void* pin, const IdxT* map, const float* probs, int probs_mode,
                      void* out, float* acc_out, int64_t T, int64_t H, int64_t E, int64_t num_rows,
                      cudaStream_t s) {
+  if (E <= kCombineMaxE)
+    return launch_combine<true, IdxT>(pin, map, probs, probs_mode, out, acc_out, T, H, E,
+                                      num_rows, s);
   switch (vec_bytes(pin, out, H)) {
     case 16:
       return launch_unpermute_v<IdxT, uint4>(pin, map, probs, probs_mode, out, acc_out, T, H, E,
@@ -418,4 +522,25 @@ extern "C" int moe_swiglu(const void* y, void* h, int64_t M, int64_t F, moe_stre
                                                             static_cast<uint4*>(h), M, fvec);
   MOE_CUDA_CHECK_LAUNCH("swiglu launch");
   return MOE_OK;
+}
+
+extern "C" int moe_unpermute_mask_token_major(const void* pin, const int64_t* row_id_map_te,
+                                              const float* probs, int32_t probs_mode, void* out,
+                                              float* acc_out, int64_t T, int64_t H, int64_t E,
+                                              int64_t num_rows, moe_stream_t stream) {
+  int st = check_row_args("unpermute_token_major", pin, out, T, H, E);
+  if (st) return st;
+  MOE_REQUIRE(E <= kCombineMaxE, "unpermute_token_major: E=%lld above %d", (long long)E,
+              kCombineMaxE);
+  MOE_REQUIRE(probs == nullptr || probs_mode == 0 || probs_mode == 1,
+              "unpermute_token_major: probs_mode must be 0 ([T,E]) or 1 (permuted)");
+  MOE_REQUIRE(num_rows >= 0, "unpermute_token_major: num_rows=%lld < 0", (long long)num_rows);
+  MOE_REQUIRE(acc_out == nullptr || (reinterpret_cast<uintptr_t>(acc_out) & 3) == 0,
+              "unpermute_token_major: acc_out must be 4-byte aligned");
+  if (T == 0 || H == 0) return MOE_OK;
+  MOE_REQUIRE(out && row_id_map_te && (pin || num_rows == 0),
+              "unpermute_token_major: null pointer");
+  return launch_combine<false, int64_t>(pin, row_id_map_te, probs, probs ? probs_mode : -1, out,
+                                        acc_out, T, H, E, num_rows,
+                                        reinterpret_cast<cudaStream_t>(stream));
 }

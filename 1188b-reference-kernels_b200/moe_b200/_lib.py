@@ -52,6 +52,8 @@ _SIGNATURES = {
                                    c_int64, c_int64, c_int64, c_int64, c_void_p],
     "moe_unpermute_mask": [c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_void_p, c_void_p,
                            c_int64, c_int64, c_int64, c_int64, c_void_p],
+    "moe_unpermute_mask_token_major": [c_void_p, c_void_p, c_void_p, c_int32, c_void_p,
+                                       c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p],
     "moe_grouped_gemm_workspace_size": [c_int64, POINTER(c_size_t)],
     "moe_grouped_gemm_plan_splits": [c_void_p, c_int64, c_int64, c_void_p, c_size_t, c_void_p],
     "moe_grouped_gemm_plan_ep": [c_void_p, c_int64, c_int64, c_void_p, c_size_t, c_void_p],
@@ -59,6 +61,10 @@ _SIGNATURES = {
                          c_int64, c_int32, c_void_p, c_size_t, c_void_p],
     "moe_grouped_gemm_check": [c_void_p, c_size_t, c_void_p, POINTER(c_int32)],
     "moe_swiglu": [c_void_p, c_void_p, c_int64, c_int64, c_void_p],
+    "moe_ipc_get_handle": [c_void_p, c_void_p, POINTER(ctypes.c_uint64)],
+    "moe_ipc_open_handle": [c_void_p, POINTER(c_void_p)],
+    "moe_ipc_close_handle": [c_void_p],
+    "moe_copy_async": [c_void_p, c_void_p, c_size_t, c_void_p],
 }
 _RESTYPE = {"moe_b200_last_error": c_char_p}
 
@@ -68,6 +74,7 @@ EXPORTED = tuple(_SIGNATURES)
 _LAUNCHES = {"moe_topk_f32": 1, "moe_router_topk": 1, "moe_row_id_map": 3,
              "moe_row_id_map_static_scratch": 3,
              "moe_permute_mask_map": 1, "moe_permute_mask_map_trans": 1, "moe_unpermute_mask": 1,
+             "moe_unpermute_mask_token_major": 1,
              "moe_grouped_gemm_plan_splits": 1, "moe_grouped_gemm_plan_ep": 1,
              "moe_grouped_gemm": 1, "moe_swiglu": 1}
 launch_count = 0

@@ -24,10 +24,14 @@ can be tested with gloo on CPU; the layer itself runs only on CUDA.
 """
 from __future__ import annotations
 
-from typing import List, Optional, Tuple
+import ctypes
+from dataclasses import dataclass
+from typing import List, Optional, Sequence, Tuple
 
 import torch
 import torch.distributed as dist
+
+from . import _lib
 
 from . import ops
 from .layer import MoEWeights
@@ -106,6 +110,156 @@ def ep_group_table(recv_counts, num_src: int, num_w: int):
     return starts, rows, widx
 
 
+@dataclass
+class ExchangePlan:
+    """Split sizes and row offsets of one EP exchange, seen from one rank.
+
+    blk[s][d] = rows rank s sends to rank d (its tokens routed to d's experts).
+    """
+    send: List[int]       # rows this rank sends to each d (its xp block for d)
+    recv: List[int]       # rows this rank receives from each s
+    send_off: List[int]   # start of the block for d in this rank's xp
+    recv_off: List[int]   # start of the rows from s in this rank's receive buffer
+    dst_off: List[int]    # where this rank's block starts in d's receive buffer
+    back_off: List[int]   # where the results for s start in s's return buffer
+
+
+def exchange_plan(counts_all: Sequence[Sequence[int]], rank: int, local_experts: int) -> ExchangePlan:
+    """Host computation of every split and offset from the gathered [G, E]
+    per-expert token counts (row s = rank s's counts for all E experts)."""
+    g = len(counts_all)
+    el = local_experts
+    blk = [[int(sum(counts_all[s][d * el:(d + 1) * el])) for d in range(g)] for s in range(g)]
+
+    def prefix(v):
+        out, acc = [], 0
+        for x in v:
+            out.append(acc)
+            acc += x
+        return out
+
+    send = blk[rank]
+    recv = [blk[s][rank] for s in range(g)]
+    dst_off = [sum(blk[s][d] for s in range(rank)) for d in range(g)]
+    back_off = [sum(blk[s][d] for d in range(rank)) for s in range(g)]
+    return ExchangePlan(send, recv, prefix(send), prefix(recv), dst_off, back_off)
+
+
+class EPPeerExchange:
+    """Row exchange through peer-mapped buffers and the copy engines.
+
+    Every rank registers a receive buffer (capacity world*T*k rows) and a
+    return buffer (T*k rows) once, with CUDA IPC. Dispatch: each rank copies
+    its block for rank d straight into d's receive buffer; combine: each rank
+    copies the results for rank s straight into s's return buffer. One copy
+    per peer, on parallel side streams, then a one-element NCCL all-reduce as
+    a stream-ordered barrier so no rank reads a buffer before every copy into
+    it has finished. Buffers are reused across forwards without double
+    buffering: a rank can only start the next dispatch after the previous
+    combine, which needs every peer's GEMMs of the previous step.
+    """
+
+    def __init__(self, num_experts: int, tokens: int, hidden: int, topk: int,
+                 device: torch.device, group: Optional[dist.ProcessGroup] = None):
+        self.group = group
+        self.world = dist.get_world_size(group)
+        self.rank = dist.get_rank(group)
+        if num_experts % self.world:
+            raise ValueError(f"{num_experts} experts do not split evenly over {self.world} ranks")
+        self.num_experts = num_experts
+        self.local_experts = num_experts // self.world
+        self.rows_cap = tokens * topk
+        self.row_bytes = hidden * 2
+        self.device = torch.device(device)
+        self.recv_buf = torch.empty((self.world * self.rows_cap, hidden), dtype=torch.bfloat16,
+                                    device=self.device)
+        self.ret_buf = torch.empty((self.rows_cap, hidden), dtype=torch.bfloat16,
+                                   device=self.device)
+        self.side = [torch.cuda.Stream(self.device) for _ in range(self.world)]
+        self.flag = torch.zeros(1, dtype=torch.float32, device=self.device)
+        self._opened: List[int] = []
+        self.peer_recv = self._share(self.recv_buf)
+        self.peer_ret = self._share(self.ret_buf)
+
+    def _share(self, t: torch.Tensor) -> List[int]:
+        lib = _lib.load()
+        handle = ctypes.create_string_buffer(64)
+        off = ctypes.c_uint64(0)
+        _lib.call("moe_ipc_get_handle", t.data_ptr(), handle, ctypes.byref(off))
+        mine = (bytes(handle.raw), int(off.value))
+        allh = [None] * self.world
+        dist.all_gather_object(allh, mine, group=self.group)
+        ptrs = []
+        for r, (h, o) in enumerate(allh):
+            if r == self.rank:
+                ptrs.append(t.data_ptr())
+                continue
+            base = ctypes.c_void_p(0)
+            _lib.call("moe_ipc_open_handle", ctypes.create_string_buffer(h, 64), ctypes.byref(base))
+            self._opened.append(base.value)
+            ptrs.append(base.value + o)
+        del lib
+        return ptrs
+
+    def exchange_counts(self, counts: torch.Tensor):
+        """All-gathers the per-expert counts; returns (plan, recv_counts [G*E_loc]
+        int32 on the device in (source, local expert) order)."""
+        c = counts.to(torch.int32).contiguous()
+        allc = torch.empty((self.world * self.num_experts,), dtype=torch.int32, device=c.device)
+        dist.all_gather_into_tensor(allc, c, group=self.group)
+        m = allc.view(self.world, self.num_experts)
+        e0 = self.rank * self.local_experts
+        recv_counts = m[:, e0:e0 + self.local_experts].contiguous().view(-1)
+        host = m.cpu().tolist()  # the one host sync of the forward
+        return exchange_plan(host, self.rank, self.local_experts), recv_counts
+
+    def _copies(self, jobs):
+        main = torch.cuda.current_stream(self.device)
+        ready = torch.cuda.Event()
+        ready.record(main)
+        done = []
+        for i, (dst, src, nbytes) in enumerate(jobs):
+            if nbytes == 0:
+                continue
+            st = self.side[i % len(self.side)]
+            st.wait_event(ready)
+            _lib.call("moe_copy_async", dst, src, nbytes, st.cuda_stream)
+            ev = torch.cuda.Event()
+            ev.record(st)
+            done.append(ev)
+        for ev in done:
+            main.wait_event(ev)
+        dist.all_reduce(self.flag, group=self.group)  # every rank's copies have landed
+
+    def dispatch(self, xp: torch.Tensor, plan: ExchangePlan) -> torch.Tensor:
+        if xp.shape[0] != sum(plan.send) or sum(plan.recv) > self.recv_buf.shape[0]:
+            raise ValueError("rows do not match the exchanged counts or exceed the buffer")
+        rb = self.row_bytes
+        base = xp.data_ptr()
+        jobs = [(self.peer_recv[d] + plan.dst_off[d] * rb, base + plan.send_off[d] * rb,
+                 plan.send[d] * rb) for d in range(self.world)]
+        self._copies(jobs)
+        return self.recv_buf[:sum(plan.recv)]
+
+    def combine(self, y: torch.Tensor, plan: ExchangePlan) -> torch.Tensor:
+        if y.shape[0] != sum(plan.recv):
+            raise ValueError("result rows do not match the received rows")
+        rb = self.row_bytes
+        base = y.data_ptr()
+        jobs = [(self.peer_ret[s] + plan.back_off[s] * rb, base + plan.recv_off[s] * rb,
+                 plan.recv[s] * rb) for s in range(self.world)]
+        self._copies(jobs)
+        return self.ret_buf[:sum(plan.send)]
+
+    def close(self) -> None:
+        if self._opened:
+            torch.cuda.synchronize(self.device)
+            dist.barrier(group=self.group)
+            for b in self._opened:
+                _lib.call("moe_ipc_close_handle", b)
+            self._opened = []
+
+
 class MoELayerEP:
     """Expert-parallel forward; this rank holds the weights of its local experts.
 
@@ -114,8 +268,19 @@ class MoELayerEP:
 
     def __init__(self, local_weights: MoEWeights, num_experts: int, topk: int = 8,
                  renorm: bool = True, expert_bias: Optional[torch.Tensor] = None,
-                 group: Optional[dist.ProcessGroup] = None):
+                 group: Optional[dist.ProcessGroup] = None, transport: str = "nccl",
+                 tokens: Optional[int] = None):
+        """transport "nccl": all_to_all_single of counts and rows; "peer": IPC-mapped
+        buffers filled by copy-engine pushes (needs `tokens`, the per-rank T)."""
         self.disp = EPDispatcher(num_experts, group)
+        self.peer = None
+        if transport == "peer":
+            if tokens is None:
+                raise ValueError("transport='peer' needs the per-rank token count")
+            self.peer = EPPeerExchange(num_experts, tokens, local_weights.hidden, topk,
+                                       local_weights.w1.device, group)
+        elif transport != "nccl":
+            raise ValueError("transport must be 'nccl' or 'peer'")
         if local_weights.num_experts != self.disp.local_experts:
             raise ValueError("local weights do not match num_experts / world size")
         self.w = local_weights
@@ -137,21 +302,32 @@ class MoELayerEP:
             raise ValueError(f"logits must be [{t},{e}]")
         self._ev("start")
         r = ops.router_topk(logits, self.k, "softmax", self.renorm, self.bias, outputs="maps")
-        rim = ops.row_id_map(r.routing_map, align=1)
+        rim = ops.row_id_map(r.routing_map, align=1, want_et=False)
         xp, _ = ops.permute(x, rim.map_te, None, num_out=t * self.k)
         self._ev("local_dispatch")
-        send, recv, recv_counts = self.disp.exchange_counts(rim.counts)
-        xr = self.disp.dispatch(xp, send, recv)
+        if self.peer is not None:
+            plan, recv_counts = self.peer.exchange_counts(rim.counts)
+            xr = self.peer.dispatch(xp, plan)
+        else:
+            send, recv, recv_counts = self.disp.exchange_counts(rim.counts)
+            xr = self.disp.dispatch(xp, send, recv)
         self._ev("a2a_dispatch")
         self.plan.from_ep_counts(recv_counts, self.disp.world, self.disp.local_experts)
         hmid = ops.grouped_gemm(xr, self.w.w1, epilogue="swiglu", plan=self.plan)
         self._ev("fc1")
         y = ops.grouped_gemm(hmid, self.w.w2, plan=self.plan)
         self._ev("fc2")
-        yb = self.disp.combine(y, send, recv)
+        if self.peer is not None:
+            yb = self.peer.combine(y, plan)
+        else:
+            yb = self.disp.combine(y, send, recv)
         self._ev("a2a_combine")
-        out = ops.unpermute(yb, rim.map_et, r.probs, probs_mode="dense")
+        out = ops.unpermute(yb, rim.map_te, r.probs, probs_mode="dense", token_major=True)
         self._ev("combine")
         return out
 
     __call__ = forward
+
+    def close(self) -> None:
+        if self.peer is not None:
+            self.peer.close()

@@ -84,7 +84,7 @@ class MoELayer:
             raise ValueError(f"x hidden {h} != weights hidden {self.w.hidden}")
         self._ev("start")
         r = ops.router_topk(logits, self.k, "softmax", self.renorm, self.bias, outputs="maps")
-        rim = ops.row_id_map(r.routing_map, align=1)
+        rim = ops.row_id_map(r.routing_map, align=1, want_et=False)
         self._ev("routing")
         rows = t * self.k
         xp, _ = ops.permute(x, rim.map_te, None, num_out=rows)
@@ -94,7 +94,7 @@ class MoELayer:
         self._ev("fc1")
         y = ops.grouped_gemm(hmid, self.w.w2, plan=self.plan)
         self._ev("fc2")
-        out = ops.unpermute(y, rim.map_et, r.probs, probs_mode="dense")
+        out = ops.unpermute(y, rim.map_te, r.probs, probs_mode="dense", token_major=True)
         self._ev("combine")
         if return_intermediates:
             return out, dict(routing=r, rim=rim, xp=xp, h=hmid, y=y)

@@ -227,11 +227,12 @@ def permute_trans(x: torch.Tensor, row_id_map: torch.Tensor, probs: Optional[tor
 
 # --------------------------------------------------------------------------- a6-a8
 def unpermute(pin: torch.Tensor, row_id_map: torch.Tensor, probs: Optional[torch.Tensor] = None,
-              probs_mode: str = "dense", return_acc: bool = False):
+              probs_mode: str = "dense", return_acc: bool = False, token_major: bool = False):
     """out[t] = bf16(sum over e ascending of w * pin[row_id_map[e,t]]), fp32 accumulation.
 
     w = 1 without probs (case15 / case24); w = probs[t,e] for probs_mode
     "dense" ([T,E]); w = probs[row] for probs_mode "permuted" ([rows]).
+    token_major=True takes the [T,E] int64 map instead of [E,T] (same result).
     Returns out (and the fp32 accumulator when return_acc).
     """
     for n_, t_ in (("pin", pin), ("row_id_map", row_id_map), ("probs", probs)):
@@ -240,7 +241,11 @@ def unpermute(pin: torch.Tensor, row_id_map: torch.Tensor, probs: Optional[torch
         raise ValueError(f"shapes pin {tuple(pin.shape)} row_id_map {tuple(row_id_map.shape)}")
     _need_dtype("pin", pin, torch.bfloat16)
     _need_dtype("row_id_map", row_id_map, torch.int64, torch.int32)
-    e, t = row_id_map.shape
+    if token_major:
+        _need_dtype("row_id_map", row_id_map, torch.int64)
+        t, e = row_id_map.shape
+    else:
+        e, t = row_id_map.shape
     pc = pin.contiguous()
     mc = row_id_map.contiguous()
     mode = -1
@@ -259,9 +264,14 @@ def unpermute(pin: torch.Tensor, row_id_map: torch.Tensor, probs: Optional[torch
             raise ValueError("probs_mode must be 'dense' or 'permuted'")
     out = torch.empty((t, pc.shape[1]), dtype=pc.dtype, device=pc.device)
     acc = torch.empty((t, pc.shape[1]), dtype=torch.float32, device=pc.device) if return_acc else None
-    bits = 64 if mc.dtype == torch.int64 else 32
-    _lib.call("moe_unpermute_mask", _p(pc), _p(mc), bits, _p(prc), mode if mode >= 0 else 0,
-              _p(out), _p(acc), t, pc.shape[1], e, pc.shape[0], _stream(pc.device))
+    if token_major:
+        _lib.call("moe_unpermute_mask_token_major", _p(pc), _p(mc), _p(prc),
+                  mode if mode >= 0 else 0, _p(out), _p(acc), t, pc.shape[1], e, pc.shape[0],
+                  _stream(pc.device))
+    else:
+        bits = 64 if mc.dtype == torch.int64 else 32
+        _lib.call("moe_unpermute_mask", _p(pc), _p(mc), bits, _p(prc), mode if mode >= 0 else 0,
+                  _p(out), _p(acc), t, pc.shape[1], e, pc.shape[0], _stream(pc.device))
     return (out, acc) if return_acc else out
 
 

@@ -57,6 +57,8 @@ def parse_args():
                     help="token sample of the CPU baseline (per step for --impl reference)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
+                    help="EP row exchange: IPC-mapped buffers + copy engines, or NCCL all-to-all")
     return ap.parse_args()
 
 
@@ -73,6 +75,7 @@ def config_dict(a, world):
             "tokens_per_gpu": a.tokens, "hidden": a.hidden, "experts": a.experts,
             "topk": a.topk, "ffn": a.ffn, "routing": a.routing,
             "parallelism": f"ep{world}" if world > 1 else "single",
+            **({"ep_transport": a.transport} if world > 1 else {}),
             "l2": "no flush: every step streams >22 GB of expert weights and 0.25 GB of "
                   "activations, both larger than the 126 MB L2"}
 
@@ -195,6 +198,18 @@ def cpu_layer_sample(a, tokens, seed=0):
     return time.perf_counter() - t0, tokens
 
 
+def use_all_cores():
+    """Lets the CPU legs use every host core (torchrun sets OMP_NUM_THREADS=1)."""
+    n = len(os.sched_getaffinity(0)) if hasattr(os, "sched_getaffinity") else (os.cpu_count() or 1)
+    import numpy  # noqa: F401  (load BLAS so its pool can be resized)
+    try:
+        from threadpoolctl import threadpool_limits
+        threadpool_limits(limits=n)
+    except Exception:
+        pass
+    return n
+
+
 def cpu_threads():
     try:
         from threadpoolctl import threadpool_info
@@ -209,6 +224,7 @@ def cpu_threads():
 def run_reference_arm(a, world, rank):
     if rank != 0:
         return
+    use_all_cores()
     for _ in range(a.warmup):
         cpu_layer_sample(a, a.cpu_tokens, seed=1)
     times = []
@@ -277,7 +293,7 @@ def main():
         stage_names = ["start", "routing", "permute", "fc1", "fc2", "combine"]
     else:
         from moe_b200.ep import MoELayerEP
-        layer = MoELayerEP(w, e, topk=k, expert_bias=bias)
+        layer = MoELayerEP(w, e, topk=k, expert_bias=bias, transport=a.transport, tokens=t)
         stage_names = ["start", "local_dispatch", "a2a_dispatch", "fc1", "fc2", "a2a_combine",
                        "combine"]
 
@@ -388,6 +404,7 @@ def main():
 
     cpu = None
     if world == 1 and rank == 0 and not a.no_cpu_baseline:
+        use_all_cores()
         dt, n = cpu_layer_sample(a, a.cpu_tokens)
         cpu = {"value": n / dt, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
                "sample": f"{n} tokens of the {t}-token layer (same H/E/F/top-k, {a.routing} "
@@ -407,6 +424,8 @@ def main():
         line.update(extra)
         print(json.dumps(line), flush=True)
     if world > 1:
+        if hasattr(layer, "close"):
+            layer.close()
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
 

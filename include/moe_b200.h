@@ -132,6 +132,14 @@ int moe_unpermute_mask(const void* pin, const void* row_id_map_et, int32_t idx_b
                        const float* probs, int32_t probs_mode, void* out, float* acc_out,
                        int64_t T, int64_t H, int64_t E, int64_t num_rows, moe_stream_t stream);
 
+/* Same combine driven by the token-major [T,E] int64 map (the layout         */
+/* kernel_cases/case12_moe_row_id_map_pass2.py:61 returns second), whose     */
+/* entries for one token are contiguous. Identical results. E <= 1024.       */
+int moe_unpermute_mask_token_major(const void* pin, const int64_t* row_id_map_te,
+                                   const float* probs, int32_t probs_mode, void* out,
+                                   float* acc_out, int64_t T, int64_t H, int64_t E,
+                                   int64_t num_rows, moe_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* a9/a10/a11  Grouped GEMM on tcgen05 tensor cores (bf16 in, fp32 acc).     */
 /* out[r, :] = x[r, :] @ w[widx(g)]^T for the rows r of group g, where       */
@@ -170,6 +178,20 @@ int moe_grouped_gemm_check(const void* workspace, size_t workspace_bytes, moe_st
 
 /* a11 standalone: h[M,F] = bf16(silu(y[:, :F]) * y[:, F:]) for y [M,2F].    */
 int moe_swiglu(const void* y, void* h, int64_t M, int64_t F, moe_stream_t stream);
+
+/* ------------------------------------------------------------------------ */
+/* Expert-parallel exchange over NVLink (e): receive buffers registered for  */
+/* peer access with CUDA IPC, rows pushed by the copy engines. Stands in for  */
+/* the intranode deep_ep dispatch / combine the reference names but does not */
+/* contain (kernel_cases/case22_ref_moe_permute_mask_kernel_true.py:3-6,     */
+/* case24_ref_moe_unpermute_mask_kernel_false.py:3-6).                        */
+/* handle: 64 bytes (cudaIpcMemHandle_t) of the allocation holding dev_ptr;  */
+/* offset: dev_ptr minus that allocation's base.                             */
+int moe_ipc_get_handle(const void* dev_ptr, void* handle_out, uint64_t* offset_out);
+int moe_ipc_open_handle(const void* handle, void** base_out);
+int moe_ipc_close_handle(void* base);
+/* Asynchronous device-to-device copy (either side may be a peer mapping).   */
+int moe_copy_async(void* dst, const void* src, size_t bytes, moe_stream_t stream);
 
 #ifdef __cplusplus
 }

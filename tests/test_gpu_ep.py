@@ -37,7 +37,7 @@ def _problem(world, t, h, e, f, routing):
     return x, lg, bias, w1, w2
 
 
-def _worker(rank, world, port, routing, q):
+def _worker(rank, world, port, routing, transport, q):
     for p in (str(PKG), str(ROOT), str(GOLDEN)):
         if p not in sys.path:
             sys.path.insert(0, p)
@@ -56,8 +56,11 @@ def _worker(rank, world, port, routing, q):
         sl = slice(rank * t, (rank + 1) * t)
         local = moe_b200.MoEWeights(w1[rank * el:(rank + 1) * el].to(dev).contiguous(),
                                     w2[rank * el:(rank + 1) * el].to(dev).contiguous())
-        layer = MoELayerEP(local, e, topk=k, expert_bias=bias.to(dev))
+        layer = MoELayerEP(local, e, topk=k, expert_bias=bias.to(dev), transport=transport,
+                           tokens=t)
         out = layer(x[sl].to(dev), lg[sl].to(dev))
+        out2 = layer(x[sl].to(dev), lg[sl].to(dev))  # buffers reused across forwards
+        assert torch.equal(out, out2)
         outs = [torch.empty_like(out) for _ in range(world)]
         dist.all_gather(outs, out)
         err = layer.plan.device_error()
@@ -67,6 +70,7 @@ def _worker(rank, world, port, routing, q):
                                      expert_bias=bias.to(dev))
             ref = full(x.to(dev), lg.to(dev))
             ok = bool(torch.equal(torch.cat(outs), ref))
+        layer.close()
         dist.barrier(device_ids=[rank])
         dist.destroy_process_group()
         q.put((rank, ok, err))
@@ -74,8 +78,10 @@ def _worker(rank, world, port, routing, q):
         q.put((rank, "error", f"{type(exc).__name__}: {exc}", traceback.format_exc()[-1500:]))
 
 
-@pytest.mark.parametrize("world,routing", [(2, "uniform"), (2, "zipf"), (4, "zipf")])
-def test_ep_equals_single_gpu(world, routing):
+@pytest.mark.parametrize("world,routing,transport", [(2, "uniform", "nccl"), (2, "zipf", "nccl"),
+                                                     (2, "zipf", "peer"), (2, "uniform", "peer"),
+                                                     (4, "zipf", "peer"), (4, "uniform", "nccl")])
+def test_ep_equals_single_gpu(world, routing, transport):
     if not torch.cuda.is_available():
         pytest.fail("GPU test selected but no CUDA device is visible")
     if torch.cuda.device_count() < world:
@@ -84,7 +90,7 @@ def test_ep_equals_single_gpu(world, routing):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, routing, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, routing, transport, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = sorted((q.get(timeout=300) for _ in range(world)), key=lambda r: r[0])

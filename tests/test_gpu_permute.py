@@ -189,6 +189,10 @@ def test_combine_vs_oracle(cuda_dev, t, h, e, k, mode):
                                  tokens=tokens)
     np.testing.assert_array_equal(acc.cpu().numpy()[tokens], ref_acc)
     np.testing.assert_array_equal(u16(out)[tokens], ref)
+    # token-major map: same sums, same bits
+    out_tm, acc_tm = moe_b200.unpermute(pin.to(cuda_dev), m.map_te, probs, mode or "dense",
+                                        return_acc=True, token_major=True)
+    assert torch.equal(out_tm, out) and torch.equal(acc_tm, acc)
 
 
 def test_permute_unpermute_round_trip_full_size(cuda_dev):
