@@ -69,6 +69,8 @@ struct Params {
   int num_kb;
   int n_tiles;
   int epilogue;
+  int raster;   // pair kernel: pair M-tiles per raster super-row
+  int l2_mode;  // pair kernel: 0 both evict_normal, 1 B evict_first, 2 A evict_last + B evict_first
 };
 
 struct Tile {
@@ -112,6 +114,39 @@ struct WalkerT {
   }
 };
 using Walker = WalkerT<BM, kSuperRow>;
+
+// Same walk with the super-row height chosen at run time.
+template <int kTileM>
+struct WalkerRT {
+  const int32_t* rows;
+  int G;
+  int n_tiles;
+  int raster;
+  int g = 0;
+  int mt = -1;
+  long long base = 0;
+
+  __device__ bool locate(long long t, Tile& tile) {
+    while (g < G) {
+      if (mt < 0) mt = (max(rows[g], 0) + kTileM - 1) / kTileM;
+      const long long cnt = static_cast<long long>(mt) * n_tiles;
+      if (t < base + cnt) break;
+      base += cnt;
+      ++g;
+      mt = -1;
+    }
+    if (g >= G) return false;
+    const long long local = t - base;
+    const long long sr_tiles = static_cast<long long>(raster) * n_tiles;
+    const int sr = static_cast<int>(local / sr_tiles);
+    const int within = static_cast<int>(local - sr * sr_tiles);
+    const int mg = min(raster, mt - sr * raster);
+    tile.g = g;
+    tile.n_idx = within / mg;
+    tile.m_idx = sr * raster + within % mg;
+    return true;
+  }
+};
 
 MOE_DEVICE bool wait_drain(uint32_t bar, uint32_t parity) {
   const unsigned long long t0 = globaltimer_ns();
@@ -447,13 +482,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  WalkerT<pairk::kPairTileM, pairk::kPairRaster> walker{p.rows, p.G, p.n_tiles};
+  WalkerRT<pairk::kPairTileM> walker{p.rows, p.G, p.n_tiles, p.raster};
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
-      const uint64_t pol_a = l2_policy_evict_normal();
-      const uint64_t pol_b = l2_policy_evict_normal();
+      // Weight slabs are read by the few M-tiles of one super-row and then not
+      // again until the next super-row; activation rows are reused by every
+      // N-tile of the super-row. Mode 1/2 let L2 drop the weights first.
+      const uint64_t pol_a = p.l2_mode == 2 ? l2_policy_evict_last() : l2_policy_evict_normal();
+      const uint64_t pol_b = p.l2_mode >= 1 ? l2_policy_evict_first() : l2_policy_evict_normal();
       int stage = 0;
       uint32_t phase = 0;
       int issued[pairk::kPairStages];
@@ -808,6 +846,13 @@ int pair_clusters(int dev) {
   return n;
 }
 
+int env_int(const char* name, int def, int lo, int hi) {
+  const char* e = getenv(name);
+  if (e == nullptr || e[0] == 0) return def;
+  const int v = atoi(e);
+  return (v < lo || v > hi) ? def : v;
+}
+
 bool pair_enabled() {
   static int v = -1;
   if (v < 0) {
@@ -939,6 +984,10 @@ extern "C" int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t
     p.n_tiles = static_cast<int>((N + gg::BN - 1) / gg::BN);
   }
   p.num_kb = static_cast<int>((K + gg::BK - 1) / gg::BK);
+  static const int raster = gg::env_int("MOE_GEMM_RASTER", gg::pairk::kPairRaster, 1, 64);
+  static const int l2_mode = gg::env_int("MOE_GEMM_L2", 0, 0, 2);
+  p.raster = raster;
+  p.l2_mode = l2_mode;
 
   int dev = 0;
   MOE_CUDA_CALL(cudaGetDevice(&dev), "cudaGetDevice");

@@ -19,19 +19,33 @@ namespace {
 
 constexpr int kTopkMaxK = 16;
 
-// a is ranked before b: NaN first (torch.topk / torch.sort treat NaN as the
-// largest value), then larger value, then lower index.
-MOE_DEVICE bool ranks_before(float av, int ai, float bv, int bi) {
-  const bool an = isnan(av), bn = isnan(bv);
-  if (an != bn) return an;
-  if (!an && av != bv) return av > bv;
-  return ai < bi;
+// Ranking key of (value, column): larger key = ranked first. The high word
+// maps floats to an unsigned order (NaN above everything, -0.0 == +0.0), the
+// low word is the inverted column so equal values rank the lower column first.
+// 0 is never a real key (the smallest real high word is that of -inf).
+MOE_DEVICE uint64_t rank_key(float v, int c) {
+  uint32_t hi;
+  if (isnan(v)) {
+    hi = 0xFFFFFFFFu;
+  } else {
+    const uint32_t u = __float_as_uint(v + 0.0f);  // -0.0 -> +0.0
+    hi = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  }
+  return (static_cast<uint64_t>(hi) << 32) | static_cast<uint32_t>(0xFFFFFFFFu - c);
+}
+MOE_DEVICE float key_value(uint64_t key) {
+  const uint32_t hi = static_cast<uint32_t>(key >> 32);
+  if (hi == 0xFFFFFFFFu) return __uint_as_float(0x7FC00000u);
+  return __uint_as_float((hi & 0x80000000u) ? (hi & 0x7FFFFFFFu) : ~hi);
+}
+MOE_DEVICE int key_column(uint64_t key) {
+  return static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(key & 0xFFFFFFFFull));
 }
 
 // One warp per row. Lane l owns columns l, l+32, ..., l+32*(VPL-1).
 // mode 0: plain top-k of the input (values = input values).
 // mode 1: router with softmax gates; mode 2: router with raw-logit gates.
-template <int VPL>
+template <int VPL, int KMAX>
 __global__ void __launch_bounds__(256) topk_router_kernel(
     const float* __restrict__ in, const float* __restrict__ bias, int64_t T, int N, int k,
     int mode, int renorm, float* __restrict__ out_vals, int64_t* __restrict__ out_idx,
@@ -42,113 +56,96 @@ __global__ void __launch_bounds__(256) topk_router_kernel(
   const float* rin = in + row * N;
 
   float v[VPL];
+  uint64_t key[VPL];
 #pragma unroll
   for (int j = 0; j < VPL; ++j) {
     const int c = lane + 32 * j;
     float x = -INFINITY;
+    key[j] = 0;
     if (c < N) {
       x = __ldg(rin + c);
       if (bias != nullptr) x += __ldg(bias + c);
+      key[j] = rank_key(x, c);
     }
     v[j] = x;
   }
 
-  uint64_t taken = 0;  // bit j: column lane+32j already selected
-  // Lane-local best untaken candidate; padding columns (c >= N) never compete.
-  auto local_best = [&](float& bv, int& bi) {
-    bv = -INFINITY;
-    bi = INT_MAX;
+  auto local_best = [&]() {
+    uint64_t b = 0;
 #pragma unroll
-    for (int j = 0; j < VPL; ++j) {
-      const int c = lane + 32 * j;
-      if (c < N && !((taken >> j) & 1ull) && ranks_before(v[j], c, bv, bi)) {
-        bv = v[j];
-        bi = c;
-      }
-    }
+    for (int j = 0; j < VPL; ++j) b = key[j] > b ? key[j] : b;
+    return b;
   };
 
-  float sel_v[kTopkMaxK];
-  int sel_i[kTopkMaxK];
-  float bv;
-  int bi;
-  local_best(bv, bi);
+  uint64_t taken = 0;  // bit j: column lane+32j selected
+  uint64_t sel[KMAX];
+  uint64_t best = local_best();
 #pragma unroll
-  for (int r = 0; r < kTopkMaxK; ++r) {
+  for (int r = 0; r < KMAX; ++r) {
     if (r < k) {
-      float wv = bv;
-      int wi = bi;
+      uint64_t w = best;
 #pragma unroll
       for (int off = 16; off > 0; off >>= 1) {
-        const float ov = __shfl_xor_sync(0xffffffffu, wv, off);
-        const int oi = __shfl_xor_sync(0xffffffffu, wi, off);
-        if (ranks_before(ov, oi, wv, wi)) {
-          wv = ov;
-          wi = oi;
-        }
+        const uint64_t o = __shfl_xor_sync(0xffffffffu, w, off);
+        w = o > w ? o : w;
       }
-      sel_v[r] = wv;
-      sel_i[r] = wi;
-      if (wi != INT_MAX && (wi & 31) == lane) {
-        taken |= 1ull << (wi >> 5);
-        local_best(bv, bi);
+      sel[r] = w;
+      if (w == best && w != 0) {  // this lane owns the winner (keys are unique)
+#pragma unroll
+        for (int j = 0; j < VPL; ++j)
+          if (key[j] == w) {
+            key[j] = 0;
+            taken |= 1ull << j;
+          }
+        best = local_best();
       }
     }
   }
 
-  // Gate weights for the selected columns.
-  float gate[kTopkMaxK];
+  // Softmax statistics: row max and the normaliser.
+  float m = 0.f, denom = 1.f, gsum = 1.f;
   if (mode == 1) {
-    // Row max is the first selected logit unless NaNs are present; use a
-    // full reduction so the softmax matches its textbook definition.
-    float m = -INFINITY;
+    m = -INFINITY;
 #pragma unroll
     for (int j = 0; j < VPL; ++j) m = fmaxf(m, v[j]);
 #pragma unroll
     for (int off = 16; off > 0; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-    float denom = 0.f;
+    float sacc = 0.f;
     if (renorm) {
 #pragma unroll
-      for (int r = 0; r < kTopkMaxK; ++r)
-        if (r < k) denom += expf(sel_v[r] - m);
+      for (int r = 0; r < KMAX; ++r)
+        if (r < k) sacc += expf(key_value(sel[r]) - m);
     } else {
-      float s = 0.f;
 #pragma unroll
       for (int j = 0; j < VPL; ++j)
-        if (lane + 32 * j < N) s += expf(v[j] - m);
+        if (lane + 32 * j < N) sacc += expf(v[j] - m);
 #pragma unroll
-      for (int off = 16; off > 0; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-      denom = s;
+      for (int off = 16; off > 0; off >>= 1) sacc += __shfl_xor_sync(0xffffffffu, sacc, off);
     }
+    denom = sacc;
+  } else if (mode == 2 && renorm) {
+    float sacc = 0.f;
 #pragma unroll
-    for (int r = 0; r < kTopkMaxK; ++r)
-      if (r < k) gate[r] = expf(sel_v[r] - m) / denom;
-  } else {
-#pragma unroll
-    for (int r = 0; r < kTopkMaxK; ++r)
-      if (r < k) gate[r] = sel_v[r];
-    if (mode == 2 && renorm) {
-      float s = 0.f;
-#pragma unroll
-      for (int r = 0; r < kTopkMaxK; ++r)
-        if (r < k) s += gate[r];
-#pragma unroll
-      for (int r = 0; r < kTopkMaxK; ++r)
-        if (r < k) gate[r] = gate[r] / s;
-    }
+    for (int r = 0; r < KMAX; ++r)
+      if (r < k) sacc += key_value(sel[r]);
+    gsum = sacc;
   }
+  auto gate_of = [&](float x) {
+    if (mode == 1) return expf(x - m) / denom;
+    if (mode == 2 && renorm) return x / gsum;
+    return x;
+  };
 
   if (lane < k) {
-    float g = 0.f;
-    int64_t idx = 0;
+    uint64_t mine = 0;
 #pragma unroll
-    for (int r = 0; r < kTopkMaxK; ++r)
-      if (r == lane) {
-        g = gate[r];
-        idx = sel_i[r];
-      }
-    if (out_vals) out_vals[row * k + lane] = g;
-    if (out_idx) out_idx[row * k + lane] = idx;
+    for (int r = 0; r < KMAX; ++r)
+      if (r == lane) mine = sel[r];
+    const int c = key_column(mine);
+    float x = __ldg(rin + c);  // exact input value (keeps -0.0 and NaN payloads)
+    if (bias != nullptr) x += __ldg(bias + c);
+    if (out_vals) out_vals[row * k + lane] = gate_of(x);
+    if (out_idx) out_idx[row * k + lane] = c;
   }
   if (routing_map != nullptr || probs != nullptr) {
 #pragma unroll
@@ -156,14 +153,8 @@ __global__ void __launch_bounds__(256) topk_router_kernel(
       const int c = lane + 32 * j;
       if (c < N) {
         const bool t = (taken >> j) & 1ull;
-        float g = 0.f;
-        if (t) {
-#pragma unroll
-          for (int r = 0; r < kTopkMaxK; ++r)
-            if (r < k && sel_i[r] == c) g = gate[r];
-        }
         if (routing_map) routing_map[row * N + c] = t ? 1 : 0;
-        if (probs) probs[row * N + c] = g;
+        if (probs) probs[row * N + c] = t ? gate_of(v[j]) : 0.f;
       }
     }
   }
@@ -175,8 +166,13 @@ void launch_topk(const float* in, const float* bias, int64_t T, int N, int k, in
                  cudaStream_t s) {
   const int rows_per_block = 8;
   const int64_t blocks = (T + rows_per_block - 1) / rows_per_block;
-  topk_router_kernel<VPL><<<static_cast<unsigned>(blocks), 32 * rows_per_block, 0, s>>>(
-      in, bias, T, N, k, mode, renorm, vals, idx, rmap, probs);
+  if (k <= 8)
+    topk_router_kernel<VPL, 8><<<static_cast<unsigned>(blocks), 32 * rows_per_block, 0, s>>>(
+        in, bias, T, N, k, mode, renorm, vals, idx, rmap, probs);
+  else
+    topk_router_kernel<VPL, kTopkMaxK><<<static_cast<unsigned>(blocks), 32 * rows_per_block, 0,
+                                         s>>>(in, bias, T, N, k, mode, renorm, vals, idx, rmap,
+                                              probs);
 }
 
 int run_topk(const float* in, const float* bias, int64_t T, int64_t N, int k, int mode, int renorm,
@@ -309,6 +305,126 @@ __global__ void __launch_bounds__(1024) rim_scan_kernel(int32_t* __restrict__ co
   }
 }
 
+// Parallel variant for E <= kRimFastMaxE: one warp per expert turns
+// counts[e][c] into chunk bases local to the expert (exclusive scan over
+// chunks) and writes the expert's total; the expert offsets are then formed
+// inside every fill block from the totals (rim_fill_offsets_kernel).
+constexpr int kRimFastMaxE = 2048;
+
+__global__ void __launch_bounds__(1024) rim_scan_experts_kernel(int32_t* __restrict__ counts, int E,
+                                                                int C,
+                                                                int64_t* __restrict__ totals) {
+  const int lane = lane_id();
+  const int e = blockIdx.x * 32 + warp_id();
+  if (e >= E) return;
+  int32_t* col = counts + static_cast<int64_t>(e) * C;
+  int carry = 0;
+  for (int c0 = 0; c0 < C; c0 += 32) {
+    const int c = c0 + lane;
+    const int x = (c < C) ? col[c] : 0;
+    int incl = x;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int y = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += y;
+    }
+    if (c < C) col[c] = carry + incl - x;
+    carry += __shfl_sync(0xffffffffu, incl, 31);
+  }
+  if (lane == 0) totals[e] = carry;
+}
+
+// Exclusive scan of the padded expert totals into s_off[0..E) by one block of
+// kRimThreads threads; block (0,0) also publishes expert_counts and num_out.
+MOE_DEVICE void rim_block_offsets(const int64_t* __restrict__ totals, int E, int64_t align,
+                                  int32_t* s_off, int64_t* s_warp, int32_t* __restrict__ expert_counts,
+                                  int64_t* __restrict__ num_out, bool publish) {
+  const int lane = lane_id(), wid = warp_id();
+  constexpr int kWarps = kRimThreads / 32;
+  int64_t carry = 0;
+  for (int e0 = 0; e0 < E; e0 += kRimThreads) {
+    const int e = e0 + threadIdx.x;
+    int64_t tot = 0, padded = 0;
+    if (e < E) {
+      tot = totals[e];
+      padded = (align > 1) ? ((tot + align - 1) / align) * align : tot;
+      if (publish && expert_counts) expert_counts[e] = static_cast<int32_t>(tot);
+    }
+    int64_t incl = padded;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int64_t y = __shfl_up_sync(0xffffffffu, incl, off);
+      if (lane >= off) incl += y;
+    }
+    if (lane == 31) s_warp[wid] = incl;
+    __syncthreads();
+    int64_t before = 0, all = 0;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const int64_t v = s_warp[w];
+      before += (w < wid) ? v : 0;
+      all += v;
+    }
+    if (e < E) s_off[e] = static_cast<int32_t>(carry + before + incl - padded);
+    carry += all;
+    __syncthreads();
+  }
+  if (publish && threadIdx.x == 0 && num_out) *num_out = carry;
+}
+
+// Ordered fill (see rim_fill_kernel) with the expert offsets computed in-block.
+__global__ void __launch_bounds__(kRimThreads) rim_fill_offsets_kernel(
+    const uint8_t* __restrict__ rmap, int64_t T, int E, int C, const int32_t* __restrict__ bases,
+    const int64_t* __restrict__ totals, int64_t align, int64_t* __restrict__ row_et,
+    int64_t* __restrict__ row_te, int32_t* __restrict__ expert_counts,
+    int64_t* __restrict__ num_out) {
+  __shared__ int32_t tile[kRimThreads][33];
+  __shared__ int32_t s_off[kRimFastMaxE];
+  __shared__ int64_t s_warp[kRimThreads / 32];
+  rim_block_offsets(totals, E, align, s_off, s_warp, expert_counts, num_out,
+                    blockIdx.x == 0 && blockIdx.y == 0);
+  const int c = blockIdx.x;
+  const int e0 = blockIdx.y * kRimThreads;
+  const int e = e0 + threadIdx.x;
+  const bool active = e < E;
+  int running = active ? s_off[e] + bases[static_cast<int64_t>(e) * C + c] : 0;
+  const int64_t tc0 = static_cast<int64_t>(c) * kRimChunk;
+  if (row_et == nullptr && row_te == nullptr) return;
+  for (int sub = 0; sub < kRimChunk; sub += 32) {
+    const int64_t t0 = tc0 + sub;
+    if (t0 >= T) break;
+    const int nt = static_cast<int>((T - t0) < 32 ? (T - t0) : 32);
+    uint8_t m[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i)
+      m[i] = (active && i < nt) ? __ldg(rmap + (t0 + i) * E + e) : 0;
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      if (i < nt) {
+        int32_t val = -1;
+        if (m[i]) val = running++;
+        if (active && row_te) row_te[(t0 + i) * E + e] = val;
+        tile[threadIdx.x][i] = val;
+      }
+    }
+    __syncthreads();
+    if (row_et) {
+      const int lane = lane_id(), wid = warp_id();
+      for (int el = wid; el < kRimThreads; el += kRimThreads / 32) {
+        const int ee = e0 + el;
+        if (ee < E && lane < nt) row_et[static_cast<int64_t>(ee) * T + t0 + lane] = tile[el][lane];
+      }
+    }
+    __syncthreads();
+  }
+}
+
+// Launch sequence shared by both row_id_map entry points: `counts` holds
+// E*C int32 chunk counts, `offs` E int64 (totals / offsets).
+int rim_launch(const uint8_t* routing_map, int64_t T, int64_t E, int64_t align,
+               int64_t* row_id_map_et, int64_t* row_id_map_te, int32_t* expert_counts,
+               int64_t* num_out, int32_t* counts, int64_t* offs, cudaStream_t s, const char* who);
+
 // Ordered fill. Block (c, eb): tokens of chunk c, experts eb*256 + tid.
 // Each thread walks its expert column in token order (a running counter),
 // writing row_te row-wise (coalesced over experts) and staging a 32-token
@@ -350,6 +466,37 @@ __global__ void __launch_bounds__(kRimThreads) rim_fill_kernel(
     }
     __syncthreads();
   }
+}
+
+int rim_launch(const uint8_t* routing_map, int64_t T, int64_t E, int64_t align,
+               int64_t* row_id_map_et, int64_t* row_id_map_te, int32_t* expert_counts,
+               int64_t* num_out, int32_t* counts, int64_t* offs, cudaStream_t s, const char* who) {
+  const int C = static_cast<int>((T + kRimChunk - 1) / kRimChunk);
+  const int eblocks = static_cast<int>((E + kRimThreads - 1) / kRimThreads);
+  if (C > 0) {
+    rim_count_kernel<<<dim3(C, eblocks), kRimThreads, 0, s>>>(routing_map, T, (int)E, C, counts);
+    MOE_CUDA_CHECK_LAUNCH(who);
+  }
+  const bool want_maps = row_id_map_et != nullptr || row_id_map_te != nullptr;
+  if (C > 0 && E <= kRimFastMaxE) {
+    rim_scan_experts_kernel<<<static_cast<unsigned>((E + 31) / 32), 1024, 0, s>>>(counts, (int)E,
+                                                                                  C, offs);
+    MOE_CUDA_CHECK_LAUNCH(who);
+    rim_fill_offsets_kernel<<<dim3(want_maps ? C : 1, want_maps ? eblocks : 1), kRimThreads, 0,
+                              s>>>(routing_map, T, (int)E, C, counts, offs, align,
+                                   want_maps ? row_id_map_et : nullptr,
+                                   want_maps ? row_id_map_te : nullptr, expert_counts, num_out);
+    MOE_CUDA_CHECK_LAUNCH(who);
+    return MOE_OK;
+  }
+  rim_scan_kernel<<<1, 1024, 0, s>>>(counts, (int)E, C, align, offs, expert_counts, num_out);
+  MOE_CUDA_CHECK_LAUNCH(who);
+  if (C > 0 && want_maps) {
+    rim_fill_kernel<<<dim3(C, eblocks), kRimThreads, 0, s>>>(routing_map, T, (int)E, C, counts,
+                                                             row_id_map_et, row_id_map_te);
+    MOE_CUDA_CHECK_LAUNCH(who);
+  }
+  return MOE_OK;
 }
 
 }  // namespace
@@ -411,19 +558,8 @@ extern "C" int moe_row_id_map(const uint8_t* routing_map, int64_t T, int64_t E, 
   int32_t* counts = static_cast<int32_t*>(workspace);
   size_t counts_bytes = (static_cast<size_t>(E) * C * 4 + 255) & ~static_cast<size_t>(255);
   int64_t* offs = reinterpret_cast<int64_t*>(static_cast<char*>(workspace) + counts_bytes);
-  const int eblocks = static_cast<int>((E + kRimThreads - 1) / kRimThreads);
-  if (C > 0) {
-    rim_count_kernel<<<dim3(C, eblocks), kRimThreads, 0, s>>>(routing_map, T, (int)E, C, counts);
-    MOE_CUDA_CHECK_LAUNCH("row_id_map count");
-  }
-  rim_scan_kernel<<<1, 1024, 0, s>>>(counts, (int)E, C, align, offs, expert_counts, num_out);
-  MOE_CUDA_CHECK_LAUNCH("row_id_map scan");
-  if (C > 0 && (row_id_map_et != nullptr || row_id_map_te != nullptr)) {
-    rim_fill_kernel<<<dim3(C, eblocks), kRimThreads, 0, s>>>(routing_map, T, (int)E, C, counts,
-                                                             row_id_map_et, row_id_map_te);
-    MOE_CUDA_CHECK_LAUNCH("row_id_map fill");
-  }
-  return MOE_OK;
+  return rim_launch(routing_map, T, E, align, row_id_map_et, row_id_map_te, expert_counts, num_out,
+                    counts, offs, s, "row_id_map launch");
 }
 
 // ---------------------------------------------------------------------------
@@ -504,17 +640,6 @@ extern "C" int moe_row_id_map_static_scratch(const uint8_t* routing_map, int64_t
   int32_t* counts = static_cast<int32_t*>(scratch);
   const size_t counts_bytes = (static_cast<size_t>(E) * C * 4 + 255) & ~static_cast<size_t>(255);
   int64_t* offs = reinterpret_cast<int64_t*>(static_cast<char*>(scratch) + counts_bytes);
-  const int eblocks = static_cast<int>((E + kRimThreads - 1) / kRimThreads);
-  if (C > 0) {
-    rim_count_kernel<<<dim3(C, eblocks), kRimThreads, 0, s>>>(routing_map, T, (int)E, C, counts);
-    MOE_CUDA_CHECK_LAUNCH("row_id_map_static_scratch count");
-  }
-  rim_scan_kernel<<<1, 1024, 0, s>>>(counts, (int)E, C, align, offs, expert_counts, num_out);
-  MOE_CUDA_CHECK_LAUNCH("row_id_map_static_scratch scan");
-  if (C > 0 && (row_id_map_et != nullptr || row_id_map_te != nullptr)) {
-    rim_fill_kernel<<<dim3(C, eblocks), kRimThreads, 0, s>>>(routing_map, T, (int)E, C, counts,
-                                                             row_id_map_et, row_id_map_te);
-    MOE_CUDA_CHECK_LAUNCH("row_id_map_static_scratch fill");
-  }
-  return MOE_OK;
+  return rim_launch(routing_map, T, E, align, row_id_map_et, row_id_map_te, expert_counts, num_out,
+                    counts, offs, s, "row_id_map_static_scratch launch");
 }
