@@ -498,14 +498,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int s = 0; s < pairk::kPairStages; ++s) issued[s] = -1;
       bool ok = true;
+      // Coordinates of this CTA's A rows and B rows for a tile.
+      auto coords = [&](const Tile& tl, int& ra, int& rb) {
+        ra = p.row_start[tl.g] + tl.m_idx * pairk::kPairTileM + static_cast<int>(rank) * 128;
+        const int wb = p.widx[tl.g] * p.n_w;
+        rb = (p.epilogue == 1) ? wb + tl.n_idx * 128 + static_cast<int>(rank) * p.f_half
+                               : wb + tl.n_idx * BN + static_cast<int>(rank) * 128;
+      };
       for (long long t = cid; ok; t += ncl) {
         Tile tile;
         if (!walker.locate(t, tile)) break;
-        const int row0 = p.row_start[tile.g] + tile.m_idx * pairk::kPairTileM + static_cast<int>(rank) * 128;
-        const int wbase = p.widx[tile.g] * p.n_w;
-        const int b0 = (p.epilogue == 1)
-                           ? wbase + tile.n_idx * 128 + static_cast<int>(rank) * p.f_half
-                           : wbase + tile.n_idx * BN + static_cast<int>(rank) * 128;
+        int row0, b0;
+        coords(tile, row0, b0);
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) {
             ok = false;

@@ -47,9 +47,9 @@ MOE_DEVICE int key_column(uint64_t key) {
 // mode 1: router with softmax gates; mode 2: router with raw-logit gates.
 template <int VPL, int KMAX>
 __global__ void __launch_bounds__(256) topk_router_kernel(
-    const float* __restrict__ in, const float* __restrict__ bias, int64_t T, int N, int k,
-    int mode, int renorm, float* __restrict__ out_vals, int64_t* __restrict__ out_idx,
-    uint8_t* __restrict__ routing_map, float* __restrict__ probs) {
+    const float* __restrict__ in, const float* __restrict__ bias, const int32_t* __restrict__ perm,
+    int64_t T, int N, int k, int mode, int renorm, float* __restrict__ out_vals,
+    int64_t* __restrict__ out_idx, uint8_t* __restrict__ routing_map, float* __restrict__ probs) {
   const int lane = lane_id();
   const int64_t row = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + warp_id();
   if (row >= T) return;
@@ -63,8 +63,9 @@ __global__ void __launch_bounds__(256) topk_router_kernel(
     float x = -INFINITY;
     key[j] = 0;
     if (c < N) {
-      x = __ldg(rin + c);
-      if (bias != nullptr) x += __ldg(bias + c);
+      const int src = perm ? __ldg(perm + c) : c;  // placement slot c reads column perm[c]
+      x = __ldg(rin + src);
+      if (bias != nullptr) x += __ldg(bias + src);
       key[j] = rank_key(x, c);
     }
     v[j] = x;
@@ -142,8 +143,9 @@ __global__ void __launch_bounds__(256) topk_router_kernel(
     for (int r = 0; r < KMAX; ++r)
       if (r == lane) mine = sel[r];
     const int c = key_column(mine);
-    float x = __ldg(rin + c);  // exact input value (keeps -0.0 and NaN payloads)
-    if (bias != nullptr) x += __ldg(bias + c);
+    const int src = perm ? __ldg(perm + c) : c;
+    float x = __ldg(rin + src);  // exact input value (keeps -0.0 and NaN payloads)
+    if (bias != nullptr) x += __ldg(bias + src);
     if (out_vals) out_vals[row * k + lane] = gate_of(x);
     if (out_idx) out_idx[row * k + lane] = c;
   }
@@ -161,22 +163,23 @@ __global__ void __launch_bounds__(256) topk_router_kernel(
 }
 
 template <int VPL>
-void launch_topk(const float* in, const float* bias, int64_t T, int N, int k, int mode,
-                 int renorm, float* vals, int64_t* idx, uint8_t* rmap, float* probs,
+void launch_topk(const float* in, const float* bias, const int32_t* perm, int64_t T, int N, int k,
+                 int mode, int renorm, float* vals, int64_t* idx, uint8_t* rmap, float* probs,
                  cudaStream_t s) {
   const int rows_per_block = 8;
   const int64_t blocks = (T + rows_per_block - 1) / rows_per_block;
   if (k <= 8)
     topk_router_kernel<VPL, 8><<<static_cast<unsigned>(blocks), 32 * rows_per_block, 0, s>>>(
-        in, bias, T, N, k, mode, renorm, vals, idx, rmap, probs);
+        in, bias, perm, T, N, k, mode, renorm, vals, idx, rmap, probs);
   else
     topk_router_kernel<VPL, kTopkMaxK><<<static_cast<unsigned>(blocks), 32 * rows_per_block, 0,
-                                         s>>>(in, bias, T, N, k, mode, renorm, vals, idx, rmap,
-                                              probs);
+                                         s>>>(in, bias, perm, T, N, k, mode, renorm, vals, idx,
+                                              rmap, probs);
 }
 
-int run_topk(const float* in, const float* bias, int64_t T, int64_t N, int k, int mode, int renorm,
-             float* vals, int64_t* idx, uint8_t* rmap, float* probs, cudaStream_t s) {
+int run_topk(const float* in, const float* bias, const int32_t* perm, int64_t T, int64_t N, int k,
+             int mode, int renorm, float* vals, int64_t* idx, uint8_t* rmap, float* probs,
+             cudaStream_t s) {
   MOE_REQUIRE(T >= 0 && N >= 1, "topk: bad shape T=%lld N=%lld", (long long)T, (long long)N);
   MOE_REQUIRE(k >= 1 && k <= N, "topk: k=%d out of range for N=%lld", k, (long long)N);
   if (k > kTopkMaxK || N > 2048) {
@@ -189,19 +192,19 @@ int run_topk(const float* in, const float* bias, int64_t T, int64_t N, int k, in
   MOE_REQUIRE(T <= (int64_t)0x7fffffff * 8, "topk: T too large");
   const int vpl = static_cast<int>((N + 31) / 32);
   if (vpl <= 1)
-    launch_topk<1>(in, bias, T, (int)N, k, mode, renorm, vals, idx, rmap, probs, s);
+    launch_topk<1>(in, bias, perm, T, (int)N, k, mode, renorm, vals, idx, rmap, probs, s);
   else if (vpl <= 2)
-    launch_topk<2>(in, bias, T, (int)N, k, mode, renorm, vals, idx, rmap, probs, s);
+    launch_topk<2>(in, bias, perm, T, (int)N, k, mode, renorm, vals, idx, rmap, probs, s);
   else if (vpl <= 4)
-    launch_topk<4>(in, bias, T, (int)N, k, mode, renorm, vals, idx, rmap, probs, s);
+    launch_topk<4>(in, bias, perm, T, (int)N, k, mode, renorm, vals, idx, rmap, probs, s);
   else if (vpl <= 8)
-    launch_topk<8>(in, bias, T, (int)N, k, mode, renorm, vals, idx, rmap, probs, s);
+    launch_topk<8>(in, bias, perm, T, (int)N, k, mode, renorm, vals, idx, rmap, probs, s);
   else if (vpl <= 16)
-    launch_topk<16>(in, bias, T, (int)N, k, mode, renorm, vals, idx, rmap, probs, s);
+    launch_topk<16>(in, bias, perm, T, (int)N, k, mode, renorm, vals, idx, rmap, probs, s);
   else if (vpl <= 32)
-    launch_topk<32>(in, bias, T, (int)N, k, mode, renorm, vals, idx, rmap, probs, s);
+    launch_topk<32>(in, bias, perm, T, (int)N, k, mode, renorm, vals, idx, rmap, probs, s);
   else
-    launch_topk<64>(in, bias, T, (int)N, k, mode, renorm, vals, idx, rmap, probs, s);
+    launch_topk<64>(in, bias, perm, T, (int)N, k, mode, renorm, vals, idx, rmap, probs, s);
   MOE_CUDA_CHECK_LAUNCH("topk launch");
   return MOE_OK;
 }
@@ -507,7 +510,7 @@ using namespace moe;
 extern "C" int moe_topk_f32(const float* input, float* values, int64_t* indices, int64_t M,
                             int64_t N, int32_t k, moe_stream_t stream) {
   MOE_REQUIRE(values != nullptr && indices != nullptr, "topk: null output");
-  return run_topk(input, nullptr, M, N, k, 0, 0, values, indices, nullptr, nullptr,
+  return run_topk(input, nullptr, nullptr, M, N, k, 0, 0, values, indices, nullptr, nullptr,
                   reinterpret_cast<cudaStream_t>(stream));
 }
 
@@ -517,8 +520,20 @@ extern "C" int moe_router_topk(const float* logits, const float* bias, int64_t T
                                moe_stream_t stream) {
   MOE_REQUIRE(score_mode == 0 || score_mode == 1, "router: score_mode must be 0 or 1");
   const int mode = score_mode == 1 ? 1 : 2;
-  return run_topk(logits, bias, T, E, k, mode, renorm, topk_vals, topk_idx, routing_map, probs,
-                  reinterpret_cast<cudaStream_t>(stream));
+  return run_topk(logits, bias, nullptr, T, E, k, mode, renorm, topk_vals, topk_idx, routing_map,
+                  probs, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int moe_router_topk_placed(const float* logits, const float* bias,
+                                      const int32_t* placement, int64_t T, int64_t E, int32_t k,
+                                      int32_t score_mode, int32_t renorm, float* topk_vals,
+                                      int64_t* topk_idx, uint8_t* routing_map, float* probs,
+                                      moe_stream_t stream) {
+  MOE_REQUIRE(score_mode == 0 || score_mode == 1, "router_placed: score_mode must be 0 or 1");
+  MOE_REQUIRE(placement != nullptr || T == 0, "router_placed: null placement");
+  const int mode = score_mode == 1 ? 1 : 2;
+  return run_topk(logits, bias, placement, T, E, k, mode, renorm, topk_vals, topk_idx,
+                  routing_map, probs, reinterpret_cast<cudaStream_t>(stream));
 }
 
 static size_t rim_ws_bytes(int64_t T, int64_t E) {

@@ -41,6 +41,8 @@ _SIGNATURES = {
     "moe_topk_f32": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int32, c_void_p],
     "moe_router_topk": [c_void_p, c_void_p, c_int64, c_int64, c_int32, c_int32, c_int32,
                         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
+    "moe_router_topk_placed": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int32, c_int32,
+                               c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
     "moe_row_id_map_workspace_size": [c_int64, c_int64, POINTER(c_size_t)],
     "moe_row_id_map": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                        c_void_p, c_void_p, c_size_t, c_void_p],
@@ -65,16 +67,21 @@ _SIGNATURES = {
     "moe_ipc_open_handle": [c_void_p, POINTER(c_void_p)],
     "moe_ipc_close_handle": [c_void_p],
     "moe_copy_async": [c_void_p, c_void_p, c_size_t, c_void_p],
+    "moe_ep_dispatch": [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int64,
+                        c_int64, c_int64, c_int64, c_int64, c_void_p],
+    "moe_ep_combine": [c_void_p, c_void_p, c_int32, c_int32, c_int64, c_void_p, c_void_p,
+                       c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p],
 }
 _RESTYPE = {"moe_b200_last_error": c_char_p}
 
 EXPORTED = tuple(_SIGNATURES)
 
 # Kernels each successful call launches (for the bench's launch count).
-_LAUNCHES = {"moe_topk_f32": 1, "moe_router_topk": 1, "moe_row_id_map": 3,
+_LAUNCHES = {"moe_topk_f32": 1, "moe_router_topk": 1, "moe_router_topk_placed": 1,
+             "moe_row_id_map": 3,
              "moe_row_id_map_static_scratch": 3,
              "moe_permute_mask_map": 1, "moe_permute_mask_map_trans": 1, "moe_unpermute_mask": 1,
-             "moe_unpermute_mask_token_major": 1,
+             "moe_unpermute_mask_token_major": 1, "moe_ep_dispatch": 1, "moe_ep_combine": 1,
              "moe_grouped_gemm_plan_splits": 1, "moe_grouped_gemm_plan_ep": 1,
              "moe_grouped_gemm": 1, "moe_swiglu": 1}
 launch_count = 0

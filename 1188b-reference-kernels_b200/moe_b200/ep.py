@@ -90,6 +90,28 @@ class EPDispatcher:
         return self._rows_a2a(y, recv_splits, send_splits, out)
 
 
+def balanced_placement(load: Sequence[float], world: int) -> List[int]:
+    """Expert placement with exactly E/world experts per rank and balanced load.
+
+    Greedy longest-processing-time: experts in decreasing load go to the rank
+    with the least load that still has a free slot. Returns the model expert
+    ids in slot order (rank r owns slots [r*E/world, (r+1)*E/world)), each
+    rank's experts in ascending id order.
+    """
+    e = len(load)
+    if e % world:
+        raise ValueError(f"{e} experts do not split evenly over {world} ranks")
+    per = e // world
+    order = sorted(range(e), key=lambda i: (-float(load[i]), i))
+    bins = [[] for _ in range(world)]
+    tot = [0.0] * world
+    for i in order:
+        d = min((r for r in range(world) if len(bins[r]) < per), key=lambda r: (tot[r], r))
+        bins[d].append(i)
+        tot[d] += float(load[i])
+    return [i for b in bins for i in sorted(b)]
+
+
 def ep_group_table(recv_counts, num_src: int, num_w: int):
     """Host restatement of the device group table for a receive buffer of
     (source rank, local expert) segments, groups ordered expert-major:
@@ -160,7 +182,13 @@ class EPPeerExchange:
     """
 
     def __init__(self, num_experts: int, tokens: int, hidden: int, topk: int,
-                 device: torch.device, group: Optional[dist.ProcessGroup] = None):
+                 device: torch.device, group: Optional[dist.ProcessGroup] = None,
+                 fused: bool = False):
+        """fused=False: receive + return buffers, rows moved by copy engines.
+        fused=True: receive + fc2-output buffers; the dispatch kernel stores
+        rows into the peers' receive buffers and the combine kernel loads the
+        results from the peers' fc2 outputs."""
+        self.fused = fused
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -171,15 +199,21 @@ class EPPeerExchange:
         self.rows_cap = tokens * topk
         self.row_bytes = hidden * 2
         self.device = torch.device(device)
-        self.recv_buf = torch.empty((self.world * self.rows_cap, hidden), dtype=torch.bfloat16,
+        self.recv_cap = self.world * self.rows_cap
+        self.recv_buf = torch.empty((self.recv_cap, hidden), dtype=torch.bfloat16,
                                     device=self.device)
-        self.ret_buf = torch.empty((self.rows_cap, hidden), dtype=torch.bfloat16,
-                                   device=self.device)
         self.side = [torch.cuda.Stream(self.device) for _ in range(self.world)]
         self.flag = torch.zeros(1, dtype=torch.float32, device=self.device)
         self._opened: List[int] = []
         self.peer_recv = self._share(self.recv_buf)
-        self.peer_ret = self._share(self.ret_buf)
+        if fused:
+            self.y_buf = torch.empty((self.recv_cap, hidden), dtype=torch.bfloat16,
+                                     device=self.device)
+            self.peer_y = self._share(self.y_buf)
+        else:
+            self.ret_buf = torch.empty((self.rows_cap, hidden), dtype=torch.bfloat16,
+                                       device=self.device)
+            self.peer_ret = self._share(self.ret_buf)
 
     def _share(self, t: torch.Tensor) -> List[int]:
         lib = _lib.load()
@@ -251,6 +285,42 @@ class EPPeerExchange:
         self._copies(jobs)
         return self.ret_buf[:sum(plan.send)]
 
+    def barrier(self) -> None:
+        """Stream-ordered barrier: returns (on the device) once every rank's
+        earlier work on its stream has finished."""
+        dist.all_reduce(self.flag, group=self.group)
+
+    def _table(self, ptrs: List[int], plan: ExchangePlan):
+        n = self.world
+        bases = (ctypes.c_int64 * n)(*ptrs)
+        deltas = (ctypes.c_int64 * n)(*[plan.dst_off[d] - plan.send_off[d] for d in range(n)])
+        for d in range(n):
+            if plan.dst_off[d] + plan.send[d] > self.recv_cap:
+                raise ValueError("exchange exceeds a receive buffer")
+        return bases, deltas
+
+    def fused_dispatch(self, x: torch.Tensor, map_te: torch.Tensor, plan: ExchangePlan) -> torch.Tensor:
+        """Permutes x straight into the owners' receive buffers, then barriers."""
+        t, h = x.shape
+        bases, deltas = self._table(self.peer_recv, plan)
+        _lib.call("moe_ep_dispatch", x.data_ptr(), map_te.data_ptr(), bases, deltas, self.world,
+                  self.local_experts, self.recv_cap, t, h, self.num_experts, sum(plan.send),
+                  torch.cuda.current_stream(self.device).cuda_stream)
+        self.barrier()
+        return self.recv_buf[:sum(plan.recv)]
+
+    def fused_combine(self, map_te: torch.Tensor, probs: Optional[torch.Tensor], plan: ExchangePlan,
+                      tokens: int, hidden: int) -> torch.Tensor:
+        """Weighted combine reading every result row from the rank that made it
+        (call after every rank's fc2 wrote into y_buf and barrier())."""
+        bases, deltas = self._table(self.peer_y, plan)
+        out = torch.empty((tokens, hidden), dtype=torch.bfloat16, device=self.device)
+        _lib.call("moe_ep_combine", bases, deltas, self.world, self.local_experts, self.recv_cap,
+                  map_te.data_ptr(), None if probs is None else probs.data_ptr(), out.data_ptr(),
+                  tokens, hidden, self.num_experts, sum(plan.send),
+                  torch.cuda.current_stream(self.device).cuda_stream)
+        return out
+
     def close(self) -> None:
         if self._opened:
             torch.cuda.synchronize(self.device)
@@ -269,18 +339,24 @@ class MoELayerEP:
     def __init__(self, local_weights: MoEWeights, num_experts: int, topk: int = 8,
                  renorm: bool = True, expert_bias: Optional[torch.Tensor] = None,
                  group: Optional[dist.ProcessGroup] = None, transport: str = "nccl",
-                 tokens: Optional[int] = None):
+                 tokens: Optional[int] = None, placement: Optional[torch.Tensor] = None):
         """transport "nccl": all_to_all_single of counts and rows; "peer": IPC-mapped
-        buffers filled by copy-engine pushes (needs `tokens`, the per-rank T)."""
+        buffers filled by copy-engine pushes; "fused": the dispatch and combine
+        kernels store / load rows in the peers' buffers directly. "peer" and
+        "fused" need `tokens`, the per-rank T. placement (int32 [E] permutation):
+        slot c is model expert placement[c]; this rank holds the weights of
+        slots [rank*E_loc, (rank+1)*E_loc) (e.g. from balanced_placement)."""
+        self.placement = placement
         self.disp = EPDispatcher(num_experts, group)
         self.peer = None
-        if transport == "peer":
+        self.fused = transport == "fused"
+        if transport in ("peer", "fused"):
             if tokens is None:
-                raise ValueError("transport='peer' needs the per-rank token count")
+                raise ValueError(f"transport='{transport}' needs the per-rank token count")
             self.peer = EPPeerExchange(num_experts, tokens, local_weights.hidden, topk,
-                                       local_weights.w1.device, group)
+                                       local_weights.w1.device, group, fused=self.fused)
         elif transport != "nccl":
-            raise ValueError("transport must be 'nccl' or 'peer'")
+            raise ValueError("transport must be 'nccl', 'peer' or 'fused'")
         if local_weights.num_experts != self.disp.local_experts:
             raise ValueError("local weights do not match num_experts / world size")
         self.w = local_weights
@@ -301,8 +377,11 @@ class MoELayerEP:
         if logits.shape != (t, e):
             raise ValueError(f"logits must be [{t},{e}]")
         self._ev("start")
-        r = ops.router_topk(logits, self.k, "softmax", self.renorm, self.bias, outputs="maps")
+        r = ops.router_topk(logits, self.k, "softmax", self.renorm, self.bias, outputs="maps",
+                            placement=self.placement)
         rim = ops.row_id_map(r.routing_map, align=1, want_et=False)
+        if self.fused:
+            return self._forward_fused(x, r, rim)
         xp, _ = ops.permute(x, rim.map_te, None, num_out=t * self.k)
         self._ev("local_dispatch")
         if self.peer is not None:
@@ -323,6 +402,24 @@ class MoELayerEP:
             yb = self.disp.combine(y, send, recv)
         self._ev("a2a_combine")
         out = ops.unpermute(yb, rim.map_te, r.probs, probs_mode="dense", token_major=True)
+        self._ev("combine")
+        return out
+
+    def _forward_fused(self, x, r, rim):
+        t, h = x.shape
+        self._ev("local_dispatch")
+        plan, recv_counts = self.peer.exchange_counts(rim.counts)
+        xr = self.peer.fused_dispatch(x, rim.map_te, plan)
+        self._ev("a2a_dispatch")
+        self.plan.from_ep_counts(recv_counts, self.disp.world, self.disp.local_experts)
+        hmid = ops.grouped_gemm(xr, self.w.w1, epilogue="swiglu", plan=self.plan)
+        self._ev("fc1")
+        y = ops.grouped_gemm(hmid, self.w.w2, plan=self.plan,
+                             out=self.peer.y_buf[:xr.shape[0]])
+        self._ev("fc2")
+        self.peer.barrier()
+        self._ev("a2a_combine")
+        out = self.peer.fused_combine(rim.map_te, r.probs, plan, t, h)
         self._ev("combine")
         return out
 

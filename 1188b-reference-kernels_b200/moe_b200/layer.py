@@ -62,11 +62,15 @@ class MoELayer:
     """Forward of one MoE expert layer on one GPU (inputs already on device)."""
 
     def __init__(self, weights: MoEWeights, topk: int = 8, renorm: bool = True,
-                 expert_bias: Optional[torch.Tensor] = None):
+                 expert_bias: Optional[torch.Tensor] = None,
+                 placement: Optional[torch.Tensor] = None):
+        """placement (optional int32 [E] permutation): weights[c] is model expert
+        placement[c]; routing, permuted rows and the combine order follow slots."""
         self.w = weights
         self.k = int(topk)
         self.renorm = renorm
         self.bias = expert_bias
+        self.placement = placement
         e = weights.num_experts
         self.plan = ops.GroupedGemmPlan(e, weights.w1.device)
         self.events = None  # optional dict name -> torch.cuda.Event for stage timing
@@ -83,7 +87,8 @@ class MoELayer:
         if h != self.w.hidden:
             raise ValueError(f"x hidden {h} != weights hidden {self.w.hidden}")
         self._ev("start")
-        r = ops.router_topk(logits, self.k, "softmax", self.renorm, self.bias, outputs="maps")
+        r = ops.router_topk(logits, self.k, "softmax", self.renorm, self.bias, outputs="maps",
+                            placement=self.placement)
         rim = ops.row_id_map(r.routing_map, align=1, want_et=False)
         self._ev("routing")
         rows = t * self.k
@@ -133,11 +138,7 @@ class HostPipeline:
         self._used = [False] * depth
         self._n = 0
 
-    def submit(self, x_host: torch.Tensor, logits_host: torch.Tensor,
-               out_host: torch.Tensor) -> torch.cuda.Event:
-        """Enqueues one step; returns the event that marks its output on the host."""
-        s = self._n % self.depth
-        self._n += 1
+    def _upload(self, s: int, x_host: torch.Tensor, logits_host: torch.Tensor) -> None:
         with torch.cuda.stream(self.up):
             if self._used[s]:
                 self.up.wait_event(self.consumed[s])
@@ -145,6 +146,8 @@ class HostPipeline:
             self.lg[s].copy_(logits_host, non_blocking=True)
             self.uploaded[s].record(self.up)
         self._used[s] = True
+
+    def _compute_download(self, s: int, out_host: torch.Tensor) -> torch.cuda.Event:
         with torch.cuda.stream(self.compute):
             self.compute.wait_event(self.uploaded[s])
             out = self.layer(self.x[s], self.lg[s])
@@ -155,6 +158,36 @@ class HostPipeline:
             out.record_stream(self.down)
             self.done[s].record(self.down)
         return self.done[s]
+
+    def submit(self, x_host: torch.Tensor, logits_host: torch.Tensor,
+               out_host: torch.Tensor) -> torch.cuda.Event:
+        """Enqueues one step; returns the event that marks its output on the host."""
+        s = self._n % self.depth
+        self._n += 1
+        self._upload(s, x_host, logits_host)
+        return self._compute_download(s, out_host)
+
+    def run(self, steps) -> None:
+        """Runs a sequence of (x_host, logits_host, out_host) steps, queueing the
+        upload of step i+1 before step i's kernels, so the upload overlaps even
+        layers that synchronise with the host mid-forward (the expert-parallel
+        layer reads its split sizes)."""
+        steps = list(steps)
+        if not steps:
+            return
+        slots = []
+        for i, (xh, lh, _) in enumerate(steps):
+            if i == 0:
+                s = self._n % self.depth
+                self._n += 1
+                self._upload(s, xh, lh)
+                slots.append(s)
+            if i + 1 < len(steps):
+                s = self._n % self.depth
+                self._n += 1
+                self._upload(s, steps[i + 1][0], steps[i + 1][1])
+                slots.append(s)
+            self._compute_download(slots[i], steps[i][2])
 
     def synchronize(self) -> None:
         self.down.synchronize()

@@ -75,7 +75,8 @@ class RouterOutput(NamedTuple):
 
 
 def router_topk(logits: torch.Tensor, k: int, score: str = "softmax", renorm: bool = True,
-                bias: Optional[torch.Tensor] = None, outputs: str = "all") -> RouterOutput:
+                bias: Optional[torch.Tensor] = None, outputs: str = "all",
+                placement: Optional[torch.Tensor] = None) -> RouterOutput:
     """Fused router: (logits + bias) -> top-k -> gates -> routing map + probs.
 
     score="softmax": gates are softmax probabilities (renormalised over the k
@@ -83,6 +84,8 @@ def router_topk(logits: torch.Tensor, k: int, score: str = "softmax", renorm: bo
     (case23 semantics). The selection follows the logits, which orders the
     experts exactly as their softmax probabilities do.
     outputs="all" or "maps" (skip topk_vals/topk_idx).
+    placement (int32 [E] permutation on the device): output column c is
+    model expert placement[c] (see moe_router_topk_placed).
     """
     _need_cuda("logits", logits)
     _need_dtype("logits", logits, torch.float32)
@@ -105,8 +108,19 @@ def router_topk(logits: torch.Tensor, k: int, score: str = "softmax", renorm: bo
         ti = torch.empty((t, k), dtype=torch.int64, device=dev)
     rmap = torch.empty((t, e), dtype=torch.bool, device=dev)
     probs = torch.empty((t, e), dtype=torch.float32, device=dev)
-    _lib.call("moe_router_topk", _p(lg), _p(bias), t, e, int(k), 1 if score == "softmax" else 0,
-              1 if renorm else 0, _p(tv), _p(ti), _p(rmap), _p(probs), _stream(dev))
+    if placement is None:
+        _lib.call("moe_router_topk", _p(lg), _p(bias), t, e, int(k),
+                  1 if score == "softmax" else 0, 1 if renorm else 0, _p(tv), _p(ti), _p(rmap),
+                  _p(probs), _stream(dev))
+    else:
+        _need_cuda("placement", placement)
+        _need_dtype("placement", placement, torch.int32)
+        if placement.shape != (e,):
+            raise ValueError(f"placement must be [{e}]")
+        pl = placement.contiguous()
+        _lib.call("moe_router_topk_placed", _p(lg), _p(bias), _p(pl), t, e, int(k),
+                  1 if score == "softmax" else 0, 1 if renorm else 0, _p(tv), _p(ti), _p(rmap),
+                  _p(probs), _stream(dev))
     return RouterOutput(tv, ti, rmap, probs)
 
 

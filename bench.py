@@ -57,8 +57,12 @@ def parse_args():
                     help="token sample of the CPU baseline (per step for --impl reference)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
-    ap.add_argument("--transport", choices=["peer", "nccl"], default="peer",
-                    help="EP row exchange: IPC-mapped buffers + copy engines, or NCCL all-to-all")
+    ap.add_argument("--placement", choices=["balanced", "contiguous"], default="balanced",
+                    help="EP expert placement: load-balanced (E/G experts per GPU, chosen from "
+                         "the routing of the benchmark's own logits) or contiguous id ranges")
+    ap.add_argument("--transport", choices=["fused", "peer", "nccl"], default="fused",
+                    help="EP row exchange: dispatch/combine kernels on peer memory, "
+                         "IPC-mapped buffers + copy engines, or NCCL all-to-all")
     return ap.parse_args()
 
 
@@ -75,7 +79,7 @@ def config_dict(a, world):
             "tokens_per_gpu": a.tokens, "hidden": a.hidden, "experts": a.experts,
             "topk": a.topk, "ffn": a.ffn, "routing": a.routing,
             "parallelism": f"ep{world}" if world > 1 else "single",
-            **({"ep_transport": a.transport} if world > 1 else {}),
+            **({"ep_transport": a.transport, "ep_placement": a.placement} if world > 1 else {}),
             "l2": "no flush: every step streams >22 GB of expert weights and 0.25 GB of "
                   "activations, both larger than the 126 MB L2"}
 
@@ -292,8 +296,17 @@ def main():
         layer = moe_b200.MoELayer(w, topk=k, expert_bias=bias)
         stage_names = ["start", "routing", "permute", "fc1", "fc2", "combine"]
     else:
-        from moe_b200.ep import MoELayerEP
-        layer = MoELayerEP(w, e, topk=k, expert_bias=bias, transport=a.transport, tokens=t)
+        from moe_b200.ep import MoELayerEP, balanced_placement
+        placement = None
+        if a.placement == "balanced":
+            # Calibration (untimed): expert loads of this job's routing, summed over ranks.
+            r0 = moe_b200.router_topk(logits, k, "softmax", True, bias, outputs="maps")
+            load = r0.routing_map.sum(0, dtype=torch.int64)
+            dist.all_reduce(load)
+            placement = torch.tensor(balanced_placement(load.cpu().tolist(), world),
+                                     dtype=torch.int32, device=dev)
+        layer = MoELayerEP(w, e, topk=k, expert_bias=bias, transport=a.transport, tokens=t,
+                           placement=placement)
         stage_names = ["start", "local_dispatch", "a2a_dispatch", "fc1", "fc2", "a2a_combine",
                        "combine"]
 
@@ -363,8 +376,7 @@ def main():
         e0 = torch.cuda.Event(enable_timing=True)
         e1 = torch.cuda.Event(enable_timing=True)
         e0.record(pipe.up)
-        for i in range(a.steps):
-            pipe.submit(x_h, lg_h, outs_h[i % 2])
+        pipe.run([(x_h, lg_h, outs_h[i % 2]) for i in range(a.steps)])
         e1.record(pipe.down)
         torch.cuda.synchronize()
         barrier()
@@ -376,7 +388,7 @@ def main():
         e2e = {"value": world * t / (e2e_ms / 1e3), "unit": UNIT,
                "h2d_bytes_per_step": x.numel() * 2 + logits.numel() * 4,
                "d2h_bytes_per_step": t * h * 2, "ms_per_step": e2e_ms,
-               "api": "moe_b200.HostPipeline.submit (copies overlapped with compute)"}
+               "api": "moe_b200.HostPipeline.run (copies overlapped with compute)"}
 
     clocks = sampler.stop()
     peaks, peak_kind = load_peaks()

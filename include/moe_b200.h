@@ -68,6 +68,16 @@ int moe_router_topk(const float* logits, const float* bias, int64_t T, int64_t E
                     int32_t score_mode, int32_t renorm, float* topk_vals, int64_t* topk_idx,
                     uint8_t* routing_map, float* probs, moe_stream_t stream);
 
+/* Router over a placement of the experts: slot c of every output (routing  */
+/* map, probs and topk_idx columns) is model expert placement[c] (an int32   */
+/* permutation of [0,E) on the device), so experts placed on one GPU get     */
+/* contiguous slots and contiguous permuted rows. Ties rank the lower slot   */
+/* first. Same arithmetic as moe_router_topk otherwise.                      */
+int moe_router_topk_placed(const float* logits, const float* bias, const int32_t* placement,
+                           int64_t T, int64_t E, int32_t k, int32_t score_mode, int32_t renorm,
+                           float* topk_vals, int64_t* topk_idx, uint8_t* routing_map,
+                           float* probs, moe_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* a3  routing_map [T,E] bool -> row_id_map, expert-major destinations:      */
 /*   row[t,e] = base[e] + #{t' <= t : map[t',e]} - 1 if map[t,e] else -1     */
@@ -192,6 +202,24 @@ int moe_ipc_open_handle(const void* handle, void** base_out);
 int moe_ipc_close_handle(void* base);
 /* Asynchronous device-to-device copy (either side may be a peer mapping).   */
 int moe_copy_async(void* dst, const void* src, size_t bytes, moe_stream_t stream);
+
+/* Fused dispatch: permute x by the token-major map, writing the row of      */
+/* (t, e) straight into rank d = e / experts_per_rank's buffer at row        */
+/* map[t,e] + peer_deltas[d] (peer_bases: this process's address of every    */
+/* rank's buffer, host arrays of `ranks` entries, ranks <= 8). Rows outside  */
+/* [0, cap_rows) of the target buffer are skipped.                           */
+int moe_ep_dispatch(const void* x, const int64_t* row_id_map_te, const int64_t* peer_bases,
+                    const int64_t* peer_deltas, int32_t ranks, int32_t experts_per_rank,
+                    int64_t cap_rows, int64_t T, int64_t H, int64_t E, int64_t num_rows,
+                    moe_stream_t stream);
+/* Fused combine: out[t] = bf16(sum over e ascending of probs[t,e] * row),   */
+/* each row read from rank e / experts_per_rank's buffer at map[t,e] +       */
+/* peer_deltas[d]; probs null = unweighted. Same arithmetic as               */
+/* moe_unpermute_mask_token_major. E <= 1024.                                */
+int moe_ep_combine(const int64_t* peer_bases, const int64_t* peer_deltas, int32_t ranks,
+                   int32_t experts_per_rank, int64_t cap_rows, const int64_t* row_id_map_te,
+                   const float* probs, void* out, int64_t T, int64_t H, int64_t E,
+                   int64_t num_rows, moe_stream_t stream);
 
 #ifdef __cplusplus
 }

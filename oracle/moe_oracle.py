@@ -70,7 +70,7 @@ def topk(inp: np.ndarray, k: int):
 
 
 def router(logits: np.ndarray, k: int, bias: np.ndarray | None = None, score: str = "softmax",
-           renorm: bool = True):
+           renorm: bool = True, placement: np.ndarray | None = None):
     """Router: softmax over experts, top-k, optional renormalisation.
 
     No reference function computes this (the reference's router case23 is the
@@ -82,6 +82,8 @@ def router(logits: np.ndarray, k: int, bias: np.ndarray | None = None, score: st
     lg = np.asarray(logits, dtype=np.float32)
     if bias is not None:
         lg = (lg + np.asarray(bias, dtype=np.float32)[None, :]).astype(np.float32)
+    if placement is not None:  # slot c holds model expert placement[c]
+        lg = np.ascontiguousarray(lg[:, np.asarray(placement)])
     _, idx = topk(lg, k)
     if score == "softmax":
         m = lg.max(axis=1, keepdims=True)
@@ -253,12 +255,14 @@ def grouped_gemm(x_u16: np.ndarray, w_u16: np.ndarray, m_splits, epilogue: str =
 # --------------------------------------------------------------------------- layer
 
 
-def moe_layer(x_u16, logits, w1_u16, w2_u16, k, bias=None, renorm=True, tokens=None):
+def moe_layer(x_u16, logits, w1_u16, w2_u16, k, bias=None, renorm=True, tokens=None,
+              placement=None):
     """Full expert-layer forward: router -> row_id_map -> permute -> fc1+SwiGLU
-    -> fc2 -> weighted combine. Returns out bf16 bits [T',H] for `tokens`."""
+    -> fc2 -> weighted combine. Returns out bf16 bits [T',H] for `tokens`.
+    With a placement, w1/w2 are in slot order (w[c] = model expert placement[c])."""
     t = x_u16.shape[0]
     e = w1_u16.shape[0]
-    _, _, rmap, probs = router(logits, k, bias, "softmax", renorm)
+    _, _, rmap, probs = router(logits, k, bias, "softmax", renorm, placement)
     map_et, map_te, counts, num_out = row_id_map(rmap)
     xp, _ = permute(x_u16, map_te, None, num_out)
     h = grouped_gemm(xp, w1_u16, counts, "swiglu")

@@ -50,3 +50,21 @@ def test_exchange_plan_matches_all_to_all(world, experts, seed):
             ret[s][p.back_off[s]:p.back_off[s] + p.recv[s]] = blk
     for r in range(world):
         np.testing.assert_array_equal(ret[r], xp[r])
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_balanced_placement(world):
+    from moe_b200.ep import balanced_placement
+    rng = np.random.default_rng(world)
+    e = 256
+    load = (rng.pareto(1.5, e) * 100).astype(int)
+    pl = balanced_placement(load.tolist(), world)
+    assert sorted(pl) == list(range(e))
+    per = e // world
+    tot = [sum(load[pl[r * per:(r + 1) * per]]) for r in range(world)]
+    contig = [sum(load[r * per:(r + 1) * per]) for r in range(world)]
+    assert max(tot) <= max(contig)
+    # LPT bound: the heaviest rank exceeds the mean by at most the largest single expert
+    assert max(tot) - np.mean(tot) <= load.max() + 1e-9
+    for r in range(world):
+        assert pl[r * per:(r + 1) * per] == sorted(pl[r * per:(r + 1) * per])

@@ -37,7 +37,7 @@ def _problem(world, t, h, e, f, routing):
     return x, lg, bias, w1, w2
 
 
-def _worker(rank, world, port, routing, transport, q):
+def _worker(rank, world, port, routing, transport, q, placed=False):
     for p in (str(PKG), str(ROOT), str(GOLDEN)):
         if p not in sys.path:
             sys.path.insert(0, p)
@@ -54,10 +54,16 @@ def _worker(rank, world, port, routing, transport, q):
         x, lg, bias, w1, w2 = _problem(world, t, h, e, f, routing)
         el = e // world
         sl = slice(rank * t, (rank + 1) * t)
+        pl = torch.arange(e, dtype=torch.int32)
+        if placed:
+            from moe_b200.ep import balanced_placement
+            load = torch.bincount(torch.topk(lg + bias, k, dim=1).indices.reshape(-1), minlength=e)
+            pl = torch.tensor(balanced_placement(load.tolist(), world), dtype=torch.int32)
+        w1, w2 = w1[pl.long()], w2[pl.long()]  # slot order
         local = moe_b200.MoEWeights(w1[rank * el:(rank + 1) * el].to(dev).contiguous(),
                                     w2[rank * el:(rank + 1) * el].to(dev).contiguous())
         layer = MoELayerEP(local, e, topk=k, expert_bias=bias.to(dev), transport=transport,
-                           tokens=t)
+                           tokens=t, placement=pl.to(dev) if placed else None)
         out = layer(x[sl].to(dev), lg[sl].to(dev))
         out2 = layer(x[sl].to(dev), lg[sl].to(dev))  # buffers reused across forwards
         assert torch.equal(out, out2)
@@ -67,7 +73,8 @@ def _worker(rank, world, port, routing, transport, q):
         ok = None
         if rank == 0:
             full = moe_b200.MoELayer(moe_b200.MoEWeights(w1.to(dev), w2.to(dev)), topk=k,
-                                     expert_bias=bias.to(dev))
+                                     expert_bias=bias.to(dev),
+                                     placement=pl.to(dev) if placed else None)
             ref = full(x.to(dev), lg.to(dev))
             ok = bool(torch.equal(torch.cat(outs), ref))
         layer.close()
@@ -80,7 +87,11 @@ def _worker(rank, world, port, routing, transport, q):
 
 @pytest.mark.parametrize("world,routing,transport", [(2, "uniform", "nccl"), (2, "zipf", "nccl"),
                                                      (2, "zipf", "peer"), (2, "uniform", "peer"),
-                                                     (4, "zipf", "peer"), (4, "uniform", "nccl")])
+                                                     (2, "zipf", "fused"), (2, "uniform", "fused"),
+                                                     (4, "zipf", "peer"), (4, "uniform", "nccl"),
+                                                     (4, "zipf", "fused"), (4, "uniform", "fused"),
+                                                     (2, "zipf", "fused+placed"),
+                                                     (4, "zipf", "fused+placed")])
 def test_ep_equals_single_gpu(world, routing, transport):
     if not torch.cuda.is_available():
         pytest.fail("GPU test selected but no CUDA device is visible")
@@ -90,7 +101,10 @@ def test_ep_equals_single_gpu(world, routing, transport):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, routing, transport, q)) for r in range(world)]
+    placed = transport.endswith("+placed")
+    tr = transport.split("+")[0]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, routing, tr, q, placed))
+             for r in range(world)]
     for p in procs:
         p.start()
     res = sorted((q.get(timeout=300) for _ in range(world)), key=lambda r: r[0])

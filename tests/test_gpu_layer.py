@@ -63,3 +63,32 @@ def test_host_pipeline_matches_direct_calls(cuda_dev):
     for i in range(5):
         ref = layer(xs[i].to(cuda_dev), lgs[i].to(cuda_dev)).cpu()
         assert torch.equal(outs[i], ref), i
+    outs2 = [torch.empty(t, h, dtype=torch.bfloat16).pin_memory() for _ in range(5)]
+    pipe.run([(xs[i], lgs[i], outs2[i]) for i in range(5)])
+    pipe.synchronize()
+    for i in range(5):
+        assert torch.equal(outs2[i], outs[i]), i
+
+
+def test_layer_with_placement(cuda_dev):
+    """Placed layer (weights in slot order) vs the oracle with the same placement."""
+    import moe_b200
+    t, h, e, f, k = 512, 512, 32, 256, 8
+    g = torch.Generator().manual_seed(21)
+    x = torch.randn(t, h, generator=g).to(torch.bfloat16)
+    lg = torch.randn(t, e, generator=g)
+    bias = -1.5 * torch.log(torch.randperm(e, generator=g).float() + 1)
+    w1 = (torch.randn(e, 2 * f, h, generator=g) * 0.03).to(torch.bfloat16)
+    w2 = (torch.randn(e, h, f, generator=g) * 0.03).to(torch.bfloat16)
+    pl = torch.randperm(e, generator=g).to(torch.int32)
+    layer = moe_b200.MoELayer(moe_b200.MoEWeights(w1[pl.long()].to(cuda_dev),
+                                                  w2[pl.long()].to(cuda_dev)),
+                              topk=k, expert_bias=bias.to(cuda_dev), placement=pl.to(cuda_dev))
+    out, mid = layer.forward(x.to(cuda_dev), lg.to(cuda_dev), return_intermediates=True)
+    _, _, rmap, _ = orc.router(lg.numpy(), k, bias.numpy(), placement=pl.numpy())
+    _, te, _, _ = orc.row_id_map(rmap)
+    np.testing.assert_array_equal(mid["rim"].map_te.cpu().numpy(), te)
+    ref = orc.moe_layer(u16(x), lg.numpy(), u16(w1[pl.long()]), u16(w2[pl.long()]), k,
+                        bias.numpy(), placement=pl.numpy())
+    np.testing.assert_allclose(orc.bf16_to_f32(u16(out)), orc.bf16_to_f32(ref), rtol=2e-2,
+                               atol=1e-2)

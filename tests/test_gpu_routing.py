@@ -146,3 +146,24 @@ def test_router_to_row_id_map_chain_cfg1(cuda_dev):
     assert num_out == 4096 * 8
     np.testing.assert_array_equal(m.map_te.cpu().numpy(), te)
     np.testing.assert_array_equal(m.map_et.cpu().numpy(), et)
+
+
+@pytest.mark.parametrize("t,e,k", [(2048, 256, 8), (333, 64, 4)])
+def test_router_with_placement(cuda_dev, t, e, k):
+    """Placed router: slot c reads model expert placement[c]; maps exact vs oracle."""
+    import moe_b200
+    g = torch.Generator().manual_seed(e + k)
+    lg = torch.randn(t, e, generator=g)
+    bias = -1.5 * torch.log(torch.randperm(e, generator=g).float() + 1)
+    pl = torch.randperm(e, generator=g).to(torch.int32)
+    r = moe_b200.router_topk(lg.to(cuda_dev), k, "softmax", True, bias.to(cuda_dev),
+                             placement=pl.to(cuda_dev))
+    gates, idx, rmap, probs = orc.router(lg.numpy(), k, bias.numpy(), "softmax", True,
+                                         placement=pl.numpy())
+    np.testing.assert_array_equal(r.topk_idx.cpu().numpy(), idx)
+    np.testing.assert_array_equal(r.routing_map.cpu().numpy(), rmap)
+    np.testing.assert_allclose(r.probs.cpu().numpy(), probs, rtol=1e-5, atol=1e-7)
+    # the same experts as the unplaced router, named by slot
+    r0 = moe_b200.router_topk(lg.to(cuda_dev), k, "softmax", True, bias.to(cuda_dev))
+    model_ids = pl.to(cuda_dev).long()[r.topk_idx]
+    assert torch.equal(torch.sort(model_ids, 1).values, torch.sort(r0.topk_idx, 1).values)
