@@ -428,12 +428,15 @@ constexpr uint32_t kPairABytes = 128 * BK * 2;            // 16 KB: this CTA's r
 constexpr uint32_t kPairBBytes = 128 * BK * 2;            // 16 KB: this CTA's half of B
 constexpr uint32_t kPairStageBytes = kPairABytes + kPairBBytes;   // 32 KB
 constexpr uint32_t kPairTxBytes = 2 * kPairStageBytes;    // both CTAs, on the leader's barrier
-constexpr size_t kPairSmemBytes = 1024 + kPairStages * kPairStageBytes + 256;
+constexpr uint32_t kEpiBoxBytes = 32 * 32 * 2;            // 32 rows x 32 bf16 columns
+constexpr uint32_t kEpiBytes = 4 * 2 * kEpiBoxBytes;        // 4 warps x 2 buffers = 16 KB
+constexpr size_t kPairSmemBytes = 1024 + kPairStages * kPairStageBytes + 1024 + kEpiBytes;
 }  // namespace pairk
 
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
-                             const __grid_constant__ CUtensorMap tmap_b, const Params p) {
+                             const __grid_constant__ CUtensorMap tmap_b,
+                             const __grid_constant__ CUtensorMap tmap_out, const Params p) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
@@ -602,12 +605,49 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue (both CTAs)
+    // Each warp owns 32 TMEM lanes (rows). When all 32 rows are inside the
+    // group, every 32-column chunk is staged in a 64B-swizzled shared buffer
+    // (conflict-free) and written by one TMA tile store; otherwise the rows
+    // are stored individually with row predicates.
     const int quad = warp & 3;  // TMEM lanes this warp may access: 32*quad ..
     const int r_in_cta = quad * 32 + lane;
     const uint32_t leader_tempty0 = map_to_rank(tempty_bar(0), 0);
     const uint32_t leader_tempty1 = map_to_rank(tempty_bar(1), 0);
+    const uint32_t epi_base = ((bar0 + 512u + 1023u) & ~1023u) + static_cast<uint32_t>(quad) * 2u * pairk::kEpiBoxBytes;
+    uint32_t chunk_no = 0;
     int it = 0;
     bool ok = true;
+    // One 32-row x 32-column chunk: packed bf16 pairs of this lane's row.
+    auto emit = [&](const uint32_t (&o)[16], bool tma, int64_t row, int col, int warp_row0,
+                    __nv_bfloat16* orow, bool rvalid) {
+      if (tma) {
+        const uint32_t buf = epi_base + (chunk_no & 1u) * pairk::kEpiBoxBytes;
+        ++chunk_no;
+        if (lane == 0) bulk_wait_read<1>();  // the store that used this buffer has read it
+        __syncwarp();
+        const uint32_t sw = static_cast<uint32_t>((lane >> 1) & 3);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          const uint32_t dst = buf + static_cast<uint32_t>(lane) * 64u + ((static_cast<uint32_t>(j) ^ sw) << 4);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(o[4 * j]),
+                       "r"(o[4 * j + 1]), "r"(o[4 * j + 2]), "r"(o[4 * j + 3])
+                       : "memory");
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) {
+          tma_store_2d(&tmap_out, col, warp_row0, buf);
+          bulk_commit();
+        }
+      } else if (rvalid) {
+#pragma unroll
+        for (int v = 0; v < 4; ++v)
+          if (col + v * 8 + 8 <= p.n_out)
+            *reinterpret_cast<uint4*>(orow + col + v * 8) =
+                make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+      }
+      (void)row;
+    };
     for (long long t = cid;; t += ncl) {
       Tile tile;
       if (!walker.locate(t, tile)) break;
@@ -621,6 +661,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m_local = tile.m_idx * pairk::kPairTileM + static_cast<int>(rank) * 128 + r_in_cta;
       const int64_t row = static_cast<int64_t>(p.row_start[tile.g]) + m_local;
       const bool rvalid = m_local < p.rows[tile.g] && row < p.x_rows;
+      const bool tma = __all_sync(0xffffffffu, rvalid);
+      const int warp_row0 = static_cast<int>(row) - lane;
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
       __nv_bfloat16* orow = p.out + row * p.n_out;
@@ -628,51 +670,37 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int n0 = tile.n_idx * BN;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
+          const int col = n0 + c * 32;
+          if (col >= p.n_out) break;  // warp-uniform
           uint32_t r[32];
           tmem_ld_32x32b_x32(tbase + c * 32, r);
           tmem_ld_wait();
-          if (rvalid) {
+          uint32_t o[16];
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              const int col = n0 + c * 32 + v * 8;
-              if (col + 8 <= p.n_out) {
-                uint4 o;
-                o.x = pack_bf16x2(__uint_as_float(r[v * 8 + 0]), __uint_as_float(r[v * 8 + 1]));
-                o.y = pack_bf16x2(__uint_as_float(r[v * 8 + 2]), __uint_as_float(r[v * 8 + 3]));
-                o.z = pack_bf16x2(__uint_as_float(r[v * 8 + 4]), __uint_as_float(r[v * 8 + 5]));
-                o.w = pack_bf16x2(__uint_as_float(r[v * 8 + 6]), __uint_as_float(r[v * 8 + 7]));
-                *reinterpret_cast<uint4*>(orow + col) = o;
-              }
-            }
-          }
+          for (int q = 0; q < 16; ++q)
+            o[q] = pack_bf16x2(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1]));
+          emit(o, tma, row, col, warp_row0, orow, rvalid);
         }
       } else {
         const int n0 = tile.n_idx * 128;
 #pragma unroll 1
         for (int c = 0; c < 128 / 32; ++c) {
+          const int col = n0 + c * 32;
+          if (col >= p.n_out) break;  // warp-uniform
           uint32_t gr[32], ur[32];
           tmem_ld_32x32b_x32(tbase + c * 32, gr);
           tmem_ld_32x32b_x32(tbase + 128 + c * 32, ur);
           tmem_ld_wait();
-          if (rvalid) {
+          uint32_t o[16];
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              const int col = n0 + c * 32 + v * 8;
-              if (col + 8 <= p.n_out) {
-                uint32_t o[4];
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                  const int j = v * 8 + 2 * q;
-                  const float h0 = swiglu_f32(round_bf16(__uint_as_float(gr[j])),
-                                              round_bf16(__uint_as_float(ur[j])));
-                  const float h1 = swiglu_f32(round_bf16(__uint_as_float(gr[j + 1])),
-                                              round_bf16(__uint_as_float(ur[j + 1])));
-                  o[q] = pack_bf16x2(h0, h1);
-                }
-                *reinterpret_cast<uint4*>(orow + col) = make_uint4(o[0], o[1], o[2], o[3]);
-              }
-            }
+          for (int q = 0; q < 16; ++q) {
+            const float h0 = swiglu_f32(round_bf16(__uint_as_float(gr[2 * q])),
+                                        round_bf16(__uint_as_float(ur[2 * q])));
+            const float h1 = swiglu_f32(round_bf16(__uint_as_float(gr[2 * q + 1])),
+                                        round_bf16(__uint_as_float(ur[2 * q + 1])));
+            o[q] = pack_bf16x2(h0, h1);
           }
+          emit(o, tma, row, col, warp_row0, orow, rvalid);
         }
       }
       tc_fence_before();
@@ -680,6 +708,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (lane == 0) mbar_arrive_cluster(acc == 0 ? leader_tempty0 : leader_tempty1);
       ++it;
     }
+    if (lane == 0) bulk_wait_all();  // every tile store has finished
+    __syncwarp();
     if (!ok && lane == 0) raise_abort(abort_flag, p.err, kErrTimeoutEpilogue);
   }
 
@@ -796,9 +826,18 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
+int make_tmap_box(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer,
+                  uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz);
+
 // 2-D bf16 tensor map over a row-major [outer, inner] matrix, box 64 x 128,
 // 128-byte swizzle (one box row = one 128-byte swizzle row).
 int make_tmap(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer) {
+  return make_tmap_box(m, ptr, inner, outer, static_cast<uint32_t>(BK), 128u,
+                       CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+int make_tmap_box(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer,
+                  uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
   auto encode = get_encode_fn();
   if (encode == nullptr) {
     set_last_error("grouped_gemm: cuTensorMapEncodeTiled unavailable");
@@ -806,12 +845,11 @@ int make_tmap(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer) {
   }
   cuuint64_t dims[2] = {inner, outer};
   cuuint64_t strides[1] = {inner * 2};
-  cuuint32_t box[2] = {static_cast<cuuint32_t>(BK), 128u};
+  cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1u, 1u};
   const CUresult r = encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
-                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     set_last_error("grouped_gemm: cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
     return MOE_ERR_CUDA;
@@ -997,6 +1035,10 @@ extern "C" int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t
   MOE_CUDA_CALL(cudaGetDevice(&dev), "cudaGetDevice");
   const int clusters = gg::pair_enabled() ? gg::pair_clusters(dev) : 0;
   if (clusters > 0) {
+    CUtensorMap to;
+    st = gg::make_tmap_box(&to, out, static_cast<uint64_t>(p.n_out), static_cast<uint64_t>(x_rows),
+                           32u, 32u, CU_TENSOR_MAP_SWIZZLE_64B);
+    if (st) return st;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters);
     cfg.blockDim = dim3(gg::kThreads);
@@ -1009,7 +1051,7 @@ extern "C" int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    MOE_CUDA_CALL(cudaLaunchKernelEx(&cfg, gg::grouped_gemm_pair_kernel, ta, tb, p),
+    MOE_CUDA_CALL(cudaLaunchKernelEx(&cfg, gg::grouped_gemm_pair_kernel, ta, tb, to, p),
                   "grouped_gemm pair launch");
     return MOE_OK;
   }

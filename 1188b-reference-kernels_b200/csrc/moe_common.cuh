@@ -9,7 +9,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
-#include "../../include/moe_b200.h"
+#include "moe_b200.h"
 
 #define MOE_DEVICE __device__ __forceinline__
 
@@ -135,6 +135,26 @@ MOE_DEVICE void tma_load_2d(uint32_t dst, const void* tmap, int32_t x, int32_t y
       " [%0], [%1, {%2, %3}], [%4], %5;" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(x), "r"(y), "r"(bar), "l"(policy)
       : "memory");
+}
+
+// TMA tile store from this CTA's shared memory (bulk async-group based).
+MOE_DEVICE void tma_store_2d(const void* tmap, int32_t x, int32_t y, uint32_t src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(x), "r"(y), "r"(src)
+               : "memory");
+}
+MOE_DEVICE void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// Waits until at most N committed bulk groups of this thread still read smem.
+template <int N>
+MOE_DEVICE void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+MOE_DEVICE void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy (TMA) reads of them.
+MOE_DEVICE void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 MOE_DEVICE uint64_t l2_policy_evict_last() {
