@@ -733,7 +733,10 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
                                                     int32_t* __restrict__ row_start,
                                                     int32_t* __restrict__ rows,
                                                     int32_t* __restrict__ widx,
-                                                    int32_t* __restrict__ tmp) {
+                                                    int32_t* __restrict__ tmp,
+                                                    int32_t* __restrict__ rows_body,
+                                                    int32_t* __restrict__ tail_start,
+                                                    int32_t* __restrict__ rows_tail) {
   __shared__ int64_t warp_sums[32];
   __shared__ int64_t carry_s;
   const int lane = lane_id(), wid = warp_id();
@@ -781,9 +784,16 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
       f = s * num_w + e;
       w = e;
     }
+    const int32_t m = max(counts[f], 0);
+    const int32_t body = (m / pairk::kPairTileM) * pairk::kPairTileM;
     row_start[g] = tmp[f];
-    rows[g] = max(counts[f], 0);
+    rows[g] = m;
     widx[g] = w;
+    // Whole 256-row tiles go to the CTA-pair kernel, the rest (< 256 rows) to
+    // the single-CTA kernel's 128-row tiles, which pads at most 127 rows.
+    rows_body[g] = body;
+    tail_start[g] = tmp[f] + body;
+    rows_tail[g] = m - body;
   }
 }
 
@@ -793,12 +803,15 @@ struct WsLayout {
   int32_t* rows;
   int32_t* widx;
   int32_t* tmp;
+  int32_t* rows_body;   // whole 256-row tiles of each group (CTA-pair kernel)
+  int32_t* tail_start;  // first row after them
+  int32_t* rows_tail;   // remaining rows (single-CTA kernel)
 };
 
 size_t ws_array_bytes(int64_t G) {
   return (static_cast<size_t>(G) * 4 + 255) & ~static_cast<size_t>(255);
 }
-size_t ws_bytes(int64_t G) { return 256 + 4 * ws_array_bytes(G); }
+size_t ws_bytes(int64_t G) { return 256 + 7 * ws_array_bytes(G); }
 
 WsLayout ws_layout(const void* ws, int64_t G) {
   char* b = static_cast<char*>(const_cast<void*>(ws));
@@ -809,6 +822,9 @@ WsLayout ws_layout(const void* ws, int64_t G) {
   l.rows = reinterpret_cast<int32_t*>(b + 256 + a);
   l.widx = reinterpret_cast<int32_t*>(b + 256 + 2 * a);
   l.tmp = reinterpret_cast<int32_t*>(b + 256 + 3 * a);
+  l.rows_body = reinterpret_cast<int32_t*>(b + 256 + 4 * a);
+  l.tail_start = reinterpret_cast<int32_t*>(b + 256 + 5 * a);
+  l.rows_tail = reinterpret_cast<int32_t*>(b + 256 + 6 * a);
   return l;
 }
 
@@ -951,7 +967,7 @@ extern "C" int moe_grouped_gemm_plan_splits(const int32_t* m_splits, int64_t G, 
   gg::WsLayout l = gg::ws_layout(workspace, G);
   gg::plan_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       m_splits, static_cast<int>(G), 0, 1, static_cast<int>(G), align, l.err, l.row_start, l.rows,
-      l.widx, l.tmp);
+      l.widx, l.tmp, l.rows_body, l.tail_start, l.rows_tail);
   MOE_CUDA_CHECK_LAUNCH("grouped_gemm plan");
   return MOE_OK;
 }
@@ -969,7 +985,7 @@ extern "C" int moe_grouped_gemm_plan_ep(const int32_t* counts, int64_t num_src, 
   gg::WsLayout l = gg::ws_layout(workspace, G);
   gg::plan_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       counts, static_cast<int>(G), 1, static_cast<int>(num_src), static_cast<int>(num_w), 1,
-      l.err, l.row_start, l.rows, l.widx, l.tmp);
+      l.err, l.row_start, l.rows, l.widx, l.tmp, l.rows_body, l.tail_start, l.rows_tail);
   MOE_CUDA_CHECK_LAUNCH("grouped_gemm plan_ep");
   return MOE_OK;
 }
@@ -1051,8 +1067,19 @@ extern "C" int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    MOE_CUDA_CALL(cudaLaunchKernelEx(&cfg, gg::grouped_gemm_pair_kernel, ta, tb, to, p),
+    static const bool split = gg::env_int("MOE_GEMM_SPLIT", 1, 0, 1) == 1;
+    gg::Params pb = p;
+    if (split) pb.rows = l.rows_body;
+    MOE_CUDA_CALL(cudaLaunchKernelEx(&cfg, gg::grouped_gemm_pair_kernel, ta, tb, to, pb),
                   "grouped_gemm pair launch");
+    if (!split) return MOE_OK;
+    // Remainders of every group (< 256 rows) on 128-row single-CTA tiles.
+    gg::Params pt = p;
+    pt.row_start = l.tail_start;
+    pt.rows = l.rows_tail;
+    gg::grouped_gemm_kernel<<<num_sms(dev), gg::kThreads, gg::kSmemBytes,
+                              reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, pt);
+    MOE_CUDA_CHECK_LAUNCH("grouped_gemm tail launch");
     return MOE_OK;
   }
   const int grid = num_sms(dev);
