@@ -1,7 +1,9 @@
 // Peer-memory plumbing for the expert-parallel exchange: CUDA IPC handles for
 // receive buffers and device-to-device copies that the copy engines execute.
-// Rows cross NVLink as plain DMA copies from this GPU into another GPU's
-// buffer; no kernel of this library reads or writes peer memory.
+// With the "peer" transport rows cross NVLink as plain DMA copies from this
+// GPU into another GPU's buffer; the fused dispatch/combine kernels
+// (ep_fused.cu) instead store to / load from the mapped peer buffers with
+// ordinary vector accesses (no TMA, no bulk copies).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <string.h>

@@ -256,7 +256,7 @@ def read_traffic():
     if not p.exists():
         return None
     for line in p.read_text().splitlines():
-        if line.startswith("dram_bytes_per_launch_full:"):
+        if line.startswith("dram_bytes_fc1_stage:"):
             try:
                 return float(line.split(":", 1)[1].split()[0])
             except ValueError:
@@ -397,7 +397,7 @@ def main():
     achieved = fc1_flops / (fc1_ms / 1e3) / 1e12
     peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
     hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
-    traffic = read_traffic()
+    traffic = read_traffic() if world == 1 else None  # captured at the single-GPU workload
     rows = fc1_rows
     perm_bytes = t * h * 2 + rows * h * 2 + t * e * 8
     comb_bytes = rows * h * 2 + t * h * 2 + t * e * 8 + t * e * 4
@@ -429,7 +429,7 @@ def main():
                 "dtype": "bf16", "data": "synthetic (seeded N(0,1) activations/logits, "
                 "N(0,0.02) weights, Zipf expert bias)",
                 "config": config_dict(a, world),
-                "roofline": {"bound": "tensor", "kernel": "grouped_gemm fc1 (tcgen05, fused SwiGLU)",
+                "roofline": {"bound": "tensor", "kernel": "grouped_gemm fc1 stage (tcgen05 pair kernel + remainder kernel, fused SwiGLU)",
                              "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
                              "frac": round(achieved / peak, 4), "traffic": traffic},
                 "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks}
