@@ -36,4 +36,4 @@ int num_sms(int device) {
 
 extern "C" const char* moe_b200_last_error(void) { return moe::g_last_error; }
 
-extern "C" int moe_b200_abi_version(void) { return 1; }
+extern "C" int moe_b200_abi_version(void) { return 2; }

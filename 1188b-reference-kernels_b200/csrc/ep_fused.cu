@@ -1,15 +1,16 @@
 // Expert-parallel dispatch and combine fused with the NVLink exchange.
 //
-// The permuted rows of rank r that belong to rank d's experts form one
-// contiguous block (the layout is expert-major and experts are split
-// contiguously), and that block lands in d's receive buffer at a fixed row
-// shift delta[d] (= d-side offset of r's block - r-side offset of the block,
-// from the host exchange plan). So:
-//   dispatch: permute, but write row r of expert e straight into rank
-//             d = e / experts_per_rank's buffer at row r + delta[d]
-//             (stores over NVLink into the peer mapping);
+// The permuted rows of this rank that belong to expert e form one contiguous
+// block (the permuted layout is expert-major), and that block lands in the
+// buffer of its owner d = e / experts_per_rank at a fixed row shift
+// expert_delta[e], computed on the host from every rank's per-expert counts.
+// With an expert-major receive layout (each local expert's rows from all
+// sources one after another) every local expert is one GEMM group. So:
+//   dispatch: permute, but write row r of expert e straight into rank d's
+//             buffer at row r + expert_delta[e] (stores over NVLink into the
+//             peer mapping);
 //   combine:  unpermute, but read the source row of (t, e) from rank d's
-//             fc2 output at row r + delta[d] (loads over NVLink).
+//             fc2 output at row r + expert_delta[e] (loads over NVLink).
 // No local permuted copy and no separate all-to-all. Each access is checked
 // against the buffers' row capacity, so a corrupt map cannot reach outside
 // them; entries that fail the check are skipped.
@@ -28,9 +29,9 @@ using namespace rowcopy;
 constexpr int kMaxRanks = 8;
 
 struct PeerRows {
-  long long base[kMaxRanks];   // address of rank d's buffer in this process
-  long long delta[kMaxRanks];  // row shift from a local row id into rank d's buffer
-  long long cap_rows;          // rows every rank's buffer holds
+  long long base[kMaxRanks];  // address of rank d's buffer in this process
+  const long long* delta;     // [E] row shift from a local row id into the owner's buffer
+  long long cap_rows;         // rows every rank's buffer holds
   int experts_per_rank;
   int ranks;
 };
@@ -38,7 +39,7 @@ struct PeerRows {
 MOE_DEVICE bool peer_row(const PeerRows& pr, int e, int64_t r, long long& base, int64_t& rr) {
   const int d = e / pr.experts_per_rank;
   if (d >= pr.ranks) return false;
-  rr = r + pr.delta[d];
+  rr = r + __ldg(pr.delta + e);
   base = pr.base[d];
   return rr >= 0 && rr < pr.cap_rows;
 }
@@ -136,26 +137,23 @@ __global__ void __launch_bounds__(kRowThreads) ep_combine_kernel(
   }
 }
 
-int make_peer_rows(PeerRows& pr, const int64_t* bases, const int64_t* deltas, int ranks,
+int make_peer_rows(PeerRows& pr, const int64_t* bases, const int64_t* expert_deltas, int ranks,
                    int experts_per_rank, int64_t cap_rows, int64_t E, int64_t H, int& vbytes,
                    const char* who) {
   MOE_REQUIRE(ranks >= 1 && ranks <= kMaxRanks, "%s: ranks=%d out of [1,%d]", who, ranks,
               kMaxRanks);
   MOE_REQUIRE(experts_per_rank >= 1 && experts_per_rank * static_cast<int64_t>(ranks) == E,
               "%s: experts_per_rank * ranks must equal E", who);
-  MOE_REQUIRE(bases != nullptr && deltas != nullptr, "%s: null peer table", who);
+  MOE_REQUIRE(bases != nullptr && expert_deltas != nullptr, "%s: null peer table", who);
   MOE_REQUIRE(cap_rows >= 0, "%s: bad capacity", who);
   uintptr_t m = (H * 2) & 15 ? 2 : 16;
   for (int d = 0; d < ranks; ++d) {
     MOE_REQUIRE(bases[d] != 0, "%s: null buffer for rank %d", who, d);
     pr.base[d] = bases[d];
-    pr.delta[d] = deltas[d];
     if ((static_cast<uintptr_t>(bases[d]) & 15) != 0) m = 2;
   }
-  for (int d = ranks; d < kMaxRanks; ++d) {
-    pr.base[d] = 0;
-    pr.delta[d] = 0;
-  }
+  for (int d = ranks; d < kMaxRanks; ++d) pr.base[d] = 0;
+  pr.delta = reinterpret_cast<const long long*>(expert_deltas);
   pr.cap_rows = cap_rows;
   pr.experts_per_rank = experts_per_rank;
   pr.ranks = ranks;
@@ -169,7 +167,7 @@ int make_peer_rows(PeerRows& pr, const int64_t* bases, const int64_t* deltas, in
 using namespace moe;
 
 extern "C" int moe_ep_dispatch(const void* x, const int64_t* row_id_map_te,
-                               const int64_t* peer_bases, const int64_t* peer_deltas,
+                               const int64_t* peer_bases, const int64_t* expert_deltas,
                                int32_t ranks, int32_t experts_per_rank, int64_t cap_rows,
                                int64_t T, int64_t H, int64_t E, int64_t num_rows,
                                moe_stream_t stream) {
@@ -178,7 +176,7 @@ extern "C" int moe_ep_dispatch(const void* x, const int64_t* row_id_map_te,
   MOE_REQUIRE(x && row_id_map_te, "ep_dispatch: null pointer");
   PeerRows pr;
   int vb = 16;
-  int st = make_peer_rows(pr, peer_bases, peer_deltas, ranks, experts_per_rank, cap_rows, E, H,
+  int st = make_peer_rows(pr, peer_bases, expert_deltas, ranks, experts_per_rank, cap_rows, E, H,
                           vb, "ep_dispatch");
   if (st) return st;
   if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) vb = 2;
@@ -204,7 +202,7 @@ extern "C" int moe_ep_dispatch(const void* x, const int64_t* row_id_map_te,
   return MOE_OK;
 }
 
-extern "C" int moe_ep_combine(const int64_t* peer_bases, const int64_t* peer_deltas,
+extern "C" int moe_ep_combine(const int64_t* peer_bases, const int64_t* expert_deltas,
                               int32_t ranks, int32_t experts_per_rank, int64_t cap_rows,
                               const int64_t* row_id_map_te, const float* probs, void* out,
                               int64_t T, int64_t H, int64_t E, int64_t num_rows,
@@ -215,7 +213,7 @@ extern "C" int moe_ep_combine(const int64_t* peer_bases, const int64_t* peer_del
   MOE_REQUIRE(out && row_id_map_te, "ep_combine: null pointer");
   PeerRows pr;
   int vb = 16;
-  int st = make_peer_rows(pr, peer_bases, peer_deltas, ranks, experts_per_rank, cap_rows, E, H,
+  int st = make_peer_rows(pr, peer_bases, expert_deltas, ranks, experts_per_rank, cap_rows, E, H,
                           vb, "ep_combine");
   if (st) return st;
   if ((reinterpret_cast<uintptr_t>(out) & 15) != 0) vb = 2;

@@ -109,7 +109,7 @@ def load(path=None, build_if_missing: bool = False):
             fn = getattr(lib, name)
             fn.argtypes = args
             fn.restype = _RESTYPE.get(name, c_int32)
-        if lib.moe_b200_abi_version() != 1:
+        if lib.moe_b200_abi_version() != 2:
             raise ImportError("libmoe_b200.so ABI version mismatch")
         _lib = lib
         return _lib

@@ -167,6 +167,42 @@ def exchange_plan(counts_all: Sequence[Sequence[int]], rank: int, local_experts:
     return ExchangePlan(send, recv, prefix(send), prefix(recv), dst_off, back_off)
 
 
+class ExpertMajorLayout:
+    """Receive layout of the fused transport, seen from one rank.
+
+    Every owner stores its local experts one after another, and inside each
+    expert the rows of source 0, 1, ... in order, so each local expert is one
+    contiguous GEMM group.
+    """
+
+    def __init__(self, deltas: List[int], splits: List[int], recv_rows: List[int]):
+        self.deltas = deltas        # [E]: row in the owner's buffer = this rank's permuted row + deltas[e]
+        self.splits = splits        # [E_loc]: rows this rank receives per local expert
+        self.recv_rows = recv_rows  # [G]: rows every rank receives
+
+
+def expert_major_layout(counts_all: Sequence[Sequence[int]], rank: int,
+                        local_experts: int) -> ExpertMajorLayout:
+    """Row shifts and group sizes of the expert-major receive layout from the
+    gathered [G, E] per-expert counts (row s = rank s's counts). This rank's
+    permuted rows of expert e start at the prefix of its own counts; in the
+    owner's buffer they start after the owner's lower experts and after the
+    rows of expert e from lower-numbered sources."""
+    import numpy as np
+    c = np.asarray(counts_all, dtype=np.int64)
+    g, e = c.shape
+    el = int(local_experts)
+    if e != g * el:
+        raise ValueError("counts do not match world size x local experts")
+    tot = c.sum(axis=0).reshape(g, el)                  # rows per expert, by owner
+    blk = (np.cumsum(tot, axis=1) - tot).reshape(-1)    # expert's block start in its owner
+    before = c[:rank].sum(axis=0)                       # rows of lower sources, per expert
+    src_start = np.cumsum(c[rank]) - c[rank]
+    deltas = blk + before - src_start
+    return ExpertMajorLayout([int(v) for v in deltas], [int(v) for v in tot[rank]],
+                             [int(v) for v in tot.sum(axis=1)])
+
+
 class EPPeerExchange:
     """Row exchange through peer-mapped buffers and the copy engines.
 
@@ -235,17 +271,30 @@ class EPPeerExchange:
         del lib
         return ptrs
 
-    def exchange_counts(self, counts: torch.Tensor):
-        """All-gathers the per-expert counts; returns (plan, recv_counts [G*E_loc]
-        int32 on the device in (source, local expert) order)."""
+    def _gather_counts(self, counts: torch.Tensor) -> torch.Tensor:
         c = counts.to(torch.int32).contiguous()
         allc = torch.empty((self.world * self.num_experts,), dtype=torch.int32, device=c.device)
         dist.all_gather_into_tensor(allc, c, group=self.group)
-        m = allc.view(self.world, self.num_experts)
+        return allc.view(self.world, self.num_experts)
+
+    def exchange_counts(self, counts: torch.Tensor):
+        """All-gathers the per-expert counts; returns (plan, recv_counts [G*E_loc]
+        int32 on the device in (source, local expert) order)."""
+        m = self._gather_counts(counts)
         e0 = self.rank * self.local_experts
         recv_counts = m[:, e0:e0 + self.local_experts].contiguous().view(-1)
         host = m.cpu().tolist()  # the one host sync of the forward
         return exchange_plan(host, self.rank, self.local_experts), recv_counts
+
+    def expert_major(self, counts: torch.Tensor):
+        """All-gathers the per-expert counts (the one host sync of the forward);
+        returns (layout, [G][E] counts on the host, device int64 [E] row shifts)."""
+        host = self._gather_counts(counts).cpu().tolist()
+        lay = expert_major_layout(host, self.rank, self.local_experts)
+        if max(lay.recv_rows) > self.recv_cap:
+            raise ValueError("exchange exceeds a receive buffer")
+        deltas = torch.tensor(lay.deltas, dtype=torch.int64).to(self.device, non_blocking=True)
+        return lay, host, deltas
 
     def _copies(self, jobs):
         main = torch.cuda.current_stream(self.device)
@@ -290,34 +339,27 @@ class EPPeerExchange:
         earlier work on its stream has finished."""
         dist.all_reduce(self.flag, group=self.group)
 
-    def _table(self, ptrs: List[int], plan: ExchangePlan):
-        n = self.world
-        bases = (ctypes.c_int64 * n)(*ptrs)
-        deltas = (ctypes.c_int64 * n)(*[plan.dst_off[d] - plan.send_off[d] for d in range(n)])
-        for d in range(n):
-            if plan.dst_off[d] + plan.send[d] > self.recv_cap:
-                raise ValueError("exchange exceeds a receive buffer")
-        return bases, deltas
-
-    def fused_dispatch(self, x: torch.Tensor, map_te: torch.Tensor, plan: ExchangePlan) -> torch.Tensor:
-        """Permutes x straight into the owners' receive buffers, then barriers."""
+    def fused_dispatch(self, x: torch.Tensor, map_te: torch.Tensor, deltas: torch.Tensor,
+                       nsend: int, nrecv: int) -> torch.Tensor:
+        """Permutes x straight into the owners' receive buffers (row of expert
+        e at its permuted row + deltas[e]), then barriers."""
         t, h = x.shape
-        bases, deltas = self._table(self.peer_recv, plan)
-        _lib.call("moe_ep_dispatch", x.data_ptr(), map_te.data_ptr(), bases, deltas, self.world,
-                  self.local_experts, self.recv_cap, t, h, self.num_experts, sum(plan.send),
+        bases = (ctypes.c_int64 * self.world)(*self.peer_recv)
+        _lib.call("moe_ep_dispatch", x.data_ptr(), map_te.data_ptr(), bases, deltas.data_ptr(),
+                  self.world, self.local_experts, self.recv_cap, t, h, self.num_experts, nsend,
                   torch.cuda.current_stream(self.device).cuda_stream)
         self.barrier()
-        return self.recv_buf[:sum(plan.recv)]
+        return self.recv_buf[:nrecv]
 
-    def fused_combine(self, map_te: torch.Tensor, probs: Optional[torch.Tensor], plan: ExchangePlan,
-                      tokens: int, hidden: int) -> torch.Tensor:
+    def fused_combine(self, map_te: torch.Tensor, probs: Optional[torch.Tensor],
+                      deltas: torch.Tensor, nsend: int, tokens: int, hidden: int) -> torch.Tensor:
         """Weighted combine reading every result row from the rank that made it
         (call after every rank's fc2 wrote into y_buf and barrier())."""
-        bases, deltas = self._table(self.peer_y, plan)
+        bases = (ctypes.c_int64 * self.world)(*self.peer_y)
         out = torch.empty((tokens, hidden), dtype=torch.bfloat16, device=self.device)
-        _lib.call("moe_ep_combine", bases, deltas, self.world, self.local_experts, self.recv_cap,
-                  map_te.data_ptr(), None if probs is None else probs.data_ptr(), out.data_ptr(),
-                  tokens, hidden, self.num_experts, sum(plan.send),
+        _lib.call("moe_ep_combine", bases, deltas.data_ptr(), self.world, self.local_experts,
+                  self.recv_cap, map_te.data_ptr(), None if probs is None else probs.data_ptr(),
+                  out.data_ptr(), tokens, hidden, self.num_experts, nsend,
                   torch.cuda.current_stream(self.device).cuda_stream)
         return out
 
@@ -363,8 +405,11 @@ class MoELayerEP:
         self.k = int(topk)
         self.renorm = renorm
         self.bias = expert_bias
-        self.plan = ops.GroupedGemmPlan(self.disp.world * self.disp.local_experts,
-                                        local_weights.w1.device)
+        # fused: one group per local expert (expert-major receive layout);
+        # otherwise one group per (source rank, local expert).
+        groups = self.disp.local_experts * (1 if self.fused else self.disp.world)
+        self.plan = ops.GroupedGemmPlan(groups, local_weights.w1.device)
+        self._deltas = None
         self.events = None  # optional dict of CUDA events for stage timing
 
     def _ev(self, name: str):
@@ -408,10 +453,13 @@ class MoELayerEP:
     def _forward_fused(self, x, r, rim):
         t, h = x.shape
         self._ev("local_dispatch")
-        plan, recv_counts = self.peer.exchange_counts(rim.counts)
-        xr = self.peer.fused_dispatch(x, rim.map_te, plan)
+        lay, host, deltas = self.peer.expert_major(rim.counts)
+        self._deltas = deltas  # read by both fused kernels of this forward
+        nsend = int(sum(host[self.peer.rank]))
+        nrecv = int(sum(lay.splits))
+        xr = self.peer.fused_dispatch(x, rim.map_te, deltas, nsend, nrecv)
         self._ev("a2a_dispatch")
-        self.plan.from_ep_counts(recv_counts, self.disp.world, self.disp.local_experts)
+        self.plan.from_splits(torch.tensor(lay.splits, dtype=torch.int32))
         hmid = ops.grouped_gemm(xr, self.w.w1, epilogue="swiglu", plan=self.plan)
         self._ev("fc1")
         y = ops.grouped_gemm(hmid, self.w.w2, plan=self.plan,
@@ -419,7 +467,7 @@ class MoELayerEP:
         self._ev("fc2")
         self.peer.barrier()
         self._ev("a2a_combine")
-        out = self.peer.fused_combine(rim.map_te, r.probs, plan, t, h)
+        out = self.peer.fused_combine(rim.map_te, r.probs, deltas, nsend, t, h)
         self._ev("combine")
         return out
 

@@ -205,18 +205,20 @@ int moe_copy_async(void* dst, const void* src, size_t bytes, moe_stream_t stream
 
 /* Fused dispatch: permute x by the token-major map, writing the row of      */
 /* (t, e) straight into rank d = e / experts_per_rank's buffer at row        */
-/* map[t,e] + peer_deltas[d] (peer_bases: this process's address of every    */
-/* rank's buffer, host arrays of `ranks` entries, ranks <= 8). Rows outside  */
-/* [0, cap_rows) of the target buffer are skipped.                           */
+/* map[t,e] + expert_deltas[e]. peer_bases: this process's address of every  */
+/* rank's buffer (host array of `ranks` entries, ranks <= 8); expert_deltas: */
+/* device array of E row shifts (one per expert, so the owner's buffer may   */
+/* be source-major or expert-major). Rows outside [0, cap_rows) of the       */
+/* target buffer are skipped.                                                */
 int moe_ep_dispatch(const void* x, const int64_t* row_id_map_te, const int64_t* peer_bases,
-                    const int64_t* peer_deltas, int32_t ranks, int32_t experts_per_rank,
+                    const int64_t* expert_deltas, int32_t ranks, int32_t experts_per_rank,
                     int64_t cap_rows, int64_t T, int64_t H, int64_t E, int64_t num_rows,
                     moe_stream_t stream);
 /* Fused combine: out[t] = bf16(sum over e ascending of probs[t,e] * row),   */
 /* each row read from rank e / experts_per_rank's buffer at map[t,e] +       */
-/* peer_deltas[d]; probs null = unweighted. Same arithmetic as               */
-/* moe_unpermute_mask_token_major. E <= 1024.                                */
-int moe_ep_combine(const int64_t* peer_bases, const int64_t* peer_deltas, int32_t ranks,
+/* expert_deltas[e] (device array); probs null = unweighted. Same arithmetic */
+/* as moe_unpermute_mask_token_major. E <= 1024.                             */
+int moe_ep_combine(const int64_t* peer_bases, const int64_t* expert_deltas, int32_t ranks,
                    int32_t experts_per_rank, int64_t cap_rows, const int64_t* row_id_map_te,
                    const float* probs, void* out, int64_t T, int64_t H, int64_t E,
                    int64_t num_rows, moe_stream_t stream);

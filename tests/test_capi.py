@@ -33,7 +33,7 @@ def test_header_symbols_exported(lib):
 
 
 def test_abi_version(lib):
-    assert lib.moe_b200_abi_version() == 1
+    assert lib.moe_b200_abi_version() == 2
 
 
 def test_workspace_sizes(lib):

@@ -9,7 +9,7 @@ sender's permuted buffer had it.
 import numpy as np
 import pytest
 
-from moe_b200.ep import ep_group_table, exchange_plan
+from moe_b200.ep import ep_group_table, exchange_plan, expert_major_layout
 
 
 @pytest.mark.parametrize("world,experts", [(2, 8), (4, 16), (8, 256)])
@@ -68,3 +68,36 @@ def test_balanced_placement(world):
     assert max(tot) - np.mean(tot) <= load.max() + 1e-9
     for r in range(world):
         assert pl[r * per:(r + 1) * per] == sorted(pl[r * per:(r + 1) * per])
+
+
+@pytest.mark.parametrize("world,experts", [(1, 8), (2, 8), (4, 16), (8, 256)])
+@pytest.mark.parametrize("seed", [0, 1, 2])
+def test_expert_major_layout(world, experts, seed):
+    """Fused-transport layout: every sender's row of expert e lands at its
+    permuted row + deltas[e] in the owner's buffer; the owner's buffer holds
+    its local experts in order, each as one block of sources 0..G-1 in order,
+    with nothing overlapping and nothing left empty."""
+    rng = np.random.default_rng(seed + 10 * world)
+    el = experts // world
+    counts = rng.integers(0, 60, size=(world, experts))
+    counts[rng.random(counts.shape) < 0.3] = 0
+    lays = [expert_major_layout(counts.tolist(), r, el) for r in range(world)]
+    tot = counts.sum(0)
+    recv = [np.full((world * counts.sum(), 3), -1) for _ in range(world)]
+    for s, lay in enumerate(lays):
+        start = np.concatenate([[0], np.cumsum(counts[s])[:-1]])
+        for e in range(experts):
+            d = e // el
+            for i in range(counts[s, e]):
+                row = start[e] + i + lay.deltas[e]
+                assert 0 <= row < lay.recv_rows[d]
+                assert recv[d][row, 0] == -1, "two rows land on one slot"
+                recv[d][row] = (e, s, i)
+    for d in range(world):
+        lay = lays[d]
+        assert lay.splits == list(tot[d * el:(d + 1) * el])
+        assert lay.recv_rows == [int(tot[q * el:(q + 1) * el].sum()) for q in range(world)]
+        expect = [(d * el + j, s, i) for j in range(el) for s in range(world)
+                  for i in range(counts[s, d * el + j])]
+        np.testing.assert_array_equal(recv[d][:lay.recv_rows[d]], np.array(expect).reshape(-1, 3))
+        assert (recv[d][lay.recv_rows[d]:] == -1).all()

@@ -2,8 +2,8 @@
 
 Each output element is accumulated in the same K order by the same kernel on
 either path, and the combine adds experts in ascending order on both, so the
-EP result must equal the single-GPU result bit for bit. Needs >= 2 GPUs;
-skipped on single-GPU hosts.
+EP result must equal the single-GPU result bit for bit. Needs >= 2 GPUs (4
+and 8 for the wider cases); skipped on hosts with fewer.
 """
 import os
 import socket
@@ -91,7 +91,9 @@ def _worker(rank, world, port, routing, transport, q, placed=False):
                                                      (4, "zipf", "peer"), (4, "uniform", "nccl"),
                                                      (4, "zipf", "fused"), (4, "uniform", "fused"),
                                                      (2, "zipf", "fused+placed"),
-                                                     (4, "zipf", "fused+placed")])
+                                                     (4, "zipf", "fused+placed"),
+                                                     (8, "zipf", "fused+placed"),
+                                                     (8, "uniform", "nccl")])
 def test_ep_equals_single_gpu(world, routing, transport):
     if not torch.cuda.is_available():
         pytest.fail("GPU test selected but no CUDA device is visible")
