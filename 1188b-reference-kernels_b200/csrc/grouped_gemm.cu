@@ -29,6 +29,7 @@
 
 #include <stdlib.h>
 
+#include <algorithm>
 #include <mutex>
 
 #include "moe_common.cuh"
@@ -60,7 +61,7 @@ struct Params {
   const int32_t* rows;
   const int32_t* widx;
   int32_t* err;
-  __nv_bfloat16* out;
+  void* out;        // bf16 [x_rows, n_out], or fp32 for epilogue 2
   int64_t x_rows;
   int G;
   int n_w;     // rows of one weight matrix (N)
@@ -68,7 +69,8 @@ struct Params {
   int f_half;  // N/2 (SwiGLU up-row offset)
   int num_kb;
   int n_tiles;
-  int epilogue;
+  int bn;        // pair kernel: N-tile width (256; narrower for epilogues 0/2 when N % 256 != 0)
+  int epilogue;  // 0 bf16 out, 1 SwiGLU -> bf16, 2 fp32 out
   int raster;   // pair kernel: pair M-tiles per raster super-row
   int l2_mode;  // pair kernel: 0 both evict_normal, 1 B evict_first, 2 A evict_last + B evict_first
 };
@@ -337,9 +339,27 @@ __global__ void __launch_bounds__(kThreads, 1)
       const bool rvalid = m_local < p.rows[tile.g] && row < p.x_rows;
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      if (p.epilogue == 0) {
+      if (p.epilogue == 2) {
         const int n0 = tile.n_idx * BN;
-        __nv_bfloat16* orow = p.out + row * p.n_out;
+        float* orow = static_cast<float*>(p.out) + row * p.n_out;
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, r);
+          tmem_ld_wait();
+          if (rvalid) {
+#pragma unroll
+            for (int v = 0; v < 8; ++v) {
+              const int col = n0 + c * 32 + v * 4;
+              if (col + 4 <= p.n_out)
+                *reinterpret_cast<uint4*>(orow + col) =
+                    make_uint4(r[v * 4], r[v * 4 + 1], r[v * 4 + 2], r[v * 4 + 3]);
+            }
+          }
+        }
+      } else if (p.epilogue == 0) {
+        const int n0 = tile.n_idx * BN;
+        __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.out) + row * p.n_out;
 #pragma unroll 1
         for (int c = 0; c < BN / 32; ++c) {
           uint32_t r[32];
@@ -362,7 +382,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
       } else {
         const int n0 = tile.n_idx * 128;
-        __nv_bfloat16* orow = p.out + row * p.n_out;
+        __nv_bfloat16* orow = static_cast<__nv_bfloat16*>(p.out) + row * p.n_out;
 #pragma unroll 1
         for (int c = 0; c < 128 / 32; ++c) {
           uint32_t gr[32], ur[32];
@@ -427,7 +447,6 @@ constexpr int kPairRaster = 8;                            // pair M-tiles per su
 constexpr uint32_t kPairABytes = 128 * BK * 2;            // 16 KB: this CTA's rows
 constexpr uint32_t kPairBBytes = 128 * BK * 2;            // 16 KB: this CTA's half of B
 constexpr uint32_t kPairStageBytes = kPairABytes + kPairBBytes;   // 32 KB
-constexpr uint32_t kPairTxBytes = 2 * kPairStageBytes;    // both CTAs, on the leader's barrier
 constexpr uint32_t kEpiBoxBytes = 32 * 32 * 2;            // 32 rows x 32 bf16 columns
 constexpr uint32_t kEpiBytes = 4 * 2 * kEpiBoxBytes;        // 4 warps x 2 buffers = 16 KB
 constexpr size_t kPairSmemBytes = 1024 + kPairStages * kPairStageBytes + 1024 + kEpiBytes;
@@ -506,8 +525,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         ra = p.row_start[tl.g] + tl.m_idx * pairk::kPairTileM + static_cast<int>(rank) * 128;
         const int wb = p.widx[tl.g] * p.n_w;
         rb = (p.epilogue == 1) ? wb + tl.n_idx * 128 + static_cast<int>(rank) * p.f_half
-                               : wb + tl.n_idx * BN + static_cast<int>(rank) * 128;
+                               : wb + tl.n_idx * p.bn + static_cast<int>(rank) * (p.bn / 2);
       };
+      // Both CTAs' bytes per stage: 128 A rows each, bn/2 B rows each.
+      const uint32_t tx = 2u * (pairk::kPairABytes + static_cast<uint32_t>(p.bn / 2) * (BK * 2));
       for (long long t = cid; ok; t += ncl) {
         Tile tile;
         if (!walker.locate(t, tile)) break;
@@ -521,7 +542,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sa = base + stage * pairk::kPairStageBytes;
           const uint32_t sb = sa + pairk::kPairABytes;
           const uint32_t leader_full = map_to_rank(full_bar(stage), 0);
-          if (leader) mbar_arrive_expect_tx(full_bar(stage), pairk::kPairTxBytes);
+          if (leader) mbar_arrive_expect_tx(full_bar(stage), tx);
           tma_load_2d_pair(sa, &tmap_a, kb * BK, row0, leader_full, pol_a);
           tma_load_2d_pair(sb, &tmap_b, kb * BK, b0, leader_full, pol_b);
           issued[stage] = static_cast<int>(phase);
@@ -553,7 +574,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader)
     if (leader && lane == 0) {
-      const uint32_t idesc = umma_idesc_bf16_f32(pairk::kPairTileM, BN);
+      const uint32_t idesc = umma_idesc_bf16_f32(pairk::kPairTileM, p.bn);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -617,9 +638,12 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint32_t chunk_no = 0;
     int it = 0;
     bool ok = true;
-    // One 32-row x 32-column chunk: packed bf16 pairs of this lane's row.
+    // One 32-row chunk of 64 bytes per row (32 bf16 or 16 fp32 columns) of
+    // this lane's row, as 16 32-bit words; col counts output elements.
+    const int elem_bytes = p.epilogue == 2 ? 4 : 2;
+    const int chunk_cols = 64 / elem_bytes;
     auto emit = [&](const uint32_t (&o)[16], bool tma, int64_t row, int col, int warp_row0,
-                    __nv_bfloat16* orow, bool rvalid) {
+                    char* orow, bool rvalid) {
       if (tma) {
         const uint32_t buf = epi_base + (chunk_no & 1u) * pairk::kEpiBoxBytes;
         ++chunk_no;
@@ -640,10 +664,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           bulk_commit();
         }
       } else if (rvalid) {
+        const int vcols = chunk_cols / 4;  // columns per 16-byte vector
 #pragma unroll
         for (int v = 0; v < 4; ++v)
-          if (col + v * 8 + 8 <= p.n_out)
-            *reinterpret_cast<uint4*>(orow + col + v * 8) =
+          if (col + (v + 1) * vcols <= p.n_out)
+            *reinterpret_cast<uint4*>(orow + static_cast<int64_t>(col + v * vcols) * elem_bytes) =
                 make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
       }
       (void)row;
@@ -665,11 +690,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int warp_row0 = static_cast<int>(row) - lane;
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
-      __nv_bfloat16* orow = p.out + row * p.n_out;
-      if (p.epilogue == 0) {
-        const int n0 = tile.n_idx * BN;
+      char* orow = static_cast<char*>(p.out) + row * p.n_out * elem_bytes;
+      if (p.epilogue == 2) {
+        const int n0 = tile.n_idx * p.bn;
 #pragma unroll 1
-        for (int c = 0; c < BN / 32; ++c) {
+        for (int c = 0; c < p.bn / 32; ++c) {
+          const int col = n0 + c * 32;
+          if (col >= p.n_out) break;  // warp-uniform
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + c * 32, r);
+          tmem_ld_wait();
+          uint32_t o[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) o[q] = r[q];
+          emit(o, tma, row, col, warp_row0, orow, rvalid);
+          if (col + 16 < p.n_out) {
+#pragma unroll
+            for (int q = 0; q < 16; ++q) o[q] = r[16 + q];
+            emit(o, tma, row, col + 16, warp_row0, orow, rvalid);
+          }
+        }
+      } else if (p.epilogue == 0) {
+        const int n0 = tile.n_idx * p.bn;
+#pragma unroll 1
+        for (int c = 0; c < p.bn / 32; ++c) {
           const int col = n0 + c * 32;
           if (col >= p.n_out) break;  // warp-uniform
           uint32_t r[32];
@@ -843,7 +887,8 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
 }
 
 int make_tmap_box(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer,
-                  uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz);
+                  uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz,
+                  bool fp32 = false);
 
 // 2-D bf16 tensor map over a row-major [outer, inner] matrix, box 64 x 128,
 // 128-byte swizzle (one box row = one 128-byte swizzle row).
@@ -852,18 +897,20 @@ int make_tmap(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer) {
                        CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
+// 2-D tensor map over a row-major [outer, inner] bf16 (or fp32) matrix.
 int make_tmap_box(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer,
-                  uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+                  uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz, bool fp32) {
   auto encode = get_encode_fn();
   if (encode == nullptr) {
     set_last_error("grouped_gemm: cuTensorMapEncodeTiled unavailable");
     return MOE_ERR_CUDA;
   }
   cuuint64_t dims[2] = {inner, outer};
-  cuuint64_t strides[1] = {inner * 2};
+  cuuint64_t strides[1] = {inner * (fp32 ? 4 : 2)};
   cuuint32_t box[2] = {box_inner, box_outer};
   cuuint32_t estr[2] = {1u, 1u};
-  const CUresult r = encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
+  const CUresult r = encode(m, fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                            2, const_cast<void*>(ptr), dims,
                             strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
@@ -994,7 +1041,7 @@ extern "C" int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t
                                 int64_t num_w, int64_t N, int64_t K, int32_t epilogue,
                                 const void* workspace, size_t workspace_bytes,
                                 moe_stream_t stream) {
-  MOE_REQUIRE(epilogue == 0 || epilogue == 1, "grouped_gemm: epilogue must be 0 or 1");
+  MOE_REQUIRE(epilogue >= 0 && epilogue <= 2, "grouped_gemm: epilogue must be 0, 1 or 2");
   MOE_REQUIRE(G >= 1 && num_w >= 1, "grouped_gemm: G=%lld num_w=%lld", (long long)G,
               (long long)num_w);
   MOE_REQUIRE(x_rows >= 0 && x_rows < (1ll << 31), "grouped_gemm: x_rows=%lld out of range",
@@ -1003,7 +1050,7 @@ extern "C" int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t
               (long long)K);
   MOE_REQUIRE(N >= 8 && N % 8 == 0, "grouped_gemm: N=%lld must be a positive multiple of 8",
               (long long)N);
-  MOE_REQUIRE(epilogue == 0 || N % 16 == 0, "grouped_gemm: SwiGLU needs N=2F with F %% 8 == 0");
+  MOE_REQUIRE(epilogue != 1 || N % 16 == 0, "grouped_gemm: SwiGLU needs N=2F with F %% 8 == 0");
   MOE_REQUIRE(num_w * N < (1ll << 31), "grouped_gemm: num_w*N too large");
   int st = check_ws(workspace, workspace_bytes, G);
   if (st) return st;
@@ -1027,7 +1074,7 @@ extern "C" int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t
   p.rows = l.rows;
   p.widx = l.widx;
   p.err = l.err;
-  p.out = static_cast<__nv_bfloat16*>(out);
+  p.out = out;
   p.x_rows = x_rows;
   p.G = static_cast<int>(G);
   p.n_w = static_cast<int>(N);
@@ -1041,6 +1088,7 @@ extern "C" int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t
     p.n_out = static_cast<int>(N);
     p.n_tiles = static_cast<int>((N + gg::BN - 1) / gg::BN);
   }
+  p.bn = gg::BN;
   p.num_kb = static_cast<int>((K + gg::BK - 1) / gg::BK);
   static const int raster = gg::env_int("MOE_GEMM_RASTER", gg::pairk::kPairRaster, 1, 64);
   static const int l2_mode = gg::env_int("MOE_GEMM_L2", 0, 0, 2);
@@ -1051,9 +1099,10 @@ extern "C" int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t
   MOE_CUDA_CALL(cudaGetDevice(&dev), "cudaGetDevice");
   const int clusters = gg::pair_enabled() ? gg::pair_clusters(dev) : 0;
   if (clusters > 0) {
+    // Epilogue tile stores: 32 rows x 64 bytes (32 bf16 or 16 fp32 columns).
     CUtensorMap to;
     st = gg::make_tmap_box(&to, out, static_cast<uint64_t>(p.n_out), static_cast<uint64_t>(x_rows),
-                           32u, 32u, CU_TENSOR_MAP_SWIZZLE_64B);
+                           epilogue == 2 ? 16u : 32u, 32u, CU_TENSOR_MAP_SWIZZLE_64B, epilogue == 2);
     if (st) return st;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * clusters);
@@ -1070,7 +1119,23 @@ extern "C" int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t
     static const bool split = gg::env_int("MOE_GEMM_SPLIT", 1, 0, 1) == 1;
     gg::Params pb = p;
     if (split) pb.rows = l.rows_body;
-    MOE_CUDA_CALL(cudaLaunchKernelEx(&cfg, gg::grouped_gemm_pair_kernel, ta, tb, to, pb),
+    // Without SwiGLU, N is cut into equal N-tiles of at most 256 columns (a
+    // multiple of 32), e.g. 320 -> 2 x 160 rather than 256 + a 64-column tile
+    // padded to 256. The B box of the pair then holds bn/2 rows per CTA.
+    CUtensorMap tbp = tb;
+    if (epilogue != 1) {
+      const int nt = static_cast<int>((N + gg::BN - 1) / gg::BN);
+      const int per = static_cast<int>((N + nt - 1) / nt);
+      pb.bn = std::min(gg::BN, (per + 31) / 32 * 32);
+      pb.n_tiles = static_cast<int>((N + pb.bn - 1) / pb.bn);
+      if (pb.bn != gg::BN) {
+        st = gg::make_tmap_box(&tbp, w, static_cast<uint64_t>(K), static_cast<uint64_t>(num_w * N),
+                               static_cast<uint32_t>(gg::BK), static_cast<uint32_t>(pb.bn / 2),
+                               CU_TENSOR_MAP_SWIZZLE_128B);
+        if (st) return st;
+      }
+    }
+    MOE_CUDA_CALL(cudaLaunchKernelEx(&cfg, gg::grouped_gemm_pair_kernel, ta, tbp, to, pb),
                   "grouped_gemm pair launch");
     if (!split) return MOE_OK;
     // Remainders of every group (< 256 rows) on 128-row single-CTA tiles.

@@ -76,14 +76,17 @@ _RESTYPE = {"moe_b200_last_error": c_char_p}
 
 EXPORTED = tuple(_SIGNATURES)
 
-# Kernels each successful call launches (for the bench's launch count).
+# Kernels each successful call launches (for the bench's launch count). A
+# grouped GEMM is two launches on B200: the CTA-pair kernel on whole 256-row
+# tiles, then the single-CTA kernel on the group remainders (one launch only
+# when CTA pairs are disabled with MOE_GEMM_PAIR=0 or MOE_GEMM_SPLIT=0).
 _LAUNCHES = {"moe_topk_f32": 1, "moe_router_topk": 1, "moe_router_topk_placed": 1,
              "moe_row_id_map": 3,
              "moe_row_id_map_static_scratch": 3,
              "moe_permute_mask_map": 1, "moe_permute_mask_map_trans": 1, "moe_unpermute_mask": 1,
              "moe_unpermute_mask_token_major": 1, "moe_ep_dispatch": 1, "moe_ep_combine": 1,
              "moe_grouped_gemm_plan_splits": 1, "moe_grouped_gemm_plan_ep": 1,
-             "moe_grouped_gemm": 1, "moe_swiglu": 1}
+             "moe_grouped_gemm": 2, "moe_swiglu": 1}
 launch_count = 0
 
 _lock = threading.Lock()

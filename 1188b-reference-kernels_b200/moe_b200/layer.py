@@ -79,9 +79,17 @@ class MoELayer:
         if self.events is not None:
             self.events[name].record()
 
-    def forward(self, x: torch.Tensor, logits: torch.Tensor, return_intermediates: bool = False):
+    def forward(self, x: torch.Tensor, logits: Optional[torch.Tensor] = None,
+                return_intermediates: bool = False,
+                router_weight: Optional[torch.Tensor] = None):
+        """logits [T,E] fp32, or router_weight [E,H] bf16 to compute them first
+        with the router gate GEMM (ops.router_logits)."""
         t, h = x.shape
         e = self.w.num_experts
+        if logits is None:
+            if router_weight is None:
+                raise ValueError("pass logits or router_weight")
+            logits = ops.router_logits(x, router_weight)
         if logits.shape != (t, e):
             raise ValueError(f"logits must be [{t},{e}]")
         if h != self.w.hidden:

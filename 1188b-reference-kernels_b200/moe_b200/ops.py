@@ -335,7 +335,8 @@ def grouped_gemm(x: torch.Tensor, w: torch.Tensor,
 
     x [rows,K] bf16, w [G,N,K] bf16 ("[out,in]" as in case03/case04). With
     epilogue="swiglu", w holds [gate|up] (N=2F) and the result is
-    silu(gate)*up, [rows,F]. m_splits defaults to the uniform split of
+    silu(gate)*up, [rows,F]; with epilogue="fp32" the result is the fp32
+    accumulator, [rows,N] float32. m_splits defaults to the uniform split of
     kernel_cases/case03_moe_grouped_gemm_fc1_fwd.py:43-46. A prebuilt plan
     (device group table) skips the planning launch.
     """
@@ -344,8 +345,9 @@ def grouped_gemm(x: torch.Tensor, w: torch.Tensor,
         _need_dtype(n_, t_, torch.bfloat16)
     if x.dim() != 2 or w.dim() != 3 or x.shape[1] != w.shape[2]:
         raise ValueError(f"shapes x {tuple(x.shape)} w {tuple(w.shape)}")
-    if epilogue not in ("none", "swiglu"):
-        raise ValueError("epilogue must be 'none' or 'swiglu'")
+    codes = {"none": 0, "swiglu": 1, "fp32": 2}
+    if epilogue not in codes:
+        raise ValueError("epilogue must be 'none', 'swiglu' or 'fp32'")
     xc = x.contiguous()
     wc = w.contiguous()
     rows, k = xc.shape
@@ -365,11 +367,45 @@ def grouped_gemm(x: torch.Tensor, w: torch.Tensor,
             ms = torch.tensor([int(v) for v in m_splits], dtype=torch.int32)
         plan = GroupedGemmPlan(g, dev).from_splits(ms, align)
     n_out = n // 2 if epilogue == "swiglu" else n
+    odt = torch.float32 if epilogue == "fp32" else torch.bfloat16
     if out is None:
-        out = torch.empty((rows, n_out), dtype=torch.bfloat16, device=dev)
+        out = torch.empty((rows, n_out), dtype=odt, device=dev)
+    elif out.dtype != odt or tuple(out.shape) != (rows, n_out) or not out.is_contiguous() \
+            or out.device != dev:
+        raise ValueError(f"out must be a contiguous {odt} [{rows},{n_out}] tensor on {dev}")
     _lib.call("moe_grouped_gemm", _p(xc), _p(wc), _p(out), rows, plan.num_groups, g, n, k,
-              1 if epilogue == "swiglu" else 0, _p(plan.workspace), plan.nbytes, _stream(dev))
+              codes[epilogue], _p(plan.workspace), plan.nbytes, _stream(dev))
     return out
+
+
+def router_logits(x: torch.Tensor, weight: torch.Tensor,
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Router gate GEMM: logits [T,E] fp32 = x [T,H] bf16 @ weight [E,H] bf16 ^T,
+    accumulated in fp32 on the tensor cores and stored unrounded.
+
+    Replaces kernel_cases/case38_ref_musa_asm_bf16_ssgemm_nt_320x256.py:51-59
+    (reference_fp32, the TN muDNN GEMM of Megatron's router gate). It is the
+    grouped GEMM with one group and the fp32 epilogue.
+    """
+    for n_, t_ in (("x", x), ("weight", weight)):
+        _need_cuda(n_, t_)
+        _need_dtype(n_, t_, torch.bfloat16)
+    if x.dim() != 2 or weight.dim() != 2 or x.shape[1] != weight.shape[1]:
+        raise ValueError(f"shapes x {tuple(x.shape)} weight {tuple(weight.shape)}")
+    key = (x.device, x.shape[0])
+    plan = _ROUTER_PLANS.get(key)
+    if plan is None:
+        if len(_ROUTER_PLANS) >= 64:
+            _ROUTER_PLANS.clear()
+        plan = GroupedGemmPlan(1, x.device).from_splits(torch.tensor([x.shape[0]], dtype=torch.int32))
+        torch.cuda.current_stream(x.device).synchronize()  # table ready for every stream
+        _ROUTER_PLANS[key] = plan
+    return grouped_gemm(x, weight.unsqueeze(0), epilogue="fp32", plan=plan, out=out)
+
+
+# One-group plans of router_logits, by (device, rows): the table depends only
+# on the row count, so repeated calls skip the planning launch.
+_ROUTER_PLANS: dict = {}
 
 
 def swiglu(y: torch.Tensor) -> torch.Tensor:

@@ -63,6 +63,11 @@ def parse_args():
     ap.add_argument("--transport", choices=["fused", "peer", "nccl"], default="fused",
                     help="EP row exchange: dispatch/combine kernels on peer memory, "
                          "IPC-mapped buffers + copy engines, or NCCL all-to-all")
+    ap.add_argument("--workload", choices=["layer", "router_gemm"], default="layer",
+                    help="layer: the MoE expert-layer forward (the headline); router_gemm: the "
+                         "router gate GEMM that produces its logits (one GPU)")
+    ap.add_argument("--router-shape", default="16384,8192,320",
+                    help="M,K,N of the router GEMM (tokens, hidden, experts)")
     return ap.parse_args()
 
 
@@ -250,6 +255,90 @@ def run_reference_arm(a, world, rank):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------- router GEMM
+def run_router_gemm(a):
+    """Router gate GEMM, logits [M,N] fp32 = x [M,K] bf16 @ w [N,K] bf16 ^T, at the
+    traced shape of kernel_cases/case38_ref_musa_asm_bf16_ssgemm_nt_320x256.py
+    (M=16384, K=8192, N=320). One GPU; x (268 MB) is larger than L2, so no flush."""
+    m, kk, n = (int(v) for v in a.router_shape.split(","))
+    flops = 2.0 * m * n * kk
+    nbytes = m * kk * 2 + n * kk * 2 + m * n * 4
+    cfg = {"workload": "router_gemm", "tokens": m, "hidden": kk, "experts": n,
+           "l2": "no flush: x is larger than the 126 MB L2"}
+    metric, unit = "router GEMM tokens/s", "tokens/s"
+    if a.impl == "reference":
+        use_all_cores()
+        import numpy as np
+        sys.path.insert(0, str(ROOT))
+        from oracle import moe_oracle as orc
+        rows = 256
+        rng = np.random.default_rng(0)
+        xs = rng.standard_normal((rows, kk), dtype=np.float32)
+        ws = rng.standard_normal((n, kk), dtype=np.float32)
+        xu, wu = orc.f32_to_bf16(xs), orc.f32_to_bf16(ws)
+        for _ in range(a.warmup):
+            orc.router_logits(xu, wu)
+        t0 = time.perf_counter()
+        for _ in range(a.steps):
+            orc.router_logits(xu, wu)
+        dt = (time.perf_counter() - t0) / a.steps
+        value = rows / dt
+        line = {"metric": metric, "value": value, "unit": unit, "n_gpus": 1, "steps": a.steps,
+                "warmup": a.warmup, "ms_per_step": 1e3 * dt * m / rows, "higher_is_better": True,
+                "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+                "impl": "reference", "config": cfg,
+                "cpu_baseline": {"value": value, "unit": unit, "cores": cpu_threads(),
+                                 "kind": "port", "sample": f"{rows} of {m} rows, numpy fp32"},
+                "e2e": {"value": value, "unit": unit, "h2d_bytes_per_step": 0,
+                        "d2h_bytes_per_step": 0}}
+        print(json.dumps(line), flush=True)
+        return
+    import torch
+    import moe_b200
+    from moe_b200 import _lib
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    moe_b200.load_library()
+    g = torch.Generator(device=dev)
+    g.manual_seed(0)
+    x = torch.randn(m, kk, device=dev, generator=g).to(torch.bfloat16)
+    w = torch.randn(n, kk, device=dev, generator=g).to(torch.bfloat16)
+    out = torch.empty(m, n, dtype=torch.float32, device=dev)
+    sampler = ClockSampler(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0])
+    sampler.start()
+    for _ in range(a.warmup):
+        moe_b200.router_logits(x, w, out=out)
+    torch.cuda.synchronize()
+    launches0 = _lib.launch_count
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    wall0 = time.time()
+    ev[0].record()
+    for _ in range(a.steps):
+        moe_b200.router_logits(x, w, out=out)
+    ev[1].record()
+    torch.cuda.synchronize()
+    sampler.mark(wall0, time.time())
+    launches = _lib.launch_count - launches0
+    t = ev[0].elapsed_time(ev[1]) / 1e3 / a.steps
+    clocks = sampler.stop()
+    peaks, peak_kind = load_peaks()
+    peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    achieved = flops / t / 1e12
+    line = {"metric": metric, "value": m / t, "unit": unit, "n_gpus": 1, "steps": a.steps,
+            "warmup": a.warmup, "ms_per_step": t * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic (N(0,1))",
+            "config": cfg,
+            "roofline": {"bound": "tensor", "kernel": "grouped_gemm, one group, fp32 epilogue",
+                         "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 4), "traffic": None},
+            "hbm": {"achieved_gbs": round(nbytes / t / 1e9, 1), "peak_gbs": hbm,
+                    "frac": round(nbytes / t / 1e9 / hbm, 4), "bytes": nbytes},
+            "peak_kind": f"bf16 burst, of {peak_kind}",
+            "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 # --------------------------------------------------------------------------- GPU arm
 def read_traffic():
     p = ROOT / "profiles" / "grouped_gemm_fc1_layer.txt"
@@ -269,6 +358,10 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if a.workload == "router_gemm":
+        if rank == 0:
+            run_router_gemm(a)
+        return
     if a.impl == "reference":
         run_reference_arm(a, world, rank)
         return

@@ -161,6 +161,10 @@ int moe_unpermute_mask_token_major(const void* pin, const int64_t* row_id_map_te
 /* epilogue 1 (SwiGLU, fc1): N = 2F with rows [0,F) = gate, [F,2F) = up;     */
 /*   out [rows, F] bf16 = silu(g) * u with g, u the bf16-rounded GEMM        */
 /*   outputs (the unfused chain fc1 -> bf16 -> silu(gate)*up).               */
+/* epilogue 2: out [rows, N] fp32, the accumulator unrounded. With G = 1     */
+/*   this is the router logits GEMM logits = inp @ weight^T (bf16 in, fp32   */
+/*   out), replacing kernel_cases/case38_ref_musa_asm_bf16_ssgemm_nt_320x256 */
+/*   .py:51-59 (reference_fp32; the muDNN TN GEMM of the router gate).       */
 /* x [x_rows, K] bf16, K % 8 == 0, N % 8 == 0 (F % 8 for SwiGLU).            */
 /* workspace: moe_grouped_gemm_workspace_size(G) bytes, 256-byte aligned.    */
 int moe_grouped_gemm_workspace_size(int64_t G, size_t* bytes);

@@ -252,6 +252,15 @@ def grouped_gemm(x_u16: np.ndarray, w_u16: np.ndarray, m_splits, epilogue: str =
     return out
 
 
+def router_logits(x_u16: np.ndarray, w_u16: np.ndarray) -> np.ndarray:
+    """Router gate GEMM, logits fp32 = x @ w.T accumulated in fp32, unrounded.
+
+    kernel_cases/case38_ref_musa_asm_bf16_ssgemm_nt_320x256.py:51-59
+    (reference_fp32: inp.float().matmul(weight.float().t())).
+    """
+    return bf16_to_f32(x_u16) @ bf16_to_f32(w_u16).T
+
+
 # --------------------------------------------------------------------------- layer
 
 

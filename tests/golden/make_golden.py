@@ -213,6 +213,12 @@ def gen_gemm(root: Path) -> None:
     inp = torch.randn(96, 512, generator=gen).to(torch.bfloat16)
     wt = torch.randn(256, 512, generator=gen).to(torch.bfloat16)
     out.update(c35_x=bits(inp), c35_w=bits(wt), c35_y=c35.reference_fp32(inp, wt).numpy())
+    # Router gate GEMM (fp32 out) at the traced N = 320 experts, small M and K.
+    c38 = load_case(root, "case38_ref_musa_asm_bf16_ssgemm_nt_320x256")
+    gen = torch.Generator().manual_seed(38)
+    inp = torch.randn(80, 512, generator=gen).to(torch.bfloat16)
+    wt = torch.randn(c38.N, 512, generator=gen).to(torch.bfloat16)
+    out.update(c38_x=bits(inp), c38_w=bits(wt), c38_y=c38.reference_fp32(inp, wt).numpy())
     # Build-only ops (no reference code): torch fp32 restatements pin the numpy oracle.
     gen = torch.Generator().manual_seed(8)
     y = torch.randn(64, 2 * 96, generator=gen).to(torch.bfloat16)

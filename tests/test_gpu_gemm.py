@@ -111,6 +111,62 @@ def test_swiglu_epilogue_vs_oracle(cuda_dev, splits, f, k):
     assert torch.equal(h, h2)
 
 
+def test_router_gemm_golden(cuda_dev, golden):
+    """case38 bundle (router logits, fp32 out) vs the reference's reference_fp32."""
+    z = golden("gemm_swiglu.npz")
+    y = load_bundle("case38_router_gemm").kernel_function(from_u16(z["c38_x"], cuda_dev),
+                                                          from_u16(z["c38_w"], cuda_dev))
+    assert y.dtype == torch.float32 and tuple(y.shape) == z["c38_y"].shape
+    np.testing.assert_allclose(y.cpu().numpy(), z["c38_y"], rtol=1e-5, atol=1e-4)
+
+
+def test_router_gemm_reference_shape(cuda_dev):
+    """The traced shape M=16384, K=8192, N=320 (case38's make_inputs sizes and
+    N(0,1) inputs), rows checked against float64 sums on the CPU. Bound: the
+    usual GEMM rounding bound |got - exact| <= c * sum_k |x_k| |w_k| with
+    c = 1e-5 (here sum_k |x_k||w_k| ~ 5200 for logits of scale ~90). The
+    tensor cores add each K=16 slice and then 512 partial sums in fp32 with
+    rounding coarser than a sequential round-to-nearest CPU sum, so two fp32
+    evaluations differ by up to ~4e-3 here, beyond the 1e-3 that case38
+    (:71-73) allows between two CPU fp32 evaluations."""
+    import moe_b200
+    m, k, n = 16384, 8192, 320
+    g = torch.Generator(device=cuda_dev).manual_seed(0)
+    inp = torch.randn(m, k, device=cuda_dev, generator=g).to(torch.bfloat16)
+    wt = torch.randn(n, k, device=cuda_dev, generator=g).to(torch.bfloat16)
+    y = moe_b200.router_logits(inp, wt)
+    rng = np.random.default_rng(1)
+    rows = np.unique(np.concatenate([[0, m // 2, m - 1], rng.integers(0, m, 61)]))
+    sel = torch.as_tensor(rows, device=cuda_dev)
+    xs = orc.bf16_to_f32(u16(inp[sel])).astype(np.float64)
+    ws = orc.bf16_to_f32(u16(wt)).astype(np.float64)
+    exact = xs @ ws.T
+    bound = 1e-5 * (np.abs(xs) @ np.abs(ws).T)
+    err = np.abs(y[sel].cpu().numpy().astype(np.float64) - exact)
+    assert (err <= bound).all(), (err.max(), (err / bound).max())
+    # the fp32 oracle (case38 reference_fp32's formula) is within the same bound
+    ref32 = orc.router_logits(u16(inp[sel]), u16(wt)).astype(np.float64)
+    assert (np.abs(ref32 - exact) <= bound).all()
+
+
+@pytest.mark.parametrize("splits,n,k", [([0, 1, 127, 128, 129, 300, 0, 5], 256, 128),
+                                        ([600, 3, 257], 200, 72), ([1], 320, 8192)])
+def test_fp32_epilogue_ragged(cuda_dev, splits, n, k):
+    """fp32 epilogue on ragged groups: whole 256-row tiles and remainders."""
+    import moe_b200
+    g = torch.Generator().manual_seed(sum(splits) + n)
+    x = _rand_bf16(g, sum(splits), k)
+    w = _rand_bf16(g, len(splits), n, k, std=0.05)
+    y = moe_b200.grouped_gemm(x.to(cuda_dev), w.to(cuda_dev), splits, epilogue="fp32")
+    assert y.dtype == torch.float32
+    ref = np.zeros((sum(splits), n), np.float32)
+    off = 0
+    for gi, m in enumerate(splits):
+        ref[off:off + m] = orc.router_logits(u16(x[off:off + m]), u16(w[gi]))
+        off += m
+    np.testing.assert_allclose(y.cpu().numpy(), ref, rtol=1e-5, atol=1e-4)
+
+
 def test_standalone_swiglu_golden(cuda_dev, golden):
     import moe_b200
     z = golden("gemm_swiglu.npz")
@@ -206,9 +262,14 @@ def test_bad_arguments(cuda_dev):
         moe_b200.grouped_gemm(x.float(), w, [8])
 
 
-def test_single_cta_kernel_variant(cuda_dev):
-    """The single-CTA kernel (used when CTA pairs cannot be scheduled, or with
-    MOE_GEMM_PAIR=0) on ragged, SwiGLU and EP-style groups, in a fresh process."""
+@pytest.mark.parametrize("env", [{"MOE_GEMM_PAIR": "0"}, {"MOE_GEMM_SPLIT": "0"}],
+                         ids=["single_cta", "pair_padded_tails"])
+def test_kernel_variants(cuda_dev, env):
+    """The non-default kernel paths, each in a fresh process, on ragged groups
+    with the bf16, SwiGLU and fp32 epilogues: the single-CTA kernel alone (used
+    when CTA pairs cannot be scheduled, or with MOE_GEMM_PAIR=0), and the pair
+    kernel with each group's last partial tile padded to 256 rows instead of
+    handed to the single-CTA kernel (MOE_GEMM_SPLIT=0)."""
     import os
     import subprocess
     import sys
@@ -227,9 +288,11 @@ y = moe_b200.grouped_gemm(x.to(dev), w.to(dev), splits)
 assert_gemm_close(y, fp32_ref(u16(x), u16(w), splits), "1cta plain")
 h = moe_b200.grouped_gemm(x.to(dev), w.to(dev), splits, epilogue="swiglu")
 assert_gemm_close(h, fp32_ref(u16(x), u16(w), splits, swiglu=True), "1cta swiglu", ulp_frac=0.995)
+f = moe_b200.grouped_gemm(x.to(dev), w.to(dev), splits, epilogue="fp32")
+np.testing.assert_allclose(f.cpu().numpy(), fp32_ref(u16(x), u16(w), splits), rtol=1e-5, atol=1e-4)
 print("OK")
 '''
-    env = dict(os.environ, MOE_GEMM_PAIR="0")
+    env = dict(os.environ, **env)
     r = subprocess.run([sys.executable, "-c", code, str(ROOT / "1188b-reference-kernels_b200"),
                         str(ROOT), str(ROOT / "tests")], env=env, capture_output=True, text=True,
                        timeout=300)

@@ -206,6 +206,15 @@ def test_single_expert_gemm_fp32_golden(golden):
     _gemm_close(y, z["c35_y"])
 
 
+def test_router_gemm_fp32_golden(golden):
+    """case38 reference_fp32 (router gate GEMM, fp32 out) at N = 320 experts:
+    both sides accumulate in fp32 and differ only in summation order."""
+    z = golden("gemm_swiglu.npz")
+    y = orc.router_logits(z["c38_x"], z["c38_w"])
+    assert y.dtype == np.float32 and y.shape == z["c38_y"].shape == (80, 320)
+    np.testing.assert_allclose(y, z["c38_y"], rtol=1e-5, atol=1e-4)
+
+
 def test_swiglu_matches_torch_restatement(golden):
     z = golden("gemm_swiglu.npz")
     h = orc.swiglu(z["swiglu_y"])
