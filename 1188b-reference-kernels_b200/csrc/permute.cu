@@ -74,11 +74,13 @@ __global__ void __launch_bounds__(kRowThreads) permute_kernel(
 }
 
 // probs_mode: -1 unweighted, 0 probs[t*E+e], 1 probs[src row].
+// gp_out (optional, [T,E] fp32): the permute backward's prob gradient,
+// gp_out[t,e] = pgrad[src row] for a routed (t,e), else 0.
 template <int VPT, typename IdxT, typename V>
 __global__ void __launch_bounds__(kRowThreads) unpermute_kernel(
     const V* __restrict__ pin, const IdxT* __restrict__ map, const float* __restrict__ probs,
     int probs_mode, V* __restrict__ out, float* __restrict__ acc_out, int64_t T, int E,
-    int nvec, int64_t num_rows) {
+    int nvec, int64_t num_rows, const float* __restrict__ pgrad, float* __restrict__ gp_out) {
   constexpr int kE = VecTraits<V>::kElems;
   __shared__ int64_t s_src[kRowThreads];
   __shared__ float s_w[kRowThreads];
@@ -98,6 +100,7 @@ __global__ void __launch_bounds__(kRowThreads) unpermute_kernel(
     int64_t s = -1;
     if (e < E) s = load_map<IdxT, true>(map, T, E, t, e);
     const bool valid = s >= 0 && s < num_rows;
+    if (gp_out != nullptr && e < E) gp_out[t * E + e] = valid ? __ldg(pgrad + s) : 0.f;
     int pos;
     const int total = compact_window(valid, s_wcnt, pos);
     if (valid) {
@@ -170,7 +173,7 @@ template <bool kTrans, typename IdxT, typename V>
 __global__ void __launch_bounds__(kRowThreads) combine_kernel(
     const V* __restrict__ pin, const IdxT* __restrict__ map, const float* __restrict__ probs,
     int probs_mode, V* __restrict__ out, float* __restrict__ acc_out, int64_t T, int E,
-    int nvec, int64_t num_rows) {
+    int nvec, int64_t num_rows, const float* __restrict__ pgrad, float* __restrict__ gp_out) {
   constexpr int kE = VecTraits<V>::kElems;
   __shared__ int64_t s_src[kCombineMaxE];
   __shared__ float s_w[kCombineMaxE];
@@ -185,6 +188,7 @@ __global__ void __launch_bounds__(kRowThreads) combine_kernel(
     int64_t s = -1;
     if (e < E) s = load_map<IdxT, kTrans>(map, T, E, t, e);
     const bool valid = s >= 0 && s < num_rows;
+    if (gp_out != nullptr && e < E) gp_out[t * E + e] = valid ? __ldg(pgrad + s) : 0.f;
     int pos;
     const int total = compact_window(valid, s_wcnt, pos);  // contains a __syncthreads
     const int base = s_n;
@@ -271,7 +275,7 @@ int launch_permute_v(const void* x, const IdxT* map, const float* probs, void* o
 template <typename IdxT, typename V>
 int launch_unpermute_v(const void* pin, const IdxT* map, const float* probs, int probs_mode,
                        void* out, float* acc_out, int64_t T, int64_t H, int64_t E,
-                       int64_t num_rows, cudaStream_t s) {
+                       int64_t num_rows, cudaStream_t s, const float* pgrad, float* gp_out) {
   const int nvec = static_cast<int>(H / VecTraits<V>::kElems);
   const int vpt = (nvec + kRowThreads - 1) / kRowThreads;
   const V* pv = static_cast<const V*>(pin);
@@ -279,7 +283,8 @@ int launch_unpermute_v(const void* pin, const IdxT* map, const float* probs, int
   const unsigned grid = static_cast<unsigned>(T);
 #define MOE_UNPERMUTE_CASE(VP)                                                           \
   unpermute_kernel<VP, IdxT, V><<<grid, kRowThreads, 0, s>>>(pv, map, probs, probs_mode, ov, \
-                                                             acc_out, T, (int)E, nvec, num_rows)
+                                                             acc_out, T, (int)E, nvec, num_rows, \
+                                                             pgrad, gp_out)
   if (vpt <= 1) MOE_UNPERMUTE_CASE(1);
   else if (vpt <= 2) MOE_UNPERMUTE_CASE(2);
   else if (vpt <= 4) MOE_UNPERMUTE_CASE(4);
@@ -308,11 +313,11 @@ int launch_permute(const void* x, const IdxT* map, const float* probs, void* out
 template <bool kTrans, typename IdxT, typename V>
 int launch_combine_v(const void* pin, const IdxT* map, const float* probs, int probs_mode,
                      void* out, float* acc_out, int64_t T, int64_t H, int64_t E, int64_t num_rows,
-                     cudaStream_t s) {
+                     cudaStream_t s, const float* pgrad, float* gp_out) {
   const int nvec = static_cast<int>(H / VecTraits<V>::kElems);
   combine_kernel<kTrans, IdxT, V><<<static_cast<unsigned>(T), kRowThreads, 0, s>>>(
       static_cast<const V*>(pin), map, probs, probs_mode, static_cast<V*>(out), acc_out, T,
-      (int)E, nvec, num_rows);
+      (int)E, nvec, num_rows, pgrad, gp_out);
   MOE_CUDA_CHECK_LAUNCH("combine launch");
   return MOE_OK;
 }
@@ -320,37 +325,37 @@ int launch_combine_v(const void* pin, const IdxT* map, const float* probs, int p
 template <bool kTrans, typename IdxT>
 int launch_combine(const void* pin, const IdxT* map, const float* probs, int probs_mode,
                    void* out, float* acc_out, int64_t T, int64_t H, int64_t E, int64_t num_rows,
-                   cudaStream_t s) {
+                   cudaStream_t s, const float* pgrad = nullptr, float* gp_out = nullptr) {
   switch (vec_bytes(pin, out, H)) {
     case 16:
       return launch_combine_v<kTrans, IdxT, uint4>(pin, map, probs, probs_mode, out, acc_out, T,
-                                                   H, E, num_rows, s);
+                                                   H, E, num_rows, s, pgrad, gp_out);
     case 4:
       return launch_combine_v<kTrans, IdxT, uint32_t>(pin, map, probs, probs_mode, out, acc_out,
-                                                      T, H, E, num_rows, s);
+                                                      T, H, E, num_rows, s, pgrad, gp_out);
     default:
       return launch_combine_v<kTrans, IdxT, uint16_t>(pin, map, probs, probs_mode, out, acc_out,
-                                                      T, H, E, num_rows, s);
+                                                      T, H, E, num_rows, s, pgrad, gp_out);
   }
 }
 
 template <typename IdxT>
 int launch_unpermute(const void* pin, const IdxT* map, const float* probs, int probs_mode,
                      void* out, float* acc_out, int64_t T, int64_t H, int64_t E, int64_t num_rows,
-                     cudaStream_t s) {
+                     cudaStream_t s, const float* pgrad = nullptr, float* gp_out = nullptr) {
   if (E <= kCombineMaxE)
     return launch_combine<true, IdxT>(pin, map, probs, probs_mode, out, acc_out, T, H, E,
-                                      num_rows, s);
+                                      num_rows, s, pgrad, gp_out);
   switch (vec_bytes(pin, out, H)) {
     case 16:
       return launch_unpermute_v<IdxT, uint4>(pin, map, probs, probs_mode, out, acc_out, T, H, E,
-                                             num_rows, s);
+                                             num_rows, s, pgrad, gp_out);
     case 4:
       return launch_unpermute_v<IdxT, uint32_t>(pin, map, probs, probs_mode, out, acc_out, T, H,
-                                                E, num_rows, s);
+                                                E, num_rows, s, pgrad, gp_out);
     default:
       return launch_unpermute_v<IdxT, uint16_t>(pin, map, probs, probs_mode, out, acc_out, T, H,
-                                                E, num_rows, s);
+                                                E, num_rows, s, pgrad, gp_out);
   }
 }
 
@@ -425,6 +430,33 @@ extern "C" int moe_unpermute_mask(const void* pin, const void* row_id_map_et, in
                                      out, acc_out, T, H, E, num_rows, s);
   return launch_unpermute<int32_t>(pin, static_cast<const int32_t*>(row_id_map_et), probs, mode,
                                    out, acc_out, T, H, E, num_rows, s);
+}
+
+extern "C" int moe_permute_backward(const void* grad_permuted, const void* row_id_map_et,
+                                    int32_t idx_bits, const float* permuted_probs_grad,
+                                    void* grad_x, float* acc_out, float* grad_probs, int64_t T,
+                                    int64_t H, int64_t E, int64_t num_rows, moe_stream_t stream) {
+  int st = check_row_args("permute_backward", grad_permuted, grad_x, T, H, E);
+  if (st) return st;
+  MOE_REQUIRE(idx_bits == 32 || idx_bits == 64, "permute_backward: idx_bits must be 32 or 64");
+  MOE_REQUIRE(num_rows >= 0, "permute_backward: num_rows=%lld < 0", (long long)num_rows);
+  MOE_REQUIRE((grad_probs == nullptr) == (permuted_probs_grad == nullptr),
+              "permute_backward: grad_probs and permuted_probs_grad go together");
+  MOE_REQUIRE(((reinterpret_cast<uintptr_t>(acc_out) | reinterpret_cast<uintptr_t>(grad_probs)) &
+               3) == 0,
+              "permute_backward: acc_out and grad_probs must be 4-byte aligned");
+  if (T == 0) return MOE_OK;
+  MOE_REQUIRE(row_id_map_et && (grad_permuted || num_rows == 0) && (grad_x || H == 0),
+              "permute_backward: null pointer");
+  if (H == 0 && grad_probs == nullptr) return MOE_OK;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (idx_bits == 64)
+    return launch_unpermute<int64_t>(grad_permuted, static_cast<const int64_t*>(row_id_map_et),
+                                     nullptr, -1, grad_x, acc_out, T, H, E, num_rows, s,
+                                     permuted_probs_grad, grad_probs);
+  return launch_unpermute<int32_t>(grad_permuted, static_cast<const int32_t*>(row_id_map_et),
+                                   nullptr, -1, grad_x, acc_out, T, H, E, num_rows, s,
+                                   permuted_probs_grad, grad_probs);
 }
 
 extern "C" int moe_swiglu(const void* y, void* h, int64_t M, int64_t F, moe_stream_t stream) {

@@ -378,6 +378,49 @@ def grouped_gemm(x: torch.Tensor, w: torch.Tensor,
     return out
 
 
+def permute_backward(grad_permuted: torch.Tensor, row_id_map: torch.Tensor,
+                     permuted_probs_grad: Optional[torch.Tensor] = None,
+                     return_acc: bool = False):
+    """Backward of the permute with an [E,T] map (int64 or int32).
+
+    grad_x[t] = bf16(sum over e ascending of fp32(grad_permuted[row_id_map[e,t]]))
+    and, with permuted_probs_grad [rows] fp32, grad_probs[t,e] =
+    permuted_probs_grad[row_id_map[e,t]] for a routed (t,e), else 0 —
+    kernel_cases/case18_moe_permute_bwd_unpermute_mask.py:56-70 (int64 map)
+    and case32_ref_moe_unpermute_mask_kernel.py:47-79 (int32 map, which also
+    returns the fp32 sums). One kernel: the unweighted combine that also
+    gathers the prob gradient while it reads the map.
+
+    Returns (grad_x, grad_probs), with the fp32 sums first when return_acc:
+    (acc, grad_x, grad_probs); grad_probs is None without permuted_probs_grad.
+    """
+    for n_, t_ in (("grad_permuted", grad_permuted), ("row_id_map", row_id_map),
+                   ("permuted_probs_grad", permuted_probs_grad)):
+        _need_cuda(n_, t_)
+    if row_id_map.dim() != 2 or grad_permuted.dim() != 2:
+        raise ValueError(f"shapes grad_permuted {tuple(grad_permuted.shape)} "
+                         f"row_id_map {tuple(row_id_map.shape)}")
+    _need_dtype("grad_permuted", grad_permuted, torch.bfloat16)
+    _need_dtype("row_id_map", row_id_map, torch.int64, torch.int32)
+    e, t = row_id_map.shape
+    gc = grad_permuted.contiguous()
+    mc = row_id_map.contiguous()
+    rows, h = gc.shape
+    pg = None
+    gp = None
+    if permuted_probs_grad is not None:
+        _need_dtype("permuted_probs_grad", permuted_probs_grad, torch.float32)
+        if permuted_probs_grad.shape != (rows,):
+            raise ValueError(f"permuted_probs_grad must be [{rows}]")
+        pg = permuted_probs_grad.contiguous()
+        gp = torch.empty((t, e), dtype=torch.float32, device=gc.device)
+    gx = torch.empty((t, h), dtype=gc.dtype, device=gc.device)
+    acc = torch.empty((t, h), dtype=torch.float32, device=gc.device) if return_acc else None
+    _lib.call("moe_permute_backward", _p(gc), _p(mc), 64 if mc.dtype == torch.int64 else 32,
+              _p(pg), _p(gx), _p(acc), _p(gp), t, h, e, rows, _stream(gc.device))
+    return (acc, gx, gp) if return_acc else (gx, gp)
+
+
 def router_logits(x: torch.Tensor, weight: torch.Tensor,
                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Router gate GEMM: logits [T,E] fp32 = x [T,H] bf16 @ weight [E,H] bf16 ^T,

@@ -142,6 +142,17 @@ int moe_unpermute_mask(const void* pin, const void* row_id_map_et, int32_t idx_b
                        const float* probs, int32_t probs_mode, void* out, float* acc_out,
                        int64_t T, int64_t H, int64_t E, int64_t num_rows, moe_stream_t stream);
 
+/* Backward of the permute (kernel_cases/case18_moe_permute_bwd_unpermute_   */
+/* mask.py:56-70 with an int64 map, case32_ref_moe_unpermute_mask_kernel.py: */
+/* 47-79 with an int32 map): grad_x[t] = bf16(sum over e ascending of        */
+/* fp32(grad_permuted[map[e,t]])) (acc_out, optional, the fp32 sums), and    */
+/* grad_probs[t,e] = permuted_probs_grad[map[e,t]] for a routed (t,e), else  */
+/* 0 (both optional, together; [T,E] fp32).                                  */
+int moe_permute_backward(const void* grad_permuted, const void* row_id_map_et, int32_t idx_bits,
+                         const float* permuted_probs_grad, void* grad_x, float* acc_out,
+                         float* grad_probs, int64_t T, int64_t H, int64_t E, int64_t num_rows,
+                         moe_stream_t stream);
+
 /* Same combine driven by the token-major [T,E] int64 map (the layout         */
 /* kernel_cases/case12_moe_row_id_map_pass2.py:61 returns second), whose     */
 /* entries for one token are contiguous. Identical results. E <= 1024.       */

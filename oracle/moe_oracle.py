@@ -206,6 +206,26 @@ def unpermute(pin_u16: np.ndarray, row_et: np.ndarray, probs: np.ndarray | None 
 # --------------------------------------------------------------------------- a9-a11 GEMM
 
 
+def permute_backward(grad_u16: np.ndarray, row_et: np.ndarray, pgrad: np.ndarray | None = None):
+    """Backward of the permute with an [E,T] map: the unweighted unpermute of
+    the row gradients and the prob gradient gathered onto [token, expert].
+
+    kernel_cases/case18_moe_permute_bwd_unpermute_mask.py:56-70 (int64 map)
+    and case32_ref_moe_unpermute_mask_kernel.py:47-79 (int32 map): acc[t] =
+    sum over e ascending of fp32 rows, out = bf16(acc), grad_probs[t,e] =
+    pgrad[row[e,t]] where routed, else 0.
+    Returns (acc fp32, out bf16 bits, grad_probs fp32 [T,E] or None).
+    """
+    acc, out = unpermute(grad_u16, row_et)
+    gp = None
+    if pgrad is not None:
+        row = np.asarray(row_et).astype(np.int64)
+        gp = np.zeros((row.shape[1], row.shape[0]), dtype=np.float32)
+        m = row >= 0
+        gp.T[m] = np.asarray(pgrad, dtype=np.float32)[row[m]]
+    return acc, out, gp
+
+
 def group_sizes(total: int, groups: int):
     """Uniform split, kernel_cases/case03_moe_grouped_gemm_fc1_fwd.py:43-46."""
     base, rem = divmod(total, groups)

@@ -25,6 +25,23 @@ def case15_pin(rows: int, hidden: int = 8192) -> torch.Tensor:
     return torch.randn(rows, hidden, generator=g).to(torch.bfloat16)
 
 
+CASE18_SEED = 20261118
+
+
+def case18_inputs(tokens: int = 4096, hidden: int = 8192, experts: int = 320, topk: int = 8):
+    """Seeded draws in the form of case18's get_inputs (kernel_cases/case18_moe_
+    permute_bwd_unpermute_mask.py:77-84): random top-k routing [T,E] bool,
+    N(0,1) gradients of the permuted rows [T*k,H] bf16 and of the permuted
+    probs [T*k] fp32."""
+    g = torch.Generator().manual_seed(CASE18_SEED)
+    rm = torch.zeros(tokens, experts, dtype=torch.bool)
+    idx = torch.argsort(torch.rand(tokens, experts, generator=g), dim=-1)[:, :topk]
+    rm.scatter_(1, idx, True)
+    dperm = torch.randn(tokens * topk, hidden, generator=g).to(torch.bfloat16)
+    dpp = torch.randn(tokens * topk, generator=g, dtype=torch.float32)
+    return rm, dperm, dpp
+
+
 def _randn(seed: int, m: int, n: int) -> torch.Tensor:
     g = torch.Generator().manual_seed(seed)
     return torch.randn(m, n, generator=g, dtype=torch.float32)

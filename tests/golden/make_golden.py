@@ -228,6 +228,41 @@ def gen_gemm(root: Path) -> None:
     save("gemm_swiglu.npz", **out)
 
 
+def gen_permute_bwd(root: Path) -> None:
+    """Backward of the permute: case18 Model (int64 map) at its own shape and
+    small, case32 reference_unpermute_mask (int32 map) on its KAT and medium."""
+    c18 = load_case(root, "case18_moe_permute_bwd_unpermute_mask")
+    c32 = load_case(root, "case32_ref_moe_unpermute_mask_kernel")
+    rm, dperm, dpp = gi.case18_inputs()
+    row = c18.make_row_id_map_trans(rm)
+    dact, dprobs = c18.Model(rm.shape[1])(dperm, dpp, row)
+    out = {"full_rmap_packed": np.packbits(rm.numpy(), axis=1),
+           "full_shape": np.array([rm.shape[0], dperm.shape[1], rm.shape[1], 8]),
+           "full_sha_dperm": np.array(sha(dperm)), "full_sha_dpp": np.array(sha(dpp)),
+           "full_sha_dact": np.array(sha(dact)), "full_sha_dprobs": np.array(sha(dprobs))}
+    rm_s, dperm_s, dpp_s = gi.case18_inputs(tokens=48, hidden=64, experts=12, topk=3)
+    row_s = c18.make_row_id_map_trans(rm_s)
+    da, dp = c18.Model(12)(dperm_s, dpp_s, row_s)
+    out.update(s18_dperm=bits(dperm_s), s18_dpp=dpp_s.numpy(), s18_map=row_s.numpy(),
+               s18_dact=bits(da), s18_dprobs=dp.numpy())
+    # case32 known answer (its _check_sum_and_prob_grad inputs) and a medium run
+    gin = torch.tensor([[4, 1], [4, 1], [7, 0]], dtype=torch.bfloat16)
+    kmap = torch.tensor([[0, -1], [-1, 2], [1, -1], [-1, -1]], dtype=torch.int32)
+    kpg = torch.tensor([10.0, 20.0, 30.0])
+    acc, stored, gathered = c32.reference_unpermute_mask(gin, kmap, kpg)
+    out.update(k32_in=bits(gin), k32_map=kmap.numpy(), k32_pg=kpg.numpy(), k32_acc=acc.numpy(),
+               k32_out=bits(stored), k32_gp=gathered.numpy())
+    mmap = c32.make_row_id_map(num_tokens=100, num_experts=24, topk=5)
+    r = int(mmap.max()) + 1
+    g = torch.Generator().manual_seed(32)
+    gin = torch.randn(r, 128, generator=g).to(torch.bfloat16)
+    pg = torch.randn(r, generator=g)
+    acc, stored, gathered = c32.reference_unpermute_mask(gin, mmap, pg)
+    out.update(m32_in=bits(gin), m32_map=mmap.numpy(), m32_pg=pg.numpy(), m32_acc=acc.numpy(),
+               m32_out=bits(stored), m32_gp=gathered.numpy())
+    save("permute_bwd.npz", **out)
+
+
 def gen_router_combine() -> None:
     """Torch fp32 restatements of the build-only router and weighted combine."""
     out = {}
@@ -276,6 +311,7 @@ def main() -> None:
     gen_case23(args.reference_root)
     gen_gemm(args.reference_root)
     gen_router_combine()
+    gen_permute_bwd(args.reference_root)
 
 
 if __name__ == "__main__":

@@ -239,3 +239,50 @@ def test_odd_hidden_sizes(cuda_dev, h):
     out2, _ = moe_b200.permute(xs, torch.from_numpy(te).to(cuda_dev), None, num_out=n)
     ref2, _ = orc.permute(u16(xs), te, None, n)
     np.testing.assert_array_equal(u16(out2), ref2)
+
+
+# ------------------------------------------------------------------ f3 permute backward
+def test_permute_backward_goldens(cuda_dev, golden):
+    """case18 bundle (int64 map) small; case32 bundle (int32 map) on its KAT and
+    a medium run: bit-exact sums, bf16 outputs and gathered prob gradients."""
+    z = golden("permute_bwd.npz")
+    k18 = load_bundle("case18_moe_permute_bwd_unpermute_mask")
+    dact, dprobs = k18.kernel_function(from_u16(z["s18_dperm"], cuda_dev),
+                                       torch.from_numpy(z["s18_dpp"]).to(cuda_dev),
+                                       torch.from_numpy(z["s18_map"]).to(cuda_dev))
+    assert dact.dtype == torch.bfloat16 and dprobs.dtype == torch.float32
+    np.testing.assert_array_equal(u16(dact), z["s18_dact"])
+    np.testing.assert_array_equal(dprobs.cpu().numpy(), z["s18_dprobs"])
+    k32 = load_bundle("case32_moe_unpermute_mask_kernel")
+    for tag in ("k32", "m32"):
+        acc, out, gp = k32.kernel_function(from_u16(z[f"{tag}_in"], cuda_dev),
+                                           torch.from_numpy(z[f"{tag}_map"]).to(cuda_dev),
+                                           torch.from_numpy(z[f"{tag}_pg"]).to(cuda_dev))
+        np.testing.assert_array_equal(acc.cpu().numpy(), z[f"{tag}_acc"], err_msg=tag)
+        np.testing.assert_array_equal(u16(out), z[f"{tag}_out"], err_msg=tag)
+        np.testing.assert_array_equal(gp.cpu().numpy(), z[f"{tag}_gp"], err_msg=tag)
+
+
+def test_permute_backward_full_reference_shape(cuda_dev, golden):
+    """case18 at its own shape (T=4096, H=8192, E=320, top-8), SHA-256 equal."""
+    z = golden("permute_bwd.npz")
+    t, h, e, k = (int(v) for v in z["full_shape"])
+    rm, dperm, dpp = gi.case18_inputs(t, h, e, k)
+    assert sha(dperm) == str(z["full_sha_dperm"]), "torch RNG differs from the fixture's"
+    et = load_bundle("case12_moe_row_id_map_pass2").kernel_function(rm.to(cuda_dev))[0]
+    dact, dprobs = load_bundle("case18_moe_permute_bwd_unpermute_mask").kernel_function(
+        dperm.to(cuda_dev), dpp.to(cuda_dev), et)
+    assert sha(dact) == str(z["full_sha_dact"])
+    assert sha(dprobs) == str(z["full_sha_dprobs"])
+
+
+def test_permute_backward_bad_arguments(cuda_dev):
+    import moe_b200
+    g = torch.zeros(8, 16, dtype=torch.bfloat16, device=cuda_dev)
+    m = torch.full((4, 2), -1, dtype=torch.int64, device=cuda_dev)
+    with pytest.raises(ValueError):
+        moe_b200.permute_backward(g, m, torch.zeros(7, device=cuda_dev))  # wrong length
+    with pytest.raises(ValueError):
+        moe_b200.permute_backward(g.float(), m)
+    gx, gp = moe_b200.permute_backward(g, m)  # nothing routed: zeros, no prob grad
+    assert gp is None and int(gx.view(torch.int16).abs().sum()) == 0

@@ -215,6 +215,34 @@ def test_router_gemm_fp32_golden(golden):
     np.testing.assert_allclose(y, z["c38_y"], rtol=1e-5, atol=1e-4)
 
 
+def test_permute_backward_goldens(golden):
+    """case18 Model (int64 map) small, case32 KAT and medium (int32 map): the
+    fp32 sums, the bf16 outputs and the gathered prob gradients, bit for bit."""
+    z = golden("permute_bwd.npz")
+    acc, out, gp = orc.permute_backward(z["s18_dperm"], z["s18_map"], z["s18_dpp"])
+    np.testing.assert_array_equal(out, z["s18_dact"])
+    np.testing.assert_array_equal(gp, z["s18_dprobs"])
+    for tag in ("k32", "m32"):
+        acc, out, gp = orc.permute_backward(z[f"{tag}_in"], z[f"{tag}_map"], z[f"{tag}_pg"])
+        np.testing.assert_array_equal(acc, z[f"{tag}_acc"], err_msg=tag)
+        np.testing.assert_array_equal(out, z[f"{tag}_out"], err_msg=tag)
+        np.testing.assert_array_equal(gp, z[f"{tag}_gp"], err_msg=tag)
+
+
+def test_permute_backward_full_reference_shape(golden):
+    """case18 at its own shape (T=4096, H=8192, E=320, top-8), SHA-256 equal."""
+    z = golden("permute_bwd.npz")
+    t, h, e, k = (int(v) for v in z["full_shape"])
+    rm, dperm, dpp = gi.case18_inputs(t, h, e, k)
+    assert sha(dperm) == str(z["full_sha_dperm"]) and sha(dpp) == str(z["full_sha_dpp"])
+    assert (np.unpackbits(z["full_rmap_packed"], axis=1)[:, :e].astype(bool) == rm.numpy()).all()
+    et, _, _, _ = orc.row_id_map(rm.numpy())
+    _, out, gp = orc.permute_backward(dperm.view(torch.int16).numpy().view(np.uint16), et,
+                                      dpp.numpy())
+    assert hashlib.sha256(out.tobytes()).hexdigest() == str(z["full_sha_dact"])
+    assert hashlib.sha256(gp.tobytes()).hexdigest() == str(z["full_sha_dprobs"])
+
+
 def test_swiglu_matches_torch_restatement(golden):
     z = golden("gemm_swiglu.npz")
     h = orc.swiglu(z["swiglu_y"])
