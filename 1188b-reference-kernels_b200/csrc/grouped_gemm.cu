@@ -70,6 +70,8 @@ struct Params {
   int num_kb;
   int n_tiles;
   int bn;        // pair kernel: N-tile width (256; narrower for epilogues 0/2 when N % 256 != 0)
+  int b_mn;      // 1: w is [num_w, K, N] (out = x @ w[g]), B staged MN-major
+  int k_rows;    // K: reduction rows of one weight matrix when b_mn
   int epilogue;  // 0 bf16 out, 1 SwiGLU -> bf16, 2 fp32 out
   int raster;   // pair kernel: pair M-tiles per raster super-row
   int l2_mode;  // pair kernel: 0 both evict_normal, 1 B evict_first, 2 A evict_last + B evict_first
@@ -227,9 +229,12 @@ __global__ void __launch_bounds__(kThreads, 1)
         Tile tile;
         if (!walker.locate(t, tile)) break;
         const int row0 = p.row_start[tile.g] + tile.m_idx * BM;
-        const int wbase = p.widx[tile.g] * p.n_w;
+        const int wbase = p.widx[tile.g] * (p.b_mn ? p.k_rows : p.n_w);
         int b0, b1;
-        if (p.epilogue == 1) {
+        if (p.b_mn) {
+          b0 = tile.n_idx * BN;  // first output column; rows follow kb
+          b1 = 0;
+        } else if (p.epilogue == 1) {
           b0 = wbase + tile.n_idx * 128;
           b1 = b0 + p.f_half;
         } else {
@@ -245,8 +250,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sb = sa + kABytes;
           mbar_arrive_expect_tx(full_bar(stage), kStageBytes);
           tma_load_2d(sa, &tmap_a, kb * BK, row0, full_bar(stage), pol_a);
-          tma_load_2d(sb, &tmap_b, kb * BK, b0, full_bar(stage), pol_b);
-          tma_load_2d(sb + kBHalfBytes, &tmap_b, kb * BK, b1, full_bar(stage), pol_b);
+          if (p.b_mn) {
+            // four 64-column x 64-row boxes of w[g] (rows = reduction index)
+#pragma unroll
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_2d(sb + j * 8192u, &tmap_b, b0 + j * 64, wbase + kb * BK, full_bar(stage),
+                          pol_b);
+          } else {
+            tma_load_2d(sb, &tmap_b, kb * BK, b0, full_bar(stage), pol_b);
+            tma_load_2d(sb + kBHalfBytes, &tmap_b, kb * BK, b1, full_bar(stage), pol_b);
+          }
           issued[stage] = static_cast<int>(phase);
           if (++stage == kStages) {
             stage = 0;
@@ -265,7 +278,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      const uint32_t idesc = umma_idesc_bf16_f32(BM, BN);
+      const uint32_t idesc = umma_idesc_bf16_f32(BM, BN) | (p.b_mn ? kIdescBMajorMN : 0u);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -291,13 +304,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sa = base + stage * kStageBytes;
           const uint32_t sb = sa + kABytes;
           const uint64_t ad = umma_desc_k_sw128(sa);
-          const uint64_t bd = umma_desc_k_sw128(sb);
+          const uint64_t bd = p.b_mn ? umma_desc_mn_sw128(sb, 8192u) : umma_desc_k_sw128(sb);
+          // K-major: +32 bytes along K inside the 128-byte swizzle atom (+2 in
+          // 16-byte units); MN-major B: +16 rows = two 1024-byte K groups (+128).
+          const uint64_t bstep = p.b_mn ? 128ull : 2ull;
 #pragma unroll
-          for (int k = 0; k < BK / 16; ++k) {
-            // +32 bytes along K inside the 128-byte swizzle atom = +2 in the
-            // 16-byte-unit start-address field.
-            umma_bf16(d_tmem, ad + 2ull * k, bd + 2ull * k, idesc, (kb | k) != 0 ? 1u : 0u);
-          }
+          for (int k = 0; k < BK / 16; ++k)
+            umma_bf16(d_tmem, ad + 2ull * k, bd + bstep * k, idesc, (kb | k) != 0 ? 1u : 0u);
           issued_any = true;
           umma_commit(empty_bar(stage));
           if (++stage == kStages) {
@@ -523,6 +536,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       // Coordinates of this CTA's A rows and B rows for a tile.
       auto coords = [&](const Tile& tl, int& ra, int& rb) {
         ra = p.row_start[tl.g] + tl.m_idx * pairk::kPairTileM + static_cast<int>(rank) * 128;
+        if (p.b_mn) {  // first output column of this CTA's half; rows follow kb
+          rb = tl.n_idx * p.bn + static_cast<int>(rank) * (p.bn / 2);
+          return;
+        }
         const int wb = p.widx[tl.g] * p.n_w;
         rb = (p.epilogue == 1) ? wb + tl.n_idx * 128 + static_cast<int>(rank) * p.f_half
                                : wb + tl.n_idx * p.bn + static_cast<int>(rank) * (p.bn / 2);
@@ -544,7 +561,14 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t leader_full = map_to_rank(full_bar(stage), 0);
           if (leader) mbar_arrive_expect_tx(full_bar(stage), tx);
           tma_load_2d_pair(sa, &tmap_a, kb * BK, row0, leader_full, pol_a);
-          tma_load_2d_pair(sb, &tmap_b, kb * BK, b0, leader_full, pol_b);
+          if (p.b_mn) {
+            const int wrow = p.widx[tile.g] * p.k_rows + kb * BK;
+#pragma unroll
+            for (int j = 0; j < 2; ++j)  // this CTA's 128 columns as two 64-column boxes
+              tma_load_2d_pair(sb + j * 8192u, &tmap_b, b0 + j * 64, wrow, leader_full, pol_b);
+          } else {
+            tma_load_2d_pair(sb, &tmap_b, kb * BK, b0, leader_full, pol_b);
+          }
           issued[stage] = static_cast<int>(phase);
           if (++stage == pairk::kPairStages) {
             stage = 0;
@@ -574,7 +598,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader)
     if (leader && lane == 0) {
-      const uint32_t idesc = umma_idesc_bf16_f32(pairk::kPairTileM, p.bn);
+      const uint32_t idesc =
+          umma_idesc_bf16_f32(pairk::kPairTileM, p.bn) | (p.b_mn ? kIdescBMajorMN : 0u);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
@@ -600,10 +625,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sa = base + stage * pairk::kPairStageBytes;
           const uint32_t sb = sa + pairk::kPairABytes;
           const uint64_t ad = umma_desc_k_sw128(sa);
-          const uint64_t bd = umma_desc_k_sw128(sb);
+          const uint64_t bd = p.b_mn ? umma_desc_mn_sw128(sb, 8192u) : umma_desc_k_sw128(sb);
+          const uint64_t bstep = p.b_mn ? 128ull : 2ull;  // see grouped_gemm_kernel
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
-            umma_bf16_pair(d_tmem, ad + 2ull * k, bd + 2ull * k, idesc, (kb | k) != 0 ? 1u : 0u);
+            umma_bf16_pair(d_tmem, ad + 2ull * k, bd + bstep * k, idesc, (kb | k) != 0 ? 1u : 0u);
           issued_any = true;
           umma_commit_pair(empty_bar(stage), 0x3);
           if (++stage == pairk::kPairStages) {
@@ -1037,11 +1063,15 @@ extern "C" int moe_grouped_gemm_plan_ep(const int32_t* counts, int64_t num_src, 
   return MOE_OK;
 }
 
-extern "C" int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t x_rows, int64_t G,
-                                int64_t num_w, int64_t N, int64_t K, int32_t epilogue,
-                                const void* workspace, size_t workspace_bytes,
-                                moe_stream_t stream) {
+// b_mn = 0: w [num_w, N, K], out = x @ w[g]^T; b_mn = 1: w [num_w, K, N],
+// out = x @ w[g] (B staged MN-major; bf16 or fp32 output, no SwiGLU).
+static int grouped_gemm_run(const void* x, const void* w, void* out, int64_t x_rows, int64_t G,
+                            int64_t num_w, int64_t N, int64_t K, int32_t epilogue,
+                            const void* workspace, size_t workspace_bytes, moe_stream_t stream,
+                            int b_mn) {
   MOE_REQUIRE(epilogue >= 0 && epilogue <= 2, "grouped_gemm: epilogue must be 0, 1 or 2");
+  MOE_REQUIRE(!b_mn || epilogue != 1, "grouped_gemm_nn: no SwiGLU epilogue");
+  MOE_REQUIRE(!b_mn || num_w * K < (1ll << 31), "grouped_gemm_nn: num_w*K too large");
   MOE_REQUIRE(G >= 1 && num_w >= 1, "grouped_gemm: G=%lld num_w=%lld", (long long)G,
               (long long)num_w);
   MOE_REQUIRE(x_rows >= 0 && x_rows < (1ll << 31), "grouped_gemm: x_rows=%lld out of range",
@@ -1065,7 +1095,11 @@ extern "C" int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t
   CUtensorMap ta, tb;
   st = gg::make_tmap(&ta, x, static_cast<uint64_t>(K), static_cast<uint64_t>(x_rows));
   if (st) return st;
-  st = gg::make_tmap(&tb, w, static_cast<uint64_t>(K), static_cast<uint64_t>(num_w * N));
+  if (b_mn)  // w viewed as [num_w*K, N]: 64-column x 64-row boxes, rows = reduction index
+    st = gg::make_tmap_box(&tb, w, static_cast<uint64_t>(N), static_cast<uint64_t>(num_w * K), 64u,
+                           64u, CU_TENSOR_MAP_SWIZZLE_128B);
+  else
+    st = gg::make_tmap(&tb, w, static_cast<uint64_t>(K), static_cast<uint64_t>(num_w * N));
   if (st) return st;
 
   gg::WsLayout l = gg::ws_layout(workspace, G);
@@ -1089,6 +1123,8 @@ extern "C" int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t
     p.n_tiles = static_cast<int>((N + gg::BN - 1) / gg::BN);
   }
   p.bn = gg::BN;
+  p.b_mn = b_mn;
+  p.k_rows = static_cast<int>(K);
   p.num_kb = static_cast<int>((K + gg::BK - 1) / gg::BK);
   static const int raster = gg::env_int("MOE_GEMM_RASTER", gg::pairk::kPairRaster, 1, 64);
   static const int l2_mode = gg::env_int("MOE_GEMM_L2", 0, 0, 2);
@@ -1123,7 +1159,7 @@ extern "C" int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t
     // multiple of 32), e.g. 320 -> 2 x 160 rather than 256 + a 64-column tile
     // padded to 256. The B box of the pair then holds bn/2 rows per CTA.
     CUtensorMap tbp = tb;
-    if (epilogue != 1) {
+    if (epilogue != 1 && !b_mn) {
       const int nt = static_cast<int>((N + gg::BN - 1) / gg::BN);
       const int per = static_cast<int>((N + nt - 1) / nt);
       pb.bn = std::min(gg::BN, (per + 31) / 32 * 32);
@@ -1152,6 +1188,22 @@ extern "C" int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t
                             reinterpret_cast<cudaStream_t>(stream)>>>(ta, tb, p);
   MOE_CUDA_CHECK_LAUNCH("grouped_gemm launch");
   return MOE_OK;
+}
+
+extern "C" int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t x_rows, int64_t G,
+                                int64_t num_w, int64_t N, int64_t K, int32_t epilogue,
+                                const void* workspace, size_t workspace_bytes,
+                                moe_stream_t stream) {
+  return grouped_gemm_run(x, w, out, x_rows, G, num_w, N, K, epilogue, workspace,
+                          workspace_bytes, stream, 0);
+}
+
+extern "C" int moe_grouped_gemm_nn(const void* x, const void* w, void* out, int64_t x_rows,
+                                   int64_t G, int64_t num_w, int64_t N, int64_t K,
+                                   int32_t epilogue, const void* workspace,
+                                   size_t workspace_bytes, moe_stream_t stream) {
+  return grouped_gemm_run(x, w, out, x_rows, G, num_w, N, K, epilogue, workspace,
+                          workspace_bytes, stream, 1);
 }
 
 extern "C" int moe_grouped_gemm_check(const void* workspace, size_t workspace_bytes,

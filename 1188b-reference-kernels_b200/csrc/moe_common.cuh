@@ -244,6 +244,20 @@ MOE_DEVICE uint64_t umma_desc_k_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// UMMA shared-memory matrix descriptor for an MN-major operand tile staged as
+// 64-element (128-byte) rows along MN, one row per K index, 128-byte swizzled:
+// 8-row K groups 1024 bytes apart (stride byte offset) and 64-element MN
+// chunks `mn_chunk_bytes` apart (leading byte offset), descriptor version 1.
+MOE_DEVICE uint64_t umma_desc_mn_sw128(uint32_t smem_addr, uint32_t mn_chunk_bytes) {
+  uint64_t d = 0;
+  d |= static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu);             // start address
+  d |= static_cast<uint64_t>((mn_chunk_bytes >> 4) & 0x3FFFu) << 16;  // leading byte offset
+  d |= static_cast<uint64_t>(1024u >> 4) << 32;                        // stride byte offset
+  d |= static_cast<uint64_t>(1u) << 46;                                // version (sm_100)
+  d |= static_cast<uint64_t>(2u) << 61;                                // SWIZZLE_128B
+  return d;
+}
+
 // Instruction descriptor, kind::f16: D fp32, A/B bf16, both K-major.
 __host__ __device__ constexpr uint32_t umma_idesc_bf16_f32(int m, int n) {
   return (1u << 4)                                 // D format: f32
@@ -252,6 +266,8 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16_f32(int m, int n) {
          | (static_cast<uint32_t>(n >> 3) << 17)   // N / 8
          | (static_cast<uint32_t>(m >> 4) << 24);  // M / 16
 }
+// Bit 16 of the instruction descriptor: B is MN-major.
+constexpr uint32_t kIdescBMajorMN = 1u << 16;
 
 // ---------------------------------------------------------------------------
 // CTA-pair (cluster of 2) helpers for the cta_group::2 GEMM.

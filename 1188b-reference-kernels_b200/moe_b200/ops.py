@@ -330,7 +330,7 @@ def grouped_gemm(x: torch.Tensor, w: torch.Tensor,
                  m_splits: Union[None, Sequence[int], torch.Tensor] = None,
                  epilogue: str = "none", align: int = 1,
                  plan: Optional[GroupedGemmPlan] = None,
-                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+                 out: Optional[torch.Tensor] = None, w_layout: str = "NK") -> torch.Tensor:
     """out = cat_g(x[seg_g] @ w[g].T) on tcgen05 tensor cores (bf16, fp32 accumulate).
 
     x [rows,K] bf16, w [G,N,K] bf16 ("[out,in]" as in case03/case04). With
@@ -339,19 +339,30 @@ def grouped_gemm(x: torch.Tensor, w: torch.Tensor,
     accumulator, [rows,N] float32. m_splits defaults to the uniform split of
     kernel_cases/case03_moe_grouped_gemm_fc1_fwd.py:43-46. A prebuilt plan
     (device group table) skips the planning launch.
+
+    w_layout="KN": w is [G,K,N] and out = cat_g(x[seg_g] @ w[g]) — the
+    grouped dgrad dx = dy @ W of kernel_cases/case07/08_moe_grouped_gemm_fc*_
+    dgrad.py:49-64 (case13/19 with one group), with the forward weight tensor
+    as it is; the weight operand is staged MN-major (no transposed copy).
     """
     for n_, t_ in (("x", x), ("w", w)):
         _need_cuda(n_, t_)
         _need_dtype(n_, t_, torch.bfloat16)
-    if x.dim() != 2 or w.dim() != 3 or x.shape[1] != w.shape[2]:
-        raise ValueError(f"shapes x {tuple(x.shape)} w {tuple(w.shape)}")
+    if w_layout not in ("NK", "KN"):
+        raise ValueError("w_layout must be 'NK' (w [G,N,K]) or 'KN' (w [G,K,N])")
+    kdim = 2 if w_layout == "NK" else 1
+    if x.dim() != 2 or w.dim() != 3 or x.shape[1] != w.shape[kdim]:
+        raise ValueError(f"shapes x {tuple(x.shape)} w {tuple(w.shape)} ({w_layout})")
+    if w_layout == "KN" and epilogue == "swiglu":
+        raise ValueError("the SwiGLU epilogue needs w_layout 'NK'")
     codes = {"none": 0, "swiglu": 1, "fp32": 2}
     if epilogue not in codes:
         raise ValueError("epilogue must be 'none', 'swiglu' or 'fp32'")
     xc = x.contiguous()
     wc = w.contiguous()
     rows, k = xc.shape
-    g, n, _ = wc.shape
+    g = wc.shape[0]
+    n = wc.shape[1] if w_layout == "NK" else wc.shape[2]
     dev = xc.device
     if plan is None:
         if m_splits is None:
@@ -373,8 +384,9 @@ def grouped_gemm(x: torch.Tensor, w: torch.Tensor,
     elif out.dtype != odt or tuple(out.shape) != (rows, n_out) or not out.is_contiguous() \
             or out.device != dev:
         raise ValueError(f"out must be a contiguous {odt} [{rows},{n_out}] tensor on {dev}")
-    _lib.call("moe_grouped_gemm", _p(xc), _p(wc), _p(out), rows, plan.num_groups, g, n, k,
-              codes[epilogue], _p(plan.workspace), plan.nbytes, _stream(dev))
+    _lib.call("moe_grouped_gemm" if w_layout == "NK" else "moe_grouped_gemm_nn", _p(xc), _p(wc),
+              _p(out), rows, plan.num_groups, g, n, k, codes[epilogue], _p(plan.workspace),
+              plan.nbytes, _stream(dev))
     return out
 
 

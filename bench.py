@@ -63,9 +63,10 @@ def parse_args():
     ap.add_argument("--transport", choices=["fused", "peer", "nccl"], default="fused",
                     help="EP row exchange: dispatch/combine kernels on peer memory, "
                          "IPC-mapped buffers + copy engines, or NCCL all-to-all")
-    ap.add_argument("--workload", choices=["layer", "router_gemm"], default="layer",
+    ap.add_argument("--workload", choices=["layer", "router_gemm", "dgrad"], default="layer",
                     help="layer: the MoE expert-layer forward (the headline); router_gemm: the "
-                         "router gate GEMM that produces its logits (one GPU)")
+                         "router gate GEMM that produces its logits; dgrad: the layer's two "
+                         "grouped input-gradient GEMMs (one GPU)")
     ap.add_argument("--router-shape", default="16384,8192,320",
                     help="M,K,N of the router GEMM (tokens, hidden, experts)")
     return ap.parse_args()
@@ -339,6 +340,80 @@ def run_router_gemm(a):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------- grouped dgrad
+def run_dgrad(a):
+    """The layer's grouped dgrads at the bench workload: dh = dy @ W2[e]
+    ([R,H] x [H,F]) and dx = dz @ W1[e] ([R,2F] x [2F,H]), the weights used as
+    stored (staged MN-major), group sizes from the layer's own routing."""
+    import torch
+    import moe_b200
+    from moe_b200 import _lib
+    t, h, e, f, k = a.tokens, a.hidden, a.experts, a.ffn, a.topk
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    moe_b200.load_library()
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000)
+    logits = torch.randn(t, e, device=dev, generator=g)
+    r = moe_b200.router_topk(logits, k, "softmax", True, zipf_bias(e, a.routing).to(dev),
+                             outputs="maps")
+    counts = moe_b200.row_id_map(r.routing_map, want_et=False).counts
+    rows = t * k
+    w = moe_b200.MoEWeights.random(e, h, f, dev, seed=77)
+    dy = torch.randn(rows, h, device=dev, generator=g).to(torch.bfloat16)
+    dz = torch.randn(rows, 2 * f, device=dev, generator=g).to(torch.bfloat16)
+    plan = moe_b200.GroupedGemmPlan(e, dev).from_splits(counts)
+    dh = torch.empty(rows, f, dtype=torch.bfloat16, device=dev)
+    dx = torch.empty(rows, h, dtype=torch.bfloat16, device=dev)
+    ev = {n: torch.cuda.Event(enable_timing=True) for n in ("s", "fc2", "fc1")}
+
+    def step():
+        moe_b200.grouped_gemm(dy, w.w2, plan=plan, out=dh, w_layout="KN")
+        ev["fc2"].record()
+        moe_b200.grouped_gemm(dz, w.w1, plan=plan, out=dx, w_layout="KN")
+
+    sampler = ClockSampler(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0])
+    sampler.start()
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    assert plan.device_error() == 0
+    launches0 = _lib.launch_count
+    wall0 = time.time()
+    t2 = t1 = 0.0
+    for _ in range(a.steps):
+        ev["s"].record()
+        step()
+        ev["fc1"].record()
+        torch.cuda.synchronize()
+        t2 += ev["s"].elapsed_time(ev["fc2"])
+        t1 += ev["fc2"].elapsed_time(ev["fc1"])
+    sampler.mark(wall0, time.time())
+    launches = _lib.launch_count - launches0
+    clocks = sampler.stop()
+    t2, t1 = t2 / a.steps / 1e3, t1 / a.steps / 1e3
+    fl2, fl1 = 2.0 * rows * h * f, 2.0 * rows * 2 * f * h
+    peaks, peak_kind = load_peaks()
+    peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    ach = (fl1 + fl2) / (t1 + t2) / 1e12
+    line = {"metric": "grouped dgrad tokens/s", "value": t / (t1 + t2), "unit": "tokens/s",
+            "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": (t1 + t2) * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (N(0,1) gradients, N(0,0.02) weights, Zipf routing counts)",
+            "config": {"workload": "grouped_dgrad", "tokens": t, "hidden": h, "experts": e,
+                       "topk": k, "ffn": f, "routing": a.routing,
+                       "l2": "no flush: every step streams >22 GB of weights"},
+            "roofline": {"bound": "tensor", "kernel": "grouped_gemm_nn (fc1 + fc2 dgrad)",
+                         "achieved": round(ach, 2), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(ach / peak, 4), "traffic": None},
+            "stages_ms": {"fc2_dgrad": round(t2 * 1e3, 4), "fc1_dgrad": round(t1 * 1e3, 4)},
+            "fc2_dgrad_tflops": round(fl2 / t2 / 1e12, 1),
+            "fc1_dgrad_tflops": round(fl1 / t1 / 1e12, 1),
+            "peak_kind": f"bf16 sustained, of {peak_kind}",
+            "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 # --------------------------------------------------------------------------- GPU arm
 def read_traffic():
     p = ROOT / "profiles" / "grouped_gemm_fc1_layer.txt"
@@ -361,6 +436,10 @@ def main():
     if a.workload == "router_gemm":
         if rank == 0:
             run_router_gemm(a)
+        return
+    if a.workload == "dgrad":
+        if rank == 0 and a.impl != "reference":
+            run_dgrad(a)
         return
     if a.impl == "reference":
         run_reference_arm(a, world, rank)

@@ -196,6 +196,15 @@ int moe_grouped_gemm(const void* x, const void* w, void* out, int64_t x_rows, in
                      int64_t num_w, int64_t N, int64_t K, int32_t epilogue,
                      const void* workspace, size_t workspace_bytes, moe_stream_t stream);
 
+/* f3  Same with w [num_w, K, N] (N contiguous): out[r, :] = x[r, :] @        */
+/* w[widx(g)] — the grouped dgrad dx = dy @ W of the forward weight as it is  */
+/* (kernel_cases/case07_moe_grouped_gemm_fc1_dgrad.py:49-64,                 */
+/* case08_moe_grouped_gemm_fc2_dgrad.py:49-64; case13/case19 with G = 1).    */
+/* The weight tile is staged MN-major (no transposed copy). Epilogue 0 or 2. */
+int moe_grouped_gemm_nn(const void* x, const void* w, void* out, int64_t x_rows, int64_t G,
+                        int64_t num_w, int64_t N, int64_t K, int32_t epilogue,
+                        const void* workspace, size_t workspace_bytes, moe_stream_t stream);
+
 /* Reads the device error word a previous moe_grouped_gemm left in the       */
 /* workspace (0 = none; blocking: synchronises the stream).                  */
 int moe_grouped_gemm_check(const void* workspace, size_t workspace_bytes, moe_stream_t stream,

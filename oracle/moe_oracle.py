@@ -246,7 +246,7 @@ def swiglu(y_u16: np.ndarray) -> np.ndarray:
 
 
 def grouped_gemm(x_u16: np.ndarray, w_u16: np.ndarray, m_splits, epilogue: str = "none",
-                 row_starts=None):
+                 row_starts=None, w_layout: str = "NK"):
     """out = cat_g(x[seg_g] @ w[g].T) in fp32, rounded to bf16.
 
     kernel_cases/case03_moe_grouped_gemm_fc1_fwd.py:57-64 and
@@ -255,8 +255,11 @@ def grouped_gemm(x_u16: np.ndarray, w_u16: np.ndarray, m_splits, epilogue: str =
     epilogue "swiglu": the fc1 output is rounded to bf16, then SwiGLU.
     Rows outside every group are left as zeros. w_u16 may also be a sequence
     of per-group float32 matrices (used by the CPU timing baseline).
+    w_layout "KN": w[g] is [K,N] and out = x @ w[g] — the grouped dgrad of
+    kernel_cases/case07/08_moe_grouped_gemm_fc*_dgrad.py:49-64 (case13/19
+    with one group): torch.mm(dy[seg], w[g]), fp32 accumulation, bf16 out.
     """
-    n = w_u16[0].shape[0]
+    n = w_u16[0].shape[0] if w_layout == "NK" else w_u16[0].shape[1]
     n_out = n // 2 if epilogue == "swiglu" else n
     out = np.zeros((x_u16.shape[0], n_out), dtype=np.uint16)
     off = 0
@@ -266,7 +269,7 @@ def grouped_gemm(x_u16: np.ndarray, w_u16: np.ndarray, m_splits, epilogue: str =
         if m > 0:
             xs = bf16_to_f32(x_u16[start:start + m])
             ws = w_u16[g] if w_u16[g].dtype == np.float32 else bf16_to_f32(w_u16[g])
-            y = f32_to_bf16(xs @ ws.T)
+            y = f32_to_bf16(xs @ (ws.T if w_layout == "NK" else ws))
             out[start:start + m] = swiglu(y) if epilogue == "swiglu" else y
         off = start + m
     return out

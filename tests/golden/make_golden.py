@@ -213,6 +213,19 @@ def gen_gemm(root: Path) -> None:
     inp = torch.randn(96, 512, generator=gen).to(torch.bfloat16)
     wt = torch.randn(256, 512, generator=gen).to(torch.bfloat16)
     out.update(c35_x=bits(inp), c35_w=bits(wt), c35_y=c35.reference_fp32(inp, wt).numpy())
+    # Grouped dgrad (dy @ w[g], "NN"): case07/08 with several groups, case13/19 with one.
+    for tag, name, (g_, t_, n_, k_) in (
+            ("c07", "case07_moe_grouped_gemm_fc1_dgrad", (4, 300, 128, 192)),
+            ("c08", "case08_moe_grouped_gemm_fc2_dgrad", (3, 200, 192, 128)),
+            ("c13", "case13_grouped_gemm_single_group_fc1_dgrad", (1, 200, 128, 128)),
+            ("c19", "case19_grouped_gemm_single_group_fc2_dgrad", (1, 100, 256, 64))):
+        mod = load_case(root, name)
+        gen = torch.Generator().manual_seed(7 + g_ + n_)
+        dy = torch.randn(t_, n_, generator=gen).to(torch.bfloat16)
+        w = (torch.randn(g_, n_, k_, generator=gen) * 0.05).to(torch.bfloat16)
+        dx = mod.Model(g_, t_)(dy, w)
+        out.update({f"{tag}_dy": bits(dy), f"{tag}_w": bits(w), f"{tag}_dx": bits(dx),
+                    f"{tag}_splits": np.array(mod.group_sizes(t_, g_))})
     # Router gate GEMM (fp32 out) at the traced N = 320 experts, small M and K.
     c38 = load_case(root, "case38_ref_musa_asm_bf16_ssgemm_nt_320x256")
     gen = torch.Generator().manual_seed(38)

@@ -206,6 +206,14 @@ def test_single_expert_gemm_fp32_golden(golden):
     _gemm_close(y, z["c35_y"])
 
 
+def test_grouped_dgrad_against_reference_models(golden):
+    """case07/08 (groups) and case13/19 (one group): dx = dy[seg] @ w[g]."""
+    z = golden("gemm_swiglu.npz")
+    for tag in ("c07", "c08", "c13", "c19"):
+        y = orc.grouped_gemm(z[f"{tag}_dy"], z[f"{tag}_w"], z[f"{tag}_splits"], w_layout="KN")
+        _gemm_close(y, orc.bf16_to_f32(z[f"{tag}_dx"]))
+
+
 def test_router_gemm_fp32_golden(golden):
     """case38 reference_fp32 (router gate GEMM, fp32 out) at N = 320 experts:
     both sides accumulate in fp32 and differ only in summation order."""
