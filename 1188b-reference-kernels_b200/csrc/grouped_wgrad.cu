@@ -1,0 +1,470 @@
+// Grouped weight gradient on B200 tensor cores (the wgrad of the expert FFN):
+//
+//   dW[g] = dy[rows of g]^T @ x[rows of g]      dW [G, N, K] bf16, fp32 accumulation
+//
+// dy [R, N] and x [R, K] are the row-major activations of the forward, groups
+// are contiguous row ranges. The reference computes this as a Python loop of
+// torch.mm(dy[seg].t(), x[seg]) (kernel_cases/case05_moe_grouped_gemm_fc2_
+// wgrad.py:49-64, case09_moe_grouped_gemm_fc1_wgrad.py:49-64, "TN").
+//
+// Both MMA operands are MN-major: a 64-row slice of dy (or x) staged by TMA as
+// 64-column x 64-row boxes is a [64 reduction rows x 64 MN columns] tile with
+// the MN columns contiguous, which tcgen05 reads directly (instruction bits 15
+// and 16). The reduction runs over a group's rows only: every group has its
+// own pair of tensor maps (built on the host from the host-side splits, stored
+// in the workspace) whose outer extent is that group's row count, so the last
+// partial 64-row block is zero-filled by TMA instead of reaching into the next
+// group. A group with no rows gets a zero dW[g], like torch.mm over zero rows.
+//
+// Kernel structure (one persistent CTA per SM, 192 threads), as the forward
+// single-CTA kernel: warp 0 TMA producer (4-stage ring, 16 KB dy + 32 KB x per
+// stage), warp 1 TMEM owner and single-thread MMA issuer (M=128 dW rows,
+// N=256 dW columns, K=16), warps 2-5 epilogue through 64B-swizzled shared
+// buffers and TMA tile stores. Every wait is bounded (2 s).
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <string.h>
+
+#include <algorithm>
+#include <mutex>
+#include <vector>
+
+#include "moe_common.cuh"
+
+namespace moe {
+namespace gw {
+
+constexpr int BM = 128;  // dW rows per tile (columns of dy)
+constexpr int BN = 256;  // dW columns per tile (columns of x)
+constexpr int BK = 64;   // reduction rows per stage
+constexpr int kStages = 4;
+constexpr int kThreads = 192;
+constexpr uint32_t kBox = 64 * 64 * 2;          // one 64-column x 64-row bf16 box
+constexpr uint32_t kABytes = (BM / 64) * kBox;  // 16 KB of dy
+constexpr uint32_t kBBytes = (BN / 64) * kBox;  // 32 KB of x
+constexpr uint32_t kStageBytes = kABytes + kBBytes;
+constexpr uint32_t kTmemCols = 2 * BN;
+constexpr uint32_t kEpiBoxBytes = 32 * 32 * 2;  // 32 rows x 32 bf16 columns
+constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + 1024 + 4 * 2 * kEpiBoxBytes;
+constexpr int kErrTimeoutProducer = 1;
+constexpr int kErrTimeoutMma = 2;
+constexpr int kErrTimeoutEpilogue = 3;
+
+struct Params {
+  const CUtensorMap* maps;  // [2G] in global memory: rows of group g of dy, then of x
+  const int32_t* rows;      // [G] rows of each group
+  int32_t* err;
+  __nv_bfloat16* out;  // dW [G, N, K]
+  int G, N, K;
+  int m_tiles, n_tiles;
+};
+
+MOE_DEVICE void tensormap_acquire(const void* tmap) {
+  asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap))
+               : "memory");
+}
+
+MOE_DEVICE bool wait_drain(uint32_t bar, uint32_t parity) {
+  const unsigned long long t0 = globaltimer_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (globaltimer_ns() - t0 > kWaitTimeoutNs) return false;
+  return true;
+}
+
+MOE_DEVICE void raise_abort(volatile int* abort_flag, int32_t* err, int code) {
+  atomicCAS(err, 0, code);
+  *abort_flag = 1;
+  __threadfence_block();
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_wgrad_kernel(const __grid_constant__ CUtensorMap tmap_out, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw_addr);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base_ptr + kStages * kStageBytes);
+  const uint32_t bar0 = smem_u32(bars);
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (kStages + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * kStages + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * kStages + 2 + a); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * kStages + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = warp_id();
+  const int lane = lane_id();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 4);
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const long long per_g = static_cast<long long>(p.m_tiles) * p.n_tiles;
+  const long long total = per_g * p.G;
+  auto locate = [&](long long t, int& g, int& mi, int& ni) {
+    g = static_cast<int>(t / per_g);
+    const int r = static_cast<int>(t - g * per_g);
+    mi = r / p.n_tiles;
+    ni = r - mi * p.n_tiles;
+  };
+  auto nkb_of = [&](int g) { return (max(p.rows[g], 0) + BK - 1) / BK; };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_normal();
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued[kStages];
+#pragma unroll
+      for (int s = 0; s < kStages; ++s) issued[s] = -1;
+      bool ok = true;
+      int last_g = -1;
+      for (long long t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        int g, mi, ni;
+        locate(t, g, mi, ni);
+        const CUtensorMap* ma = p.maps + 2 * g;  // dy rows of group g
+        const CUtensorMap* mb = ma + 1;          // x rows of group g
+        if (g != last_g) {
+          tensormap_acquire(ma);
+          tensormap_acquire(mb);
+          last_g = g;
+        }
+        const int nkb = nkb_of(g);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = base + stage * kStageBytes;
+          const uint32_t sb = sa + kABytes;
+          mbar_arrive_expect_tx(full_bar(stage), kStageBytes);
+#pragma unroll
+          for (int j = 0; j < BM / 64; ++j)
+            tma_load_2d(sa + j * kBox, ma, mi * BM + j * 64, kb * BK, full_bar(stage), pol);
+#pragma unroll
+          for (int j = 0; j < BN / 64; ++j)
+            tma_load_2d(sb + j * kBox, mb, ni * BN + j * 64, kb * BK, full_bar(stage), pol);
+          issued[stage] = static_cast<int>(phase);
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (!ok) {
+        raise_abort(abort_flag, p.err, kErrTimeoutProducer);
+        for (int s = 0; s < kStages; ++s)
+          if (issued[s] >= 0) wait_drain(full_bar(s), static_cast<uint32_t>(issued[s]));
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16_f32(BM, BN) | (1u << 15) | kIdescBMajorMN;
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (long long t = blockIdx.x; t < total && ok; t += gridDim.x) {
+        int g, mi, ni;
+        locate(t, g, mi, ni);
+        const int acc = it & 1;
+        const uint32_t aph = static_cast<uint32_t>((it >> 1) & 1);
+        if (!mbar_wait(tempty_bar(acc), aph ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        const int nkb = nkb_of(g);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(full_bar(stage), phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = base + stage * kStageBytes;
+          const uint32_t sb = sa + kABytes;
+          // MN-major operands: 64-column chunks 8 KB apart, 8-row groups 1 KB
+          // apart; each K=16 slice moves two row groups (+2 KB = +128).
+          const uint64_t ad = umma_desc_mn_sw128(sa, kBox);
+          const uint64_t bd = umma_desc_mn_sw128(sb, kBox);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_bf16(d_tmem, ad + 128ull * k, bd + 128ull * k, idesc, (kb | k) != 0 ? 1u : 0u);
+          issued_any = true;
+          umma_commit(empty_bar(stage));
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(tfull_bar(acc));  // also for a group without rows: the epilogue writes zeros
+        ++it;
+      }
+      if (!ok) {
+        raise_abort(abort_flag, p.err, kErrTimeoutMma);
+        if (issued_any) {
+          umma_commit(drain_bar);
+          wait_drain(drain_bar, 0);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int quad = warp & 3;  // TMEM lanes this warp may access: 32*quad ..
+    const uint32_t epi_base = ((bar0 + 512u + 1023u) & ~1023u) +
+                              static_cast<uint32_t>(quad) * 2u * kEpiBoxBytes;
+    uint32_t chunk_no = 0;
+    int it = 0;
+    bool ok = true;
+    for (long long t = blockIdx.x; t < total; t += gridDim.x) {
+      int g, mi, ni;
+      locate(t, g, mi, ni);
+      const int acc = it & 1;
+      const uint32_t aph = static_cast<uint32_t>((it >> 1) & 1);
+      if (!mbar_wait(tfull_bar(acc), aph, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const bool no_rows = p.rows[g] <= 0;
+      const int rowl = mi * BM + quad * 32 + lane;  // row of dW[g]
+      const bool rvalid = rowl < p.N;
+      const bool tma = __all_sync(0xffffffffu, rvalid);
+      const int warp_row0 = g * p.N + mi * BM + quad * 32;  // in the [G*N, K] view
+      __nv_bfloat16* orow = p.out + (static_cast<int64_t>(g) * p.N + rowl) * p.K;
+      const uint32_t tbase =
+          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int col = ni * BN + c * 32;
+        if (col >= p.K) break;  // warp-uniform
+        uint32_t r[32];
+        if (!no_rows) {
+          tmem_ld_32x32b_x32(tbase + c * 32, r);
+          tmem_ld_wait();
+        } else {
+#pragma unroll
+          for (int q = 0; q < 32; ++q) r[q] = 0u;
+        }
+        uint32_t o[16];
+#pragma unroll
+        for (int q = 0; q < 16; ++q)
+          o[q] = pack_bf16x2(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1]));
+        if (tma) {
+          const uint32_t buf = epi_base + (chunk_no & 1u) * kEpiBoxBytes;
+          ++chunk_no;
+          if (lane == 0) bulk_wait_read<1>();
+          __syncwarp();
+          const uint32_t sw = static_cast<uint32_t>((lane >> 1) & 3);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            const uint32_t dst =
+                buf + static_cast<uint32_t>(lane) * 64u + ((static_cast<uint32_t>(j) ^ sw) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(o[4 * j]),
+                         "r"(o[4 * j + 1]), "r"(o[4 * j + 2]), "r"(o[4 * j + 3])
+                         : "memory");
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmap_out, col, warp_row0, buf);
+            bulk_commit();
+          }
+        } else if (rvalid) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v)
+            if (col + v * 8 + 8 <= p.K)
+              *reinterpret_cast<uint4*>(orow + col + v * 8) =
+                  make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(tempty_bar(acc));
+      ++it;
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+    if (!ok && lane == 0) raise_abort(abort_flag, p.err, kErrTimeoutEpilogue);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, kTmemCols);
+  }
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* q = nullptr;
+    cudaDriverEntryPointQueryResult r;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &q, cudaEnableDefault, &r) ==
+            cudaSuccess &&
+        r == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(q);
+  });
+  return fn;
+}
+
+// bf16 row-major [outer, inner] at ptr; box box_inner x box_outer.
+int encode_bf16(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer,
+                uint32_t box_inner, uint32_t box_outer, CUtensorMapSwizzle swz) {
+  auto encode = encode_fn();
+  if (encode == nullptr) {
+    set_last_error("grouped_wgrad: cuTensorMapEncodeTiled unavailable");
+    return MOE_ERR_CUDA;
+  }
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {inner * 2};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1u, 1u};
+  const CUresult r = encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims,
+                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_last_error("grouped_wgrad: cuTensorMapEncodeTiled failed (%d)", static_cast<int>(r));
+    return MOE_ERR_CUDA;
+  }
+  return MOE_OK;
+}
+
+size_t rows_bytes(int64_t G) { return (static_cast<size_t>(G) * 4 + 255) & ~static_cast<size_t>(255); }
+size_t ws_bytes(int64_t G) { return 256 + rows_bytes(G) + 2 * static_cast<size_t>(G) * sizeof(CUtensorMap); }
+
+int ensure_smem_attr() {
+  int dev = 0;
+  MOE_CUDA_CALL(cudaGetDevice(&dev), "cudaGetDevice");
+  static std::mutex mu;
+  static bool done[64] = {};
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev < 64 && done[dev]) return MOE_OK;
+  MOE_CUDA_CALL(cudaFuncSetAttribute(grouped_wgrad_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(kSmemBytes)),
+                "cudaFuncSetAttribute(grouped_wgrad)");
+  if (dev < 64) done[dev] = true;
+  return MOE_OK;
+}
+
+}  // namespace gw
+}  // namespace moe
+
+using namespace moe;
+
+extern "C" int moe_grouped_wgrad_workspace_size(int64_t G, size_t* bytes) {
+  MOE_REQUIRE(bytes != nullptr, "grouped_wgrad_workspace_size: null output");
+  MOE_REQUIRE(G >= 1 && G <= (1 << 20), "grouped_wgrad: G=%lld out of range", (long long)G);
+  *bytes = gw::ws_bytes(G);
+  return MOE_OK;
+}
+
+extern "C" int moe_grouped_wgrad(const void* dy, const void* x, void* dw, int64_t rows_total,
+                                 int64_t G, int64_t N, int64_t K, const int32_t* m_splits,
+                                 void* workspace, size_t workspace_bytes, moe_stream_t stream) {
+  MOE_REQUIRE(G >= 1 && G <= (1 << 20), "grouped_wgrad: G=%lld out of range", (long long)G);
+  MOE_REQUIRE(rows_total >= 0 && rows_total < (1ll << 31), "grouped_wgrad: rows=%lld out of range",
+              (long long)rows_total);
+  MOE_REQUIRE(N >= 8 && N % 8 == 0 && K >= 8 && K % 8 == 0,
+              "grouped_wgrad: N=%lld and K=%lld must be positive multiples of 8", (long long)N,
+              (long long)K);
+  MOE_REQUIRE(G * N < (1ll << 31), "grouped_wgrad: G*N too large");
+  MOE_REQUIRE(m_splits != nullptr, "grouped_wgrad: null m_splits (host array of G counts)");
+  MOE_REQUIRE(workspace != nullptr && workspace_bytes >= gw::ws_bytes(G) &&
+                  (reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
+              "grouped_wgrad: workspace must hold %zu bytes, 256-byte aligned", gw::ws_bytes(G));
+  MOE_REQUIRE(dy && x && dw, "grouped_wgrad: null pointer");
+  MOE_REQUIRE(((reinterpret_cast<uintptr_t>(dy) | reinterpret_cast<uintptr_t>(x) |
+                reinterpret_cast<uintptr_t>(dw)) & 15) == 0,
+              "grouped_wgrad: dy, x and dw must be 16-byte aligned");
+  int64_t sum = 0;
+  for (int64_t g = 0; g < G; ++g) {
+    MOE_REQUIRE(m_splits[g] >= 0, "grouped_wgrad: m_splits[%lld] < 0", (long long)g);
+    sum += m_splits[g];
+  }
+  MOE_REQUIRE(sum <= rows_total, "grouped_wgrad: sum(m_splits)=%lld exceeds rows=%lld",
+              (long long)sum, (long long)rows_total);
+  int st = gw::ensure_smem_attr();
+  if (st) return st;
+
+  // Host image of the workspace after the error word: row counts, then the
+  // per-group tensor maps (dy rows of g, x rows of g).
+  const size_t rb = gw::rows_bytes(G);
+  std::vector<uint8_t> host(rb + 2 * static_cast<size_t>(G) * sizeof(CUtensorMap), 0);
+  memcpy(host.data(), m_splits, static_cast<size_t>(G) * 4);
+  std::vector<CUtensorMap> maps(2 * static_cast<size_t>(G));
+  const char* dyb = static_cast<const char*>(dy);
+  const char* xb = static_cast<const char*>(x);
+  int64_t r0 = 0;
+  for (int64_t g = 0; g < G; ++g) {
+    const int64_t m = m_splits[g];
+    // A group without rows never loads; its maps only need to be valid.
+    const uint64_t outer = static_cast<uint64_t>(m > 0 ? m : 1);
+    const int64_t start = m > 0 ? r0 : 0;
+    if ((st = gw::encode_bf16(&maps[2 * g], dyb + start * N * 2, static_cast<uint64_t>(N), outer,
+                              64u, 64u, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+        (st = gw::encode_bf16(&maps[2 * g + 1], xb + start * K * 2, static_cast<uint64_t>(K),
+                              outer, 64u, 64u, CU_TENSOR_MAP_SWIZZLE_128B)))
+      return st;
+    r0 += m;
+  }
+  memcpy(host.data() + rb, maps.data(), maps.size() * sizeof(CUtensorMap));
+  CUtensorMap tout;
+  st = gw::encode_bf16(&tout, dw, static_cast<uint64_t>(K), static_cast<uint64_t>(G * N), 32u,
+                       32u, CU_TENSOR_MAP_SWIZZLE_64B);
+  if (st) return st;
+
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  char* ws = static_cast<char*>(workspace);
+  MOE_CUDA_CALL(cudaMemsetAsync(ws, 0, 4, s), "grouped_wgrad: clear error word");
+  // From pageable memory: returns once the bytes are staged, so `host` may go.
+  MOE_CUDA_CALL(cudaMemcpyAsync(ws + 256, host.data(), host.size(), cudaMemcpyHostToDevice, s),
+                "grouped_wgrad: upload group table");
+
+  gw::Params p;
+  p.maps = reinterpret_cast<const CUtensorMap*>(ws + 256 + rb);
+  p.rows = reinterpret_cast<const int32_t*>(ws + 256);
+  p.err = reinterpret_cast<int32_t*>(ws);
+  p.out = static_cast<__nv_bfloat16*>(dw);
+  p.G = static_cast<int>(G);
+  p.N = static_cast<int>(N);
+  p.K = static_cast<int>(K);
+  p.m_tiles = static_cast<int>((N + gw::BM - 1) / gw::BM);
+  p.n_tiles = static_cast<int>((K + gw::BN - 1) / gw::BN);
+  int dev = 0;
+  MOE_CUDA_CALL(cudaGetDevice(&dev), "cudaGetDevice");
+  const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles * G;
+  const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms(dev)));
+  gw::grouped_wgrad_kernel<<<grid, gw::kThreads, gw::kSmemBytes, s>>>(tout, p);
+  MOE_CUDA_CHECK_LAUNCH("grouped_wgrad launch");
+  return MOE_OK;
+}

@@ -433,6 +433,45 @@ def permute_backward(grad_permuted: torch.Tensor, row_id_map: torch.Tensor,
     return (acc, gx, gp) if return_acc else (gx, gp)
 
 
+def grouped_wgrad(dy: torch.Tensor, x: torch.Tensor,
+                  m_splits: Union[Sequence[int], torch.Tensor],
+                  out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """dW[g] = dy[seg_g]^T @ x[seg_g] on tcgen05 tensor cores, [G,N,K] bf16.
+
+    dy [rows,N] and x [rows,K] bf16 (the forward's output gradient and input,
+    groups contiguous in order), fp32 accumulation; an empty group gives
+    zeros. The torch.mm(dy[seg].t(), x[seg]) loop of kernel_cases/
+    case05_moe_grouped_gemm_fc2_wgrad.py:49-64 / case09_moe_grouped_gemm_fc1_
+    wgrad.py:49-64. m_splits are needed on the host (a CUDA tensor is read
+    back, which synchronises): they size each group's tensor maps.
+    """
+    for n_, t_ in (("dy", dy), ("x", x)):
+        _need_cuda(n_, t_)
+        _need_dtype(n_, t_, torch.bfloat16)
+    if dy.dim() != 2 or x.dim() != 2 or dy.shape[0] != x.shape[0]:
+        raise ValueError(f"shapes dy {tuple(dy.shape)} x {tuple(x.shape)}")
+    if isinstance(m_splits, torch.Tensor):
+        m_splits = m_splits.detach().cpu().tolist()
+    splits = [int(v) for v in m_splits]
+    if any(v < 0 for v in splits) or sum(splits) > dy.shape[0] or not splits:
+        raise ValueError("m_splits must be >= 0 and sum to at most the rows")
+    g = len(splits)
+    dyc, xc = dy.contiguous(), x.contiguous()
+    n, k = dyc.shape[1], xc.shape[1]
+    dev = dyc.device
+    if out is None:
+        out = torch.empty((g, n, k), dtype=torch.bfloat16, device=dev)
+    elif out.dtype != torch.bfloat16 or tuple(out.shape) != (g, n, k) or not out.is_contiguous():
+        raise ValueError(f"out must be a contiguous bf16 [{g},{n},{k}] tensor")
+    nb = c_size_t(0)
+    _lib.call("moe_grouped_wgrad_workspace_size", g, byref(nb))
+    ws = _workspace(nb.value, dev)
+    host = (c_int32 * g)(*splits)
+    _lib.call("moe_grouped_wgrad", _p(dyc), _p(xc), _p(out), dyc.shape[0], g, n, k, host,
+              _p(ws), nb.value, _stream(dev))
+    return out  # ws returns to torch's allocator, reused only after this stream's work
+
+
 def router_logits(x: torch.Tensor, weight: torch.Tensor,
                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Router gate GEMM: logits [T,E] fp32 = x [T,H] bf16 @ weight [E,H] bf16 ^T,

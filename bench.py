@@ -63,10 +63,10 @@ def parse_args():
     ap.add_argument("--transport", choices=["fused", "peer", "nccl"], default="fused",
                     help="EP row exchange: dispatch/combine kernels on peer memory, "
                          "IPC-mapped buffers + copy engines, or NCCL all-to-all")
-    ap.add_argument("--workload", choices=["layer", "router_gemm", "dgrad"], default="layer",
+    ap.add_argument("--workload", choices=["layer", "router_gemm", "backward"], default="layer",
                     help="layer: the MoE expert-layer forward (the headline); router_gemm: the "
-                         "router gate GEMM that produces its logits; dgrad: the layer's two "
-                         "grouped input-gradient GEMMs (one GPU)")
+                         "router gate GEMM that produces its logits; backward: the layer's "
+                         "grouped dgrad and wgrad GEMMs (one GPU)")
     ap.add_argument("--router-shape", default="16384,8192,320",
                     help="M,K,N of the router GEMM (tokens, hidden, experts)")
     return ap.parse_args()
@@ -340,11 +340,13 @@ def run_router_gemm(a):
     print(json.dumps(line), flush=True)
 
 
-# --------------------------------------------------------------------------- grouped dgrad
-def run_dgrad(a):
-    """The layer's grouped dgrads at the bench workload: dh = dy @ W2[e]
-    ([R,H] x [H,F]) and dx = dz @ W1[e] ([R,2F] x [2F,H]), the weights used as
-    stored (staged MN-major), group sizes from the layer's own routing."""
+# --------------------------------------------------------------------------- grouped backward
+def run_backward(a):
+    """The layer's grouped-GEMM backward at the bench workload, group sizes from
+    the layer's own routing: fc2 dgrad dh = dy @ W2[e] ([R,H] x [H,F]), fc2
+    wgrad dW2[e] = dy[seg]^T @ h[seg], fc1 dgrad dx = dz @ W1[e] ([R,2F] x
+    [2F,H]) and fc1 wgrad dW1[e] = dz[seg]^T @ x[seg]. dgrad uses the weights
+    as stored (staged MN-major); wgrad writes every expert's gradient."""
     import torch
     import moe_b200
     from moe_b200 import _lib
@@ -358,19 +360,31 @@ def run_dgrad(a):
     r = moe_b200.router_topk(logits, k, "softmax", True, zipf_bias(e, a.routing).to(dev),
                              outputs="maps")
     counts = moe_b200.row_id_map(r.routing_map, want_et=False).counts
+    splits = counts.cpu().tolist()
     rows = t * k
     w = moe_b200.MoEWeights.random(e, h, f, dev, seed=77)
     dy = torch.randn(rows, h, device=dev, generator=g).to(torch.bfloat16)
     dz = torch.randn(rows, 2 * f, device=dev, generator=g).to(torch.bfloat16)
+    xp = torch.randn(rows, h, device=dev, generator=g).to(torch.bfloat16)
+    hm = torch.randn(rows, f, device=dev, generator=g).to(torch.bfloat16)
     plan = moe_b200.GroupedGemmPlan(e, dev).from_splits(counts)
     dh = torch.empty(rows, f, dtype=torch.bfloat16, device=dev)
     dx = torch.empty(rows, h, dtype=torch.bfloat16, device=dev)
-    ev = {n: torch.cuda.Event(enable_timing=True) for n in ("s", "fc2", "fc1")}
+    dw2 = torch.empty(e, h, f, dtype=torch.bfloat16, device=dev)
+    dw1 = torch.empty(e, 2 * f, h, dtype=torch.bfloat16, device=dev)
+    names = ["fc2_dgrad", "fc2_wgrad", "fc1_dgrad", "fc1_wgrad"]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)]
 
     def step():
+        ev[0].record()
         moe_b200.grouped_gemm(dy, w.w2, plan=plan, out=dh, w_layout="KN")
-        ev["fc2"].record()
+        ev[1].record()
+        moe_b200.grouped_wgrad(dy, hm, splits, out=dw2)
+        ev[2].record()
         moe_b200.grouped_gemm(dz, w.w1, plan=plan, out=dx, w_layout="KN")
+        ev[3].record()
+        moe_b200.grouped_wgrad(dz, xp, splits, out=dw1)
+        ev[4].record()
 
     sampler = ClockSampler(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0])
     sampler.start()
@@ -380,36 +394,38 @@ def run_dgrad(a):
     assert plan.device_error() == 0
     launches0 = _lib.launch_count
     wall0 = time.time()
-    t2 = t1 = 0.0
+    tot = [0.0] * len(names)
     for _ in range(a.steps):
-        ev["s"].record()
         step()
-        ev["fc1"].record()
         torch.cuda.synchronize()
-        t2 += ev["s"].elapsed_time(ev["fc2"])
-        t1 += ev["fc2"].elapsed_time(ev["fc1"])
+        for i in range(len(names)):
+            tot[i] += ev[i].elapsed_time(ev[i + 1]) / 1e3
     sampler.mark(wall0, time.time())
     launches = _lib.launch_count - launches0
     clocks = sampler.stop()
-    t2, t1 = t2 / a.steps / 1e3, t1 / a.steps / 1e3
-    fl2, fl1 = 2.0 * rows * h * f, 2.0 * rows * 2 * f * h
+    sec = {n: v / a.steps for n, v in zip(names, tot)}
+    flops = {"fc2_dgrad": 2.0 * rows * h * f, "fc2_wgrad": 2.0 * rows * h * f,
+             "fc1_dgrad": 2.0 * rows * 2 * f * h, "fc1_wgrad": 2.0 * rows * 2 * f * h}
+    step_s = sum(sec.values())
     peaks, peak_kind = load_peaks()
     peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
-    ach = (fl1 + fl2) / (t1 + t2) / 1e12
-    line = {"metric": "grouped dgrad tokens/s", "value": t / (t1 + t2), "unit": "tokens/s",
-            "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": (t1 + t2) * 1e3,
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    ach = sum(flops.values()) / step_s / 1e12
+    wg_bytes = (e * h * f + e * 2 * f * h) * 2  # every expert's gradient is written
+    line = {"metric": "grouped GEMM backward tokens/s", "value": t / step_s, "unit": "tokens/s",
+            "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": step_s * 1e3,
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic (N(0,1) gradients, N(0,0.02) weights, Zipf routing counts)",
-            "config": {"workload": "grouped_dgrad", "tokens": t, "hidden": h, "experts": e,
-                       "topk": k, "ffn": f, "routing": a.routing,
-                       "l2": "no flush: every step streams >22 GB of weights"},
-            "roofline": {"bound": "tensor", "kernel": "grouped_gemm_nn (fc1 + fc2 dgrad)",
+            "data": "synthetic (N(0,1) activations/gradients, N(0,0.02) weights, Zipf routing)",
+            "config": {"workload": "grouped_gemm_backward", "tokens": t, "hidden": h,
+                       "experts": e, "topk": k, "ffn": f, "routing": a.routing,
+                       "l2": "no flush: every step streams >22 GB of weights and gradients"},
+            "roofline": {"bound": "tensor", "kernel": "grouped dgrad + wgrad (fc1 + fc2)",
                          "achieved": round(ach, 2), "peak": peak, "unit": "TFLOP/s",
                          "frac": round(ach / peak, 4), "traffic": None},
-            "stages_ms": {"fc2_dgrad": round(t2 * 1e3, 4), "fc1_dgrad": round(t1 * 1e3, 4)},
-            "fc2_dgrad_tflops": round(fl2 / t2 / 1e12, 1),
-            "fc1_dgrad_tflops": round(fl1 / t1 / 1e12, 1),
-            "peak_kind": f"bf16 sustained, of {peak_kind}",
+            "stages_ms": {n: round(v * 1e3, 4) for n, v in sec.items()},
+            "stage_tflops": {n: round(flops[n] / sec[n] / 1e12, 1) for n in names},
+            "wgrad_write_gbs": round(wg_bytes / (sec["fc1_wgrad"] + sec["fc2_wgrad"]) / 1e9, 1),
+            "hbm_peak_gbs": hbm, "peak_kind": f"bf16 sustained, of {peak_kind}",
             "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clocks}
     print(json.dumps(line), flush=True)
 
@@ -437,9 +453,9 @@ def main():
         if rank == 0:
             run_router_gemm(a)
         return
-    if a.workload == "dgrad":
+    if a.workload == "backward":
         if rank == 0 and a.impl != "reference":
-            run_dgrad(a)
+            run_backward(a)
         return
     if a.impl == "reference":
         run_reference_arm(a, world, rank)

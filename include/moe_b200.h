@@ -205,6 +205,22 @@ int moe_grouped_gemm_nn(const void* x, const void* w, void* out, int64_t x_rows,
                         int64_t num_w, int64_t N, int64_t K, int32_t epilogue,
                         const void* workspace, size_t workspace_bytes, moe_stream_t stream);
 
+/* f3  Grouped weight gradient: dW[g] = dy[rows of g]^T @ x[rows of g],      */
+/* dy [rows_total, N], x [rows_total, K] bf16 row-major, groups contiguous   */
+/* in order with host-side row counts m_splits[G] (sum <= rows_total), dW    */
+/* [G, N, K] bf16 (fp32 accumulation); a group with no rows gets zeros.      */
+/* Replaces the torch.mm(dy[seg].t(), x[seg]) loop of kernel_cases/case05_   */
+/* moe_grouped_gemm_fc2_wgrad.py:49-64 and case09_moe_grouped_gemm_fc1_      */
+/* wgrad.py:49-64 ("TN"). The workspace (moe_grouped_wgrad_workspace_size)   */
+/* receives the group table and per-group tensor maps, uploaded on `stream`  */
+/* from host memory (the one entry point whose upload may wait for the       */
+/* stream's earlier work); its first 4 bytes are the device error word       */
+/* (read it with moe_grouped_gemm_check).                                    */
+int moe_grouped_wgrad_workspace_size(int64_t G, size_t* bytes);
+int moe_grouped_wgrad(const void* dy, const void* x, void* dw, int64_t rows_total, int64_t G,
+                      int64_t N, int64_t K, const int32_t* m_splits, void* workspace,
+                      size_t workspace_bytes, moe_stream_t stream);
+
 /* Reads the device error word a previous moe_grouped_gemm left in the       */
 /* workspace (0 = none; blocking: synchronises the stream).                  */
 int moe_grouped_gemm_check(const void* workspace, size_t workspace_bytes, moe_stream_t stream,

@@ -275,6 +275,24 @@ def grouped_gemm(x_u16: np.ndarray, w_u16: np.ndarray, m_splits, epilogue: str =
     return out
 
 
+def grouped_wgrad(dy_u16: np.ndarray, x_u16: np.ndarray, m_splits) -> np.ndarray:
+    """dW[g] = dy[seg_g]^T @ x[seg_g] in fp32, rounded to bf16; [G,N,K] bits.
+
+    kernel_cases/case05_moe_grouped_gemm_fc2_wgrad.py:49-64 and
+    case09_moe_grouped_gemm_fc1_wgrad.py:49-64 (torch.mm(dy[seg].t(), x[seg]),
+    stacked); a group without rows gives zeros.
+    """
+    n, k = dy_u16.shape[1], x_u16.shape[1]
+    out = np.zeros((len(m_splits), n, k), dtype=np.uint16)
+    off = 0
+    for g, m in enumerate(m_splits):
+        m = int(m)
+        if m > 0:
+            out[g] = f32_to_bf16(bf16_to_f32(dy_u16[off:off + m]).T @ bf16_to_f32(x_u16[off:off + m]))
+        off += m
+    return out
+
+
 def router_logits(x_u16: np.ndarray, w_u16: np.ndarray) -> np.ndarray:
     """Router gate GEMM, logits fp32 = x @ w.T accumulated in fp32, unrounded.
 

@@ -226,6 +226,17 @@ def gen_gemm(root: Path) -> None:
         dx = mod.Model(g_, t_)(dy, w)
         out.update({f"{tag}_dy": bits(dy), f"{tag}_w": bits(w), f"{tag}_dx": bits(dx),
                     f"{tag}_splits": np.array(mod.group_sizes(t_, g_))})
+    # Grouped wgrad (dy[seg].T @ x[seg], "TN"): case05 (fc2) and case09 (fc1).
+    for tag, name, (g_, t_, n_, k_) in (
+            ("c05", "case05_moe_grouped_gemm_fc2_wgrad", (3, 200, 192, 128)),
+            ("c09", "case09_moe_grouped_gemm_fc1_wgrad", (4, 300, 128, 192))):
+        mod = load_case(root, name)
+        gen = torch.Generator().manual_seed(5 + g_ + n_)
+        dy = torch.randn(t_, n_, generator=gen).to(torch.bfloat16)
+        xw = torch.randn(t_, k_, generator=gen).to(torch.bfloat16)
+        dw = mod.Model(g_, t_)(dy, xw)
+        out.update({f"{tag}_dy": bits(dy), f"{tag}_x": bits(xw), f"{tag}_dw": bits(dw),
+                    f"{tag}_splits": np.array(mod.group_sizes(t_, g_))})
     # Router gate GEMM (fp32 out) at the traced N = 320 experts, small M and K.
     c38 = load_case(root, "case38_ref_musa_asm_bf16_ssgemm_nt_320x256")
     gen = torch.Generator().manual_seed(38)

@@ -183,6 +183,77 @@ def test_dgrad_layer_shapes_spot_check(cuda_dev):
                                             w_layout="KN"), f"dx g{gidx}")
 
 
+def test_wgrad_reference_models_golden(cuda_dev, golden):
+    """Grouped wgrad bundles (dW[g] = dy[seg].T @ x[seg], "TN") vs case05/09
+    Model outputs and the fp32 oracle."""
+    z = golden("gemm_swiglu.npz")
+    for tag, case in (("c05", "case05_moe_grouped_gemm_fc2_wgrad"),
+                      ("c09", "case09_moe_grouped_gemm_fc1_wgrad")):
+        sp = z[f"{tag}_splits"]
+        dw = load_bundle(case).kernel_function(from_u16(z[f"{tag}_dy"], cuda_dev),
+                                               from_u16(z[f"{tag}_x"], cuda_dev),
+                                               num_groups=len(sp))
+        assert dw.dtype == torch.bfloat16 and dw.shape == z[f"{tag}_dw"].shape
+        assert_gemm_close(dw, orc.bf16_to_f32(z[f"{tag}_dw"]), tag)
+        assert_gemm_close(dw, _wgrad_f32(z[f"{tag}_dy"], z[f"{tag}_x"], sp), tag)
+
+
+def _wgrad_f32(dy_u16, x_u16, splits):
+    """Unrounded fp32 dy[seg].T @ x[seg] per group, [G,N,K]."""
+    out = np.zeros((len(splits), dy_u16.shape[1], x_u16.shape[1]), np.float32)
+    off = 0
+    for g, m in enumerate(splits):
+        m = int(m)
+        if m:
+            out[g] = orc.bf16_to_f32(dy_u16[off:off + m]).T @ orc.bf16_to_f32(x_u16[off:off + m])
+        off += m
+    return out
+
+
+@pytest.mark.parametrize("splits,n,k", [
+    ([0, 1, 63, 64, 65, 200, 0, 128], 256, 256),   # empty groups, partial 64-row blocks
+    ([700, 33, 513], 512, 768),
+    ([10, 0, 250], 200, 72),                       # N, K off the 128 x 256 tile
+    ([5], 128, 8192),
+])
+def test_wgrad_ragged_vs_oracle(cuda_dev, splits, n, k):
+    import moe_b200
+    g = torch.Generator().manual_seed(sum(splits) + n + 7 * k)
+    rows = sum(splits) + 3  # trailing rows that no group owns must not leak in
+    dy = _rand_bf16(g, rows, n)
+    x = _rand_bf16(g, rows, k)
+    dw = moe_b200.grouped_wgrad(dy.to(cuda_dev), x.to(cuda_dev), splits)
+    ref = _wgrad_f32(u16(dy), u16(x), splits)
+    assert_gemm_close(dw, ref, f"wgrad {splits}")
+    for gi, m in enumerate(splits):
+        if m == 0:
+            assert int(dw[gi].view(torch.int16).abs().sum()) == 0  # zeros, like torch.mm
+
+
+def test_wgrad_reference_shape_spot_check(cuda_dev):
+    """case09's traced shape: 40 groups over 4096 rows, N=5120, K=8192;
+    dW[g] checked on sampled 64 x 64 blocks of sampled groups."""
+    import moe_b200
+    gsz, t, n, k = 40, 4096, 5120, 8192
+    gd = torch.Generator(device=cuda_dev).manual_seed(9)
+    dy = torch.randn(t, n, device=cuda_dev, generator=gd).to(torch.bfloat16)
+    x = torch.randn(t, k, device=cuda_dev, generator=gd).to(torch.bfloat16)
+    dw = load_bundle("case09_moe_grouped_gemm_fc1_wgrad").kernel_function(dy, x)
+    assert tuple(dw.shape) == (gsz, n, k)
+    base, rem = divmod(t, gsz)
+    splits = [base + (1 if i < rem else 0) for i in range(gsz)]
+    starts = np.concatenate([[0], np.cumsum(splits)[:-1]])
+    rng = np.random.default_rng(3)
+    for gi in (0, 17, gsz - 1):
+        for _ in range(2):
+            n0 = int(rng.integers(0, n // 64)) * 64
+            k0 = int(rng.integers(0, k // 64)) * 64
+            seg = slice(int(starts[gi]), int(starts[gi]) + splits[gi])
+            ref = orc.bf16_to_f32(u16(dy[seg, n0:n0 + 64])).T @ orc.bf16_to_f32(
+                u16(x[seg, k0:k0 + 64]))
+            assert_gemm_close(dw[gi, n0:n0 + 64, k0:k0 + 64], ref, f"g{gi} {n0} {k0}")
+
+
 def test_router_gemm_golden(cuda_dev, golden):
     """case38 bundle (router logits, fp32 out) vs the reference's reference_fp32."""
     z = golden("gemm_swiglu.npz")

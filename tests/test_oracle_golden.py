@@ -214,6 +214,15 @@ def test_grouped_dgrad_against_reference_models(golden):
         _gemm_close(y, orc.bf16_to_f32(z[f"{tag}_dx"]))
 
 
+def test_grouped_wgrad_against_reference_models(golden):
+    """case05 (fc2) and case09 (fc1): dW[g] = dy[seg].T @ x[seg]."""
+    z = golden("gemm_swiglu.npz")
+    for tag in ("c05", "c09"):
+        y = orc.grouped_wgrad(z[f"{tag}_dy"], z[f"{tag}_x"], z[f"{tag}_splits"])
+        assert y.shape == z[f"{tag}_dw"].shape
+        _gemm_close(y, orc.bf16_to_f32(z[f"{tag}_dw"]))
+
+
 def test_router_gemm_fp32_golden(golden):
     """case38 reference_fp32 (router gate GEMM, fp32 out) at N = 320 experts:
     both sides accumulate in fp32 and differ only in summation order."""
