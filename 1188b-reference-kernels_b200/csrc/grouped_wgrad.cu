@@ -19,8 +19,11 @@
 // Kernel structure (one persistent CTA per SM, 192 threads), as the forward
 // single-CTA kernel: warp 0 TMA producer (4-stage ring, 16 KB dy + 32 KB x per
 // stage), warp 1 TMEM owner and single-thread MMA issuer (M=128 dW rows,
-// N=256 dW columns, K=16), warps 2-5 epilogue through 64B-swizzled shared
-// buffers and TMA tile stores. Every wait is bounded (2 s).
+// N=256 dW columns, K=16), warps 2-5 epilogue. With few rows per group the
+// tile's mainloop is short and dW's bytes dominate, so the epilogue moves 64
+// columns per step (two TMEM loads under one wait, one 32 x 64 TMA tile store
+// from a 128B-swizzled buffer, four stores in flight per warp). Every wait is
+// bounded (2 s).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <string.h>
@@ -37,25 +40,29 @@ namespace gw {
 constexpr int BM = 128;  // dW rows per tile (columns of dy)
 constexpr int BN = 256;  // dW columns per tile (columns of x)
 constexpr int BK = 64;   // reduction rows per stage
-constexpr int kStages = 4;
+constexpr int kStages = 3;  // K-loops are a group's rows / 64: short for most groups
 constexpr int kThreads = 192;
 constexpr uint32_t kBox = 64 * 64 * 2;          // one 64-column x 64-row bf16 box
 constexpr uint32_t kABytes = (BM / 64) * kBox;  // 16 KB of dy
 constexpr uint32_t kBBytes = (BN / 64) * kBox;  // 32 KB of x
 constexpr uint32_t kStageBytes = kABytes + kBBytes;
 constexpr uint32_t kTmemCols = 2 * BN;
-constexpr uint32_t kEpiBoxBytes = 32 * 32 * 2;  // 32 rows x 32 bf16 columns
-constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + 1024 + 4 * 2 * kEpiBoxBytes;
+constexpr uint32_t kEpiBoxBytes = 32 * 64 * 2;  // 32 rows x 64 bf16 columns, 128B-swizzled
+constexpr int kEpiBufs = 4;                     // tile stores in flight per epilogue warp
+constexpr size_t kSmemBytes = 1024 + kStages * kStageBytes + 1024 + 4 * kEpiBufs * kEpiBoxBytes;
 constexpr int kErrTimeoutProducer = 1;
 constexpr int kErrTimeoutMma = 2;
 constexpr int kErrTimeoutEpilogue = 3;
 
+// Only groups with rows are walked (their dW slices of empty groups are
+// zeroed by the host with memsets); entry i of the tables is group gid[i].
 struct Params {
-  const CUtensorMap* maps;  // [2G] in global memory: rows of group g of dy, then of x
-  const int32_t* rows;      // [G] rows of each group
+  const CUtensorMap* maps;  // [2Gnz] in global memory: rows of group gid[i] of dy, then of x
+  const int32_t* rows;      // [Gnz] rows of those groups
+  const int32_t* gid;       // [Gnz] their group ids
   int32_t* err;
   __nv_bfloat16* out;  // dW [G, N, K]
-  int G, N, K;
+  int G, N, K;         // G = groups with rows
   int m_tiles, n_tiles;
 };
 
@@ -120,6 +127,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const long long per_g = static_cast<long long>(p.m_tiles) * p.n_tiles;
   const long long total = per_g * p.G;
+  // g: index into the tables (and maps); p.gid[g] is the group's id in dW.
   auto locate = [&](long long t, int& g, int& mi, int& ni) {
     g = static_cast<int>(t / per_g);
     const int r = static_cast<int>(t - g * per_g);
@@ -238,7 +246,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ------------------------------------------------------------ epilogue
     const int quad = warp & 3;  // TMEM lanes this warp may access: 32*quad ..
     const uint32_t epi_base = ((bar0 + 512u + 1023u) & ~1023u) +
-                              static_cast<uint32_t>(quad) * 2u * kEpiBoxBytes;
+                              static_cast<uint32_t>(quad) * kEpiBufs * kEpiBoxBytes;
     uint32_t chunk_no = 0;
     int it = 0;
     bool ok = true;
@@ -256,36 +264,41 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int rowl = mi * BM + quad * 32 + lane;  // row of dW[g]
       const bool rvalid = rowl < p.N;
       const bool tma = __all_sync(0xffffffffu, rvalid);
-      const int warp_row0 = g * p.N + mi * BM + quad * 32;  // in the [G*N, K] view
-      __nv_bfloat16* orow = p.out + (static_cast<int64_t>(g) * p.N + rowl) * p.K;
+      const int gd = p.gid[g];                               // group id in dW
+      const int warp_row0 = gd * p.N + mi * BM + quad * 32;  // in the [G*N, K] view
+      __nv_bfloat16* orow = p.out + (static_cast<int64_t>(gd) * p.N + rowl) * p.K;
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int col = ni * BN + c * 32;
+      for (int c = 0; c < BN / 64; ++c) {
+        const int col = ni * BN + c * 64;
         if (col >= p.K) break;  // warp-uniform
-        uint32_t r[32];
+        uint32_t r[64];
         if (!no_rows) {
-          tmem_ld_32x32b_x32(tbase + c * 32, r);
+          uint32_t (&r0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[0]);
+          uint32_t (&r1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[32]);
+          tmem_ld_32x32b_x32(tbase + c * 64, r0);
+          tmem_ld_32x32b_x32(tbase + c * 64 + 32, r1);
           tmem_ld_wait();
         } else {
 #pragma unroll
-          for (int q = 0; q < 32; ++q) r[q] = 0u;
+          for (int q = 0; q < 64; ++q) r[q] = 0u;
         }
-        uint32_t o[16];
+        uint32_t o[32];  // this lane's row: 64 bf16 = 128 bytes
 #pragma unroll
-        for (int q = 0; q < 16; ++q)
+        for (int q = 0; q < 32; ++q)
           o[q] = pack_bf16x2(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1]));
         if (tma) {
-          const uint32_t buf = epi_base + (chunk_no & 1u) * kEpiBoxBytes;
+          const uint32_t buf = epi_base + (chunk_no % kEpiBufs) * kEpiBoxBytes;
           ++chunk_no;
-          if (lane == 0) bulk_wait_read<1>();
+          if (lane == 0) bulk_wait_read<kEpiBufs - 1>();
           __syncwarp();
-          const uint32_t sw = static_cast<uint32_t>((lane >> 1) & 3);
+          // 128-byte swizzle: 16-byte chunk j of row r lives at chunk j ^ (r & 7).
+          const uint32_t sw = static_cast<uint32_t>(lane & 7);
 #pragma unroll
-          for (int j = 0; j < 4; ++j) {
+          for (int j = 0; j < 8; ++j) {
             const uint32_t dst =
-                buf + static_cast<uint32_t>(lane) * 64u + ((static_cast<uint32_t>(j) ^ sw) << 4);
+                buf + static_cast<uint32_t>(lane) * 128u + ((static_cast<uint32_t>(j) ^ sw) << 4);
             asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(o[4 * j]),
                          "r"(o[4 * j + 1]), "r"(o[4 * j + 2]), "r"(o[4 * j + 3])
                          : "memory");
@@ -298,7 +311,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         } else if (rvalid) {
 #pragma unroll
-          for (int v = 0; v < 4; ++v)
+          for (int v = 0; v < 8; ++v)
             if (col + v * 8 + 8 <= p.K)
               *reinterpret_cast<uint4*>(orow + col + v * 8) =
                   make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
@@ -359,7 +372,9 @@ int encode_bf16(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer,
 }
 
 size_t rows_bytes(int64_t G) { return (static_cast<size_t>(G) * 4 + 255) & ~static_cast<size_t>(255); }
-size_t ws_bytes(int64_t G) { return 256 + rows_bytes(G) + 2 * static_cast<size_t>(G) * sizeof(CUtensorMap); }
+size_t ws_bytes(int64_t G) {
+  return 256 + 2 * rows_bytes(G) + 2 * static_cast<size_t>(G) * sizeof(CUtensorMap);
+}
 
 int ensure_smem_attr() {
   int dev = 0;
@@ -416,53 +431,77 @@ extern "C" int moe_grouped_wgrad(const void* dy, const void* x, void* dw, int64_
   int st = gw::ensure_smem_attr();
   if (st) return st;
 
-  // Host image of the workspace after the error word: row counts, then the
-  // per-group tensor maps (dy rows of g, x rows of g).
+  // Host image of the workspace after the error word, for the groups with
+  // rows only: row counts, group ids, then the tensor maps (dy rows, x rows).
   const size_t rb = gw::rows_bytes(G);
-  std::vector<uint8_t> host(rb + 2 * static_cast<size_t>(G) * sizeof(CUtensorMap), 0);
-  memcpy(host.data(), m_splits, static_cast<size_t>(G) * 4);
-  std::vector<CUtensorMap> maps(2 * static_cast<size_t>(G));
+  std::vector<int32_t> rows_nz, gid_nz;
+  std::vector<CUtensorMap> maps;
   const char* dyb = static_cast<const char*>(dy);
   const char* xb = static_cast<const char*>(x);
   int64_t r0 = 0;
   for (int64_t g = 0; g < G; ++g) {
     const int64_t m = m_splits[g];
-    // A group without rows never loads; its maps only need to be valid.
-    const uint64_t outer = static_cast<uint64_t>(m > 0 ? m : 1);
-    const int64_t start = m > 0 ? r0 : 0;
-    if ((st = gw::encode_bf16(&maps[2 * g], dyb + start * N * 2, static_cast<uint64_t>(N), outer,
-                              64u, 64u, CU_TENSOR_MAP_SWIZZLE_128B)) ||
-        (st = gw::encode_bf16(&maps[2 * g + 1], xb + start * K * 2, static_cast<uint64_t>(K),
-                              outer, 64u, 64u, CU_TENSOR_MAP_SWIZZLE_128B)))
-      return st;
+    if (m > 0) {
+      CUtensorMap a, b;
+      if ((st = gw::encode_bf16(&a, dyb + r0 * N * 2, static_cast<uint64_t>(N),
+                                static_cast<uint64_t>(m), 64u, 64u, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+          (st = gw::encode_bf16(&b, xb + r0 * K * 2, static_cast<uint64_t>(K),
+                                static_cast<uint64_t>(m), 64u, 64u, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return st;
+      maps.push_back(a);
+      maps.push_back(b);
+      rows_nz.push_back(static_cast<int32_t>(m));
+      gid_nz.push_back(static_cast<int32_t>(g));
+    }
     r0 += m;
   }
-  memcpy(host.data() + rb, maps.data(), maps.size() * sizeof(CUtensorMap));
+  const int64_t gnz = static_cast<int64_t>(rows_nz.size());
+  std::vector<uint8_t> host(2 * rb + maps.size() * sizeof(CUtensorMap), 0);
+  if (gnz > 0) {
+    memcpy(host.data(), rows_nz.data(), rows_nz.size() * 4);
+    memcpy(host.data() + rb, gid_nz.data(), gid_nz.size() * 4);
+    memcpy(host.data() + 2 * rb, maps.data(), maps.size() * sizeof(CUtensorMap));
+  }
   CUtensorMap tout;
-  st = gw::encode_bf16(&tout, dw, static_cast<uint64_t>(K), static_cast<uint64_t>(G * N), 32u,
-                       32u, CU_TENSOR_MAP_SWIZZLE_64B);
+  st = gw::encode_bf16(&tout, dw, static_cast<uint64_t>(K), static_cast<uint64_t>(G * N), 64u,
+                       32u, CU_TENSOR_MAP_SWIZZLE_128B);
   if (st) return st;
 
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
   MOE_CUDA_CALL(cudaMemsetAsync(ws, 0, 4, s), "grouped_wgrad: clear error word");
+  // dW of the groups without rows: zeros, one memset per run of such groups.
+  const size_t slice = static_cast<size_t>(N) * static_cast<size_t>(K) * 2;
+  for (int64_t g = 0; g < G;) {
+    if (m_splits[g] > 0) {
+      ++g;
+      continue;
+    }
+    int64_t e = g;
+    while (e < G && m_splits[e] == 0) ++e;
+    MOE_CUDA_CALL(cudaMemsetAsync(static_cast<char*>(dw) + g * slice, 0, (e - g) * slice, s),
+                  "grouped_wgrad: zero empty groups");
+    g = e;
+  }
+  if (gnz == 0) return MOE_OK;
   // From pageable memory: returns once the bytes are staged, so `host` may go.
   MOE_CUDA_CALL(cudaMemcpyAsync(ws + 256, host.data(), host.size(), cudaMemcpyHostToDevice, s),
                 "grouped_wgrad: upload group table");
 
   gw::Params p;
-  p.maps = reinterpret_cast<const CUtensorMap*>(ws + 256 + rb);
+  p.maps = reinterpret_cast<const CUtensorMap*>(ws + 256 + 2 * rb);
   p.rows = reinterpret_cast<const int32_t*>(ws + 256);
+  p.gid = reinterpret_cast<const int32_t*>(ws + 256 + rb);
   p.err = reinterpret_cast<int32_t*>(ws);
   p.out = static_cast<__nv_bfloat16*>(dw);
-  p.G = static_cast<int>(G);
+  p.G = static_cast<int>(gnz);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
   p.m_tiles = static_cast<int>((N + gw::BM - 1) / gw::BM);
   p.n_tiles = static_cast<int>((K + gw::BN - 1) / gw::BN);
   int dev = 0;
   MOE_CUDA_CALL(cudaGetDevice(&dev), "cudaGetDevice");
-  const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles * G;
+  const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles * gnz;
   const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms(dev)));
   gw::grouped_wgrad_kernel<<<grid, gw::kThreads, gw::kSmemBytes, s>>>(tout, p);
   MOE_CUDA_CHECK_LAUNCH("grouped_wgrad launch");

@@ -60,13 +60,20 @@ def parse_args():
     ap.add_argument("--placement", choices=["balanced", "contiguous"], default="balanced",
                     help="EP expert placement: load-balanced (E/G experts per GPU, chosen from "
                          "the routing of the benchmark's own logits) or contiguous id ranges")
-    ap.add_argument("--transport", choices=["fused", "peer", "nccl"], default="fused",
-                    help="EP row exchange: dispatch/combine kernels on peer memory, "
-                         "IPC-mapped buffers + copy engines, or NCCL all-to-all")
-    ap.add_argument("--workload", choices=["layer", "router_gemm", "backward"], default="layer",
+    ap.add_argument("--transport", choices=["fused", "fused_dedup", "peer", "nccl"],
+                    default="fused",
+                    help="EP row exchange: dispatch/combine kernels on peer memory (fused_dedup: "
+                         "a token row crosses NVLink once per destination rank), IPC-mapped "
+                         "buffers + copy engines, or NCCL all-to-all")
+    ap.add_argument("--workload", choices=["layer", "router_gemm", "backward", "wgrad"],
+                    default="layer",
                     help="layer: the MoE expert-layer forward (the headline); router_gemm: the "
                          "router gate GEMM that produces its logits; backward: the layer's "
-                         "grouped dgrad and wgrad GEMMs (one GPU)")
+                         "grouped dgrad and wgrad GEMMs; wgrad: the grouped wgrad alone at "
+                         "--wgrad-shape (one GPU)")
+    ap.add_argument("--wgrad-shape", default="40,4096,5120,8192",
+                    help="G,T,N,K of --workload wgrad (uniform groups; default: the traced "
+                         "shape of kernel_cases/case09_moe_grouped_gemm_fc1_wgrad.py)")
     ap.add_argument("--router-shape", default="16384,8192,320",
                     help="M,K,N of the router GEMM (tokens, hidden, experts)")
     return ap.parse_args()
@@ -430,6 +437,59 @@ def run_backward(a):
     print(json.dumps(line), flush=True)
 
 
+# --------------------------------------------------------------------------- grouped wgrad alone
+def run_wgrad(a):
+    """dW[g] = dy[seg]^T @ x[seg] over G uniform groups of T rows (N(0,1)
+    inputs), timed over --steps calls of the public op."""
+    import torch
+    import moe_b200
+    from moe_b200 import _lib
+    gsz, t, n, k = (int(v) for v in a.wgrad_shape.split(","))
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    moe_b200.load_library()
+    g = torch.Generator(device=dev)
+    g.manual_seed(9)
+    dy = torch.randn(t, n, device=dev, generator=g).to(torch.bfloat16)
+    x = torch.randn(t, k, device=dev, generator=g).to(torch.bfloat16)
+    base, rem = divmod(t, gsz)
+    splits = [base + (1 if i < rem else 0) for i in range(gsz)]
+    out = torch.empty(gsz, n, k, dtype=torch.bfloat16, device=dev)
+    sampler = ClockSampler(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0])
+    sampler.start()
+    for _ in range(a.warmup):
+        moe_b200.grouped_wgrad(dy, x, splits, out=out)
+    torch.cuda.synchronize()
+    launches0 = _lib.launch_count
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    wall0 = time.time()
+    ev[0].record()
+    for _ in range(a.steps):
+        moe_b200.grouped_wgrad(dy, x, splits, out=out)
+    ev[1].record()
+    torch.cuda.synchronize()
+    sampler.mark(wall0, time.time())
+    launches = _lib.launch_count - launches0
+    clocks = sampler.stop()
+    sec = ev[0].elapsed_time(ev[1]) / 1e3 / a.steps
+    flops = 2.0 * t * n * k
+    nbytes = gsz * n * k * 2 + t * (n + k) * 2
+    peaks, peak_kind = load_peaks()
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    line = {"metric": "grouped wgrad TFLOP/s", "value": flops / sec / 1e12, "unit": "TFLOP/s",
+            "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": sec * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (N(0,1))",
+            "config": {"workload": "grouped_wgrad", "groups": gsz, "rows": t, "n": n, "k": k,
+                       "l2": "no flush: dW is larger than L2"},
+            "roofline": {"bound": "hbm", "kernel": "grouped_wgrad_kernel",
+                         "achieved": round(nbytes / sec / 1e9, 1), "peak": hbm, "unit": "GB/s",
+                         "frac": round(nbytes / sec / 1e9 / hbm, 4), "traffic": None},
+            "peak_kind": f"hbm copy, of {peak_kind}",
+            "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 # --------------------------------------------------------------------------- GPU arm
 def read_traffic():
     p = ROOT / "profiles" / "grouped_gemm_fc1_layer.txt"
@@ -456,6 +516,10 @@ def main():
     if a.workload == "backward":
         if rank == 0 and a.impl != "reference":
             run_backward(a)
+        return
+    if a.workload == "wgrad":
+        if rank == 0 and a.impl != "reference":
+            run_wgrad(a)
         return
     if a.impl == "reference":
         run_reference_arm(a, world, rank)
