@@ -137,6 +137,121 @@ __global__ void __launch_bounds__(kRowThreads) ep_combine_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// Deduplicated dispatch: a token row crosses NVLink once per destination rank
+// instead of once per (token, expert). Each rank owns a staging block per
+// source rank ([T rows] of token rows + [T x E_loc] int32 destination rows,
+// -1 = not routed there) and a per-source row counter that the sources bump
+// with remote atomics. Rows for this rank's own experts are written straight
+// into the receive buffer. After the barrier, ep_expand_kernel copies every
+// staged row to its listed receive rows; the receive layout (and so the
+// GEMMs and the combine) is the same as without deduplication.
+// ---------------------------------------------------------------------------
+struct StageRows {
+  long long stage[kMaxRanks];  // rank d's staging rows, this process's address
+  long long meta[kMaxRanks];   // rank d's destination-row table
+  long long count[kMaxRanks];  // rank d's per-source counters (int32 [ranks])
+  long long rows_per_src;      // staging rows per source (T)
+  int my_rank;
+};
+
+constexpr int kDedupMaxE = 1024;
+
+template <int VPT, typename V>
+__global__ void __launch_bounds__(kRowThreads) ep_dispatch_dedup_kernel(
+    const V* __restrict__ x, const int64_t* __restrict__ map_te, const PeerRows pr,
+    const StageRows sr, int64_t T, int E, int nvec, int64_t num_rows) {
+  __shared__ long long s_dest[kDedupMaxE];  // receive row per expert (-1: not routed)
+  __shared__ int s_has[kMaxRanks];
+  __shared__ int s_slot;
+  const int64_t t = blockIdx.x;
+  const int tid = threadIdx.x;
+  const int el = pr.experts_per_rank;
+  const V* src = x + t * nvec;
+  V r[VPT];
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int i = tid + v * kRowThreads;
+    if (i < nvec) r[v] = __ldg(src + i);
+  }
+  if (tid < kMaxRanks) s_has[tid] = 0;
+  __syncthreads();
+  for (int e = tid; e < E; e += kRowThreads) {
+    const int64_t row = __ldg(map_te + t * E + e);
+    long long base = 0;
+    int64_t rr = -1;
+    const bool valid = row >= 0 && row < num_rows && peer_row(pr, e, row, base, rr);
+    s_dest[e] = valid ? rr : -1;
+    if (valid) s_has[e / el] = 1;
+  }
+  __syncthreads();
+  for (int d = 0; d < pr.ranks; ++d) {
+    if (!s_has[d]) continue;  // block-uniform
+    if (d == sr.my_rank) {
+      // own experts: straight into this rank's receive buffer, one copy per expert
+      for (int le = 0; le < el; ++le) {
+        const long long rr = s_dest[d * el + le];
+        if (rr < 0) continue;
+        V* o = reinterpret_cast<V*>(pr.base[d]) + rr * nvec;
+#pragma unroll
+        for (int v = 0; v < VPT; ++v) {
+          const int i = tid + v * kRowThreads;
+          if (i < nvec) o[i] = r[v];
+        }
+      }
+      continue;
+    }
+    if (tid == 0) s_slot = atomicAdd(reinterpret_cast<int*>(sr.count[d]) + sr.my_rank, 1);
+    __syncthreads();
+    const long long slot = s_slot;
+    __syncthreads();
+    if (slot >= sr.rows_per_src) continue;  // cannot happen for a valid map; never overrun
+    const long long srow = static_cast<long long>(sr.my_rank) * sr.rows_per_src + slot;
+    V* o = reinterpret_cast<V*>(sr.stage[d]) + srow * nvec;
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const int i = tid + v * kRowThreads;
+      if (i < nvec) o[i] = r[v];
+    }
+    int* m = reinterpret_cast<int*>(sr.meta[d]) + srow * el;
+    for (int le = tid; le < el; le += kRowThreads)
+      m[le] = static_cast<int>(s_dest[d * el + le]);
+  }
+}
+
+// Receiver side: each staged row (of every other source) is read once and
+// written to the receive rows its table lists. Grid-stride over all slots.
+template <int VPT, typename V>
+__global__ void __launch_bounds__(kRowThreads) ep_expand_kernel(
+    const V* __restrict__ stage, const int* __restrict__ meta, const int* __restrict__ count,
+    V* __restrict__ recv, int ranks, int my_rank, int el, long long rows_per_src,
+    long long cap_rows, int nvec) {
+  const long long total = static_cast<long long>(ranks) * rows_per_src;
+  for (long long i = blockIdx.x; i < total; i += gridDim.x) {
+    const int s = static_cast<int>(i / rows_per_src);
+    const long long j = i - s * rows_per_src;
+    if (s == my_rank || j >= __ldg(count + s)) continue;  // block-uniform
+    const V* src = stage + i * nvec;
+    V r[VPT];
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const int q = threadIdx.x + v * kRowThreads;
+      if (q < nvec) r[v] = __ldg(src + q);
+    }
+    const int* m = meta + i * el;
+    for (int le = 0; le < el; ++le) {
+      const long long rr = __ldg(m + le);
+      if (rr < 0 || rr >= cap_rows) continue;
+      V* o = recv + rr * nvec;
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        const int q = threadIdx.x + v * kRowThreads;
+        if (q < nvec) o[q] = r[v];
+      }
+    }
+  }
+}
+
 int make_peer_rows(PeerRows& pr, const int64_t* bases, const int64_t* expert_deltas, int ranks,
                    int experts_per_rank, int64_t cap_rows, int64_t E, int64_t H, int& vbytes,
                    const char* who) {
@@ -229,5 +344,99 @@ extern "C" int moe_ep_combine(const int64_t* peer_bases, const int64_t* expert_d
                                                              (int)E, static_cast<int>(H),
                                                              num_rows);
   MOE_CUDA_CHECK_LAUNCH("ep_combine launch");
+  return MOE_OK;
+}
+
+extern "C" int moe_ep_dispatch_dedup(const void* x, const int64_t* row_id_map_te,
+                                     const int64_t* peer_bases, const int64_t* expert_deltas,
+                                     const int64_t* peer_stage, const int64_t* peer_meta,
+                                     const int64_t* peer_count, int32_t ranks, int32_t my_rank,
+                                     int32_t experts_per_rank, int64_t cap_rows, int64_t T,
+                                     int64_t H, int64_t E, int64_t num_rows,
+                                     moe_stream_t stream) {
+  MOE_REQUIRE(T >= 0 && H >= 0 && E >= 1, "ep_dispatch_dedup: bad shape");
+  MOE_REQUIRE(E <= kDedupMaxE, "ep_dispatch_dedup: E=%lld above %d", (long long)E, kDedupMaxE);
+  if (T == 0 || H == 0) return MOE_OK;
+  MOE_REQUIRE(x && row_id_map_te && peer_stage && peer_meta && peer_count,
+              "ep_dispatch_dedup: null pointer");
+  MOE_REQUIRE(my_rank >= 0 && my_rank < ranks, "ep_dispatch_dedup: my_rank out of range");
+  PeerRows pr;
+  int vb = 16;
+  int st = make_peer_rows(pr, peer_bases, expert_deltas, ranks, experts_per_rank, cap_rows, E, H,
+                          vb, "ep_dispatch_dedup");
+  if (st) return st;
+  StageRows sr;
+  for (int d = 0; d < kMaxRanks; ++d) {
+    const bool in = d < ranks;
+    MOE_REQUIRE(!in || (peer_stage[d] && peer_meta[d] && peer_count[d]),
+                "ep_dispatch_dedup: null staging buffer for rank %d", d);
+    sr.stage[d] = in ? peer_stage[d] : 0;
+    sr.meta[d] = in ? peer_meta[d] : 0;
+    sr.count[d] = in ? peer_count[d] : 0;
+    if (in && (static_cast<uintptr_t>(peer_stage[d]) & 15) != 0) vb = 2;
+  }
+  sr.rows_per_src = T;
+  sr.my_rank = my_rank;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) vb = 2;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned grid = static_cast<unsigned>(T);
+  if (vb == 16) {
+    const int nvec = static_cast<int>(H / 8);
+    const int vpt = (nvec + kRowThreads - 1) / kRowThreads;
+    MOE_REQUIRE(vpt <= 8, "ep_dispatch_dedup: H=%lld above 8192", (long long)H);
+    const uint4* xv = static_cast<const uint4*>(x);
+    if (vpt <= 2) ep_dispatch_dedup_kernel<2, uint4><<<grid, kRowThreads, 0, s>>>(xv, row_id_map_te, pr, sr, T, (int)E, nvec, num_rows);
+    else if (vpt <= 4) ep_dispatch_dedup_kernel<4, uint4><<<grid, kRowThreads, 0, s>>>(xv, row_id_map_te, pr, sr, T, (int)E, nvec, num_rows);
+    else ep_dispatch_dedup_kernel<8, uint4><<<grid, kRowThreads, 0, s>>>(xv, row_id_map_te, pr, sr, T, (int)E, nvec, num_rows);
+  } else {
+    const int nvec = static_cast<int>(H);
+    const int vpt = (nvec + kRowThreads - 1) / kRowThreads;
+    MOE_REQUIRE(vpt <= 16, "ep_dispatch_dedup: H=%lld above 2048 for unaligned rows", (long long)H);
+    ep_dispatch_dedup_kernel<16, uint16_t><<<grid, kRowThreads, 0, s>>>(
+        static_cast<const uint16_t*>(x), row_id_map_te, pr, sr, T, (int)E, nvec, num_rows);
+  }
+  MOE_CUDA_CHECK_LAUNCH("ep_dispatch_dedup launch");
+  return MOE_OK;
+}
+
+extern "C" int moe_ep_expand(const void* stage, const int32_t* meta, int32_t* count, void* recv,
+                             int32_t ranks, int32_t my_rank, int32_t experts_per_rank,
+                             int64_t rows_per_src, int64_t cap_rows, int64_t H,
+                             moe_stream_t stream) {
+  MOE_REQUIRE(ranks >= 1 && ranks <= kMaxRanks && my_rank >= 0 && my_rank < ranks,
+              "ep_expand: bad ranks=%d my_rank=%d", ranks, my_rank);
+  MOE_REQUIRE(experts_per_rank >= 1 && rows_per_src >= 0 && cap_rows >= 0 && H >= 0,
+              "ep_expand: bad sizes");
+  MOE_REQUIRE(stage && meta && count && recv, "ep_expand: null pointer");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  if (rows_per_src > 0 && H > 0) {
+    int dev = 0;
+    MOE_CUDA_CALL(cudaGetDevice(&dev), "cudaGetDevice");
+    const long long total = static_cast<long long>(ranks) * rows_per_src;
+    const unsigned grid = static_cast<unsigned>(std::min<long long>(total, 16ll * num_sms(dev)));
+    const bool al = ((reinterpret_cast<uintptr_t>(stage) | reinterpret_cast<uintptr_t>(recv)) & 15) == 0 &&
+                    H % 8 == 0;
+    if (al) {
+      const int nvec = static_cast<int>(H / 8);
+      const int vpt = (nvec + kRowThreads - 1) / kRowThreads;
+      MOE_REQUIRE(vpt <= 8, "ep_expand: H=%lld above 8192", (long long)H);
+      const uint4* sv = static_cast<const uint4*>(stage);
+      uint4* rv = static_cast<uint4*>(recv);
+      if (vpt <= 2) ep_expand_kernel<2, uint4><<<grid, kRowThreads, 0, s>>>(sv, meta, count, rv, ranks, my_rank, experts_per_rank, rows_per_src, cap_rows, nvec);
+      else if (vpt <= 4) ep_expand_kernel<4, uint4><<<grid, kRowThreads, 0, s>>>(sv, meta, count, rv, ranks, my_rank, experts_per_rank, rows_per_src, cap_rows, nvec);
+      else ep_expand_kernel<8, uint4><<<grid, kRowThreads, 0, s>>>(sv, meta, count, rv, ranks, my_rank, experts_per_rank, rows_per_src, cap_rows, nvec);
+    } else {
+      const int nvec = static_cast<int>(H);
+      MOE_REQUIRE(nvec <= 16 * kRowThreads, "ep_expand: H=%lld above 2048 for unaligned rows",
+                  (long long)H);
+      ep_expand_kernel<16, uint16_t><<<grid, kRowThreads, 0, s>>>(
+          static_cast<const uint16_t*>(stage), meta, count, static_cast<uint16_t*>(recv), ranks,
+          my_rank, experts_per_rank, rows_per_src, cap_rows, nvec);
+    }
+    MOE_CUDA_CHECK_LAUNCH("ep_expand launch");
+  }
+  // the counters start from zero for the next forward's dispatch
+  MOE_CUDA_CALL(cudaMemsetAsync(count, 0, static_cast<size_t>(ranks) * sizeof(int32_t), s),
+                "ep_expand: clear counters");
   return MOE_OK;
 }

@@ -219,12 +219,16 @@ class EPPeerExchange:
 
     def __init__(self, num_experts: int, tokens: int, hidden: int, topk: int,
                  device: torch.device, group: Optional[dist.ProcessGroup] = None,
-                 fused: bool = False):
+                 fused: bool = False, dedup: bool = False):
         """fused=False: receive + return buffers, rows moved by copy engines.
         fused=True: receive + fc2-output buffers; the dispatch kernel stores
         rows into the peers' receive buffers and the combine kernel loads the
-        results from the peers' fc2 outputs."""
+        results from the peers' fc2 outputs. dedup=True (with fused): a token
+        row crosses NVLink once per destination rank into that rank's staging
+        rows, and each rank expands them into its receive buffer."""
         self.fused = fused
+        self.dedup = bool(dedup and fused)
+        self.tokens = int(tokens)
         self.group = group
         self.world = dist.get_world_size(group)
         self.rank = dist.get_rank(group)
@@ -246,6 +250,15 @@ class EPPeerExchange:
             self.y_buf = torch.empty((self.recv_cap, hidden), dtype=torch.bfloat16,
                                      device=self.device)
             self.peer_y = self._share(self.y_buf)
+        if self.dedup:
+            rows = self.world * self.tokens
+            self.stage_buf = torch.empty((rows, hidden), dtype=torch.bfloat16, device=self.device)
+            self.stage_meta = torch.empty((rows, self.local_experts), dtype=torch.int32,
+                                          device=self.device)
+            self.stage_count = torch.zeros(self.world, dtype=torch.int32, device=self.device)
+            self.peer_stage = self._share(self.stage_buf)
+            self.peer_meta = self._share(self.stage_meta)
+            self.peer_count = self._share(self.stage_count)
         else:
             self.ret_buf = torch.empty((self.rows_cap, hidden), dtype=torch.bfloat16,
                                        device=self.device)
@@ -351,6 +364,27 @@ class EPPeerExchange:
         self.barrier()
         return self.recv_buf[:nrecv]
 
+    def fused_dispatch_dedup(self, x: torch.Tensor, map_te: torch.Tensor, deltas: torch.Tensor,
+                             nsend: int, nrecv: int) -> torch.Tensor:
+        """Token rows once per destination rank into the peers' staging rows
+        (own experts straight into the receive buffer), barrier, then this
+        rank's expansion of its staging rows into the receive buffer."""
+        t, h = x.shape
+        if t > self.tokens:
+            raise ValueError(f"{t} tokens exceed the staging capacity of {self.tokens}")
+        n = self.world
+        arr = lambda v: (ctypes.c_int64 * n)(*v)  # noqa: E731
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.call("moe_ep_dispatch_dedup", x.data_ptr(), map_te.data_ptr(), arr(self.peer_recv),
+                  deltas.data_ptr(), arr(self.peer_stage), arr(self.peer_meta),
+                  arr(self.peer_count), n, self.rank, self.local_experts, self.recv_cap, t, h,
+                  self.num_experts, nsend, stream)
+        self.barrier()
+        _lib.call("moe_ep_expand", self.stage_buf.data_ptr(), self.stage_meta.data_ptr(),
+                  self.stage_count.data_ptr(), self.recv_buf.data_ptr(), n, self.rank,
+                  self.local_experts, self.tokens, self.recv_cap, h, stream)
+        return self.recv_buf[:nrecv]
+
     def fused_combine(self, map_te: torch.Tensor, probs: Optional[torch.Tensor],
                       deltas: torch.Tensor, nsend: int, tokens: int, hidden: int) -> torch.Tensor:
         """Weighted combine reading every result row from the rank that made it
@@ -384,21 +418,23 @@ class MoELayerEP:
                  tokens: Optional[int] = None, placement: Optional[torch.Tensor] = None):
         """transport "nccl": all_to_all_single of counts and rows; "peer": IPC-mapped
         buffers filled by copy-engine pushes; "fused": the dispatch and combine
-        kernels store / load rows in the peers' buffers directly. "peer" and
-        "fused" need `tokens`, the per-rank T. placement (int32 [E] permutation):
+        kernels store / load rows in the peers' buffers directly; "fused_dedup":
+        as "fused", with each token row sent once per destination rank and
+        expanded there. "peer" and "fused*" need `tokens`, the per-rank T. placement (int32 [E] permutation):
         slot c is model expert placement[c]; this rank holds the weights of
         slots [rank*E_loc, (rank+1)*E_loc) (e.g. from balanced_placement)."""
         self.placement = placement
         self.disp = EPDispatcher(num_experts, group)
         self.peer = None
-        self.fused = transport == "fused"
-        if transport in ("peer", "fused"):
+        self.fused = transport in ("fused", "fused_dedup")
+        if transport in ("peer", "fused", "fused_dedup"):
             if tokens is None:
                 raise ValueError(f"transport='{transport}' needs the per-rank token count")
             self.peer = EPPeerExchange(num_experts, tokens, local_weights.hidden, topk,
-                                       local_weights.w1.device, group, fused=self.fused)
+                                       local_weights.w1.device, group, fused=self.fused,
+                                       dedup=transport == "fused_dedup")
         elif transport != "nccl":
-            raise ValueError("transport must be 'nccl', 'peer' or 'fused'")
+            raise ValueError("transport must be 'nccl', 'peer', 'fused' or 'fused_dedup'")
         if local_weights.num_experts != self.disp.local_experts:
             raise ValueError("local weights do not match num_experts / world size")
         self.w = local_weights
@@ -457,7 +493,10 @@ class MoELayerEP:
         self._deltas = deltas  # read by both fused kernels of this forward
         nsend = int(sum(host[self.peer.rank]))
         nrecv = int(sum(lay.splits))
-        xr = self.peer.fused_dispatch(x, rim.map_te, deltas, nsend, nrecv)
+        if self.peer.dedup:
+            xr = self.peer.fused_dispatch_dedup(x, rim.map_te, deltas, nsend, nrecv)
+        else:
+            xr = self.peer.fused_dispatch(x, rim.map_te, deltas, nsend, nrecv)
         self._ev("a2a_dispatch")
         self.plan.from_splits(torch.tensor(lay.splits, dtype=torch.int32))
         hmid = ops.grouped_gemm(xr, self.w.w1, epilogue="swiglu", plan=self.plan)

@@ -41,6 +41,12 @@ UNIT = "tokens/s"
 FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
 
 
+def resolve_transport(transport: str, world: int) -> str:
+    if transport != "auto":
+        return transport
+    return "fused_dedup" if world <= 4 else "fused"
+
+
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -60,11 +66,13 @@ def parse_args():
     ap.add_argument("--placement", choices=["balanced", "contiguous"], default="balanced",
                     help="EP expert placement: load-balanced (E/G experts per GPU, chosen from "
                          "the routing of the benchmark's own logits) or contiguous id ranges")
-    ap.add_argument("--transport", choices=["fused", "fused_dedup", "peer", "nccl"],
-                    default="fused",
+    ap.add_argument("--transport", choices=["auto", "fused", "fused_dedup", "peer", "nccl"],
+                    default="auto",
                     help="EP row exchange: dispatch/combine kernels on peer memory (fused_dedup: "
                          "a token row crosses NVLink once per destination rank), IPC-mapped "
-                         "buffers + copy engines, or NCCL all-to-all")
+                         "buffers + copy engines, or NCCL all-to-all; auto = fused_dedup up to "
+                         "4 GPUs, fused at 8 (where tokens reach 6.8 of 8 ranks and the "
+                         "receiver's expansion copy outweighs the saved rows)")
     ap.add_argument("--workload", choices=["layer", "router_gemm", "backward", "wgrad"],
                     default="layer",
                     help="layer: the MoE expert-layer forward (the headline); router_gemm: the "
@@ -92,7 +100,8 @@ def config_dict(a, world):
             "tokens_per_gpu": a.tokens, "hidden": a.hidden, "experts": a.experts,
             "topk": a.topk, "ffn": a.ffn, "routing": a.routing,
             "parallelism": f"ep{world}" if world > 1 else "single",
-            **({"ep_transport": a.transport, "ep_placement": a.placement} if world > 1 else {}),
+            **({"ep_transport": resolve_transport(a.transport, world),
+                "ep_placement": a.placement} if world > 1 else {}),
             "l2": "no flush: every step streams >22 GB of expert weights and 0.25 GB of "
                   "activations, both larger than the 126 MB L2"}
 
@@ -557,7 +566,8 @@ def main():
             dist.all_reduce(load)
             placement = torch.tensor(balanced_placement(load.cpu().tolist(), world),
                                      dtype=torch.int32, device=dev)
-        layer = MoELayerEP(w, e, topk=k, expert_bias=bias, transport=a.transport, tokens=t,
+        layer = MoELayerEP(w, e, topk=k, expert_bias=bias,
+                           transport=resolve_transport(a.transport, world), tokens=t,
                            placement=placement)
         stage_names = ["start", "local_dispatch", "a2a_dispatch", "fc1", "fc2", "a2a_combine",
                        "combine"]

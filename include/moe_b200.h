@@ -263,6 +263,27 @@ int moe_ep_combine(const int64_t* peer_bases, const int64_t* expert_deltas, int3
                    const float* probs, void* out, int64_t T, int64_t H, int64_t E,
                    int64_t num_rows, moe_stream_t stream);
 
+/* Deduplicated dispatch (the token-once-per-rank scheme of the deep_ep       */
+/* FusedDispatch the reference names, kernel_cases/case22_ref_moe_permute_    */
+/* mask_kernel_true.py:3-6): a token row crosses NVLink once per destination  */
+/* rank. Rows for this rank's own experts go straight to                      */
+/* peer_bases[my_rank] at map[t,e] + expert_deltas[e]; for every other rank d  */
+/* the row is stored once into d's staging rows (peer_stage[d], block of T     */
+/* rows per source, slot from an atomic on peer_count[d][my_rank]) with a      */
+/* destination-row table (peer_meta[d], int32 [ranks*T, experts_per_rank],     */
+/* -1 = not routed). E <= 1024, H <= 8192.                                    */
+int moe_ep_dispatch_dedup(const void* x, const int64_t* row_id_map_te, const int64_t* peer_bases,
+                          const int64_t* expert_deltas, const int64_t* peer_stage,
+                          const int64_t* peer_meta, const int64_t* peer_count, int32_t ranks,
+                          int32_t my_rank, int32_t experts_per_rank, int64_t cap_rows, int64_t T,
+                          int64_t H, int64_t E, int64_t num_rows, moe_stream_t stream);
+/* After every rank's dedup dispatch (a barrier): copies each staged row of   */
+/* every other source to the receive rows its table lists (rows outside       */
+/* [0, cap_rows) skipped), then zeroes the counters for the next dispatch.    */
+int moe_ep_expand(const void* stage, const int32_t* meta, int32_t* count, void* recv,
+                  int32_t ranks, int32_t my_rank, int32_t experts_per_rank, int64_t rows_per_src,
+                  int64_t cap_rows, int64_t H, moe_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -93,7 +93,11 @@ def _worker(rank, world, port, routing, transport, q, placed=False):
                                                      (2, "zipf", "fused+placed"),
                                                      (4, "zipf", "fused+placed"),
                                                      (8, "zipf", "fused+placed"),
-                                                     (8, "uniform", "nccl")])
+                                                     (8, "uniform", "nccl"),
+                                                     (2, "zipf", "fused_dedup"),
+                                                     (4, "uniform", "fused_dedup"),
+                                                     (4, "zipf", "fused_dedup+placed"),
+                                                     (8, "zipf", "fused_dedup+placed")])
 def test_ep_equals_single_gpu(world, routing, transport):
     if not torch.cuda.is_available():
         pytest.fail("GPU test selected but no CUDA device is visible")
