@@ -551,6 +551,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (!walker.locate(t, tile)) break;
         int row0, b0;
         coords(tile, row0, b0);
+        const int wrow0 = p.b_mn ? p.widx[tile.g] * p.k_rows : 0;  // first reduction row of w[g]
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) {
             ok = false;
@@ -562,7 +563,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (leader) mbar_arrive_expect_tx(full_bar(stage), tx);
           tma_load_2d_pair(sa, &tmap_a, kb * BK, row0, leader_full, pol_a);
           if (p.b_mn) {
-            const int wrow = p.widx[tile.g] * p.k_rows + kb * BK;
+            const int wrow = wrow0 + kb * BK;
 #pragma unroll
             for (int j = 0; j < 2; ++j)  // this CTA's 128 columns as two 64-column boxes
               tma_load_2d_pair(sb + j * 8192u, &tmap_b, b0 + j * 64, wrow, leader_full, pol_b);
