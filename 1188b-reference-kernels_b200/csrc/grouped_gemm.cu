@@ -8,16 +8,28 @@
 // of torch.mm over uniform splits (kernel_cases/case03_moe_grouped_gemm_fc1_fwd
 // .py:57-64, case04_moe_grouped_gemm_fc2_fwd.py:57-64); here the groups are
 // ragged and described by a device-side table, so no host sync is needed.
+// moe_grouped_gemm_nn takes W as [num_w, K, N] instead (out = x @ W[g], the
+// dgrad of case07/08 with the forward weight as stored): its B tiles are
+// staged MN-major and described to tcgen05 as such.
+// Epilogues: bf16 out, SwiGLU (fc1: gate|up -> silu(gate)*up), or the fp32
+// accumulator (the router logits GEMM of case38 with one group).
 //
-// Kernel structure (one persistent CTA per SM, 192 threads):
+// Two kernels share the group table, the raster order and the epilogues:
+//   grouped_gemm_pair_kernel (default): CTA pairs (cta_group::2, clusters of
+//     2) on 256-row tiles, epilogue through 64B-swizzled shared buffers and
+//     TMA tile stores; it takes every group's whole 256-row tiles.
+//   grouped_gemm_kernel: one CTA per SM on 128-row tiles; it takes each
+//     group's remainder (< 256 rows) after the pair kernel, or everything
+//     when CTA pairs cannot be scheduled.
+// Single-CTA kernel structure (one persistent CTA per SM, 192 threads):
 //   warp 0      TMA producer: 128x64 A tile + 2 x 128x64 B half-tiles per
 //               stage, 128-byte swizzle, 4-stage mbarrier ring.
 //   warp 1      TMEM owner (512 columns = two 128x256 fp32 accumulators) and
 //               single-thread tcgen05.mma issuer (M=128, N=256, K=16).
 //   warps 2-5   epilogue: tcgen05.ld (32 lanes x 32 columns), bf16 convert
-//               (or SwiGLU for fc1), predicated 16-byte global stores.
+//               (or SwiGLU for fc1, or fp32), predicated 16-byte global stores.
 // Two accumulators let the epilogue of tile i overlap the mainloop of i+1.
-// Tiles are walked group by group; inside a group, super-rows of 16 M-tiles
+// Tiles are walked group by group; inside a group, super-rows of M-tiles
 // sweep all N-tiles so that concurrently running CTAs share both the weight
 // slab and the activation rows in L2.
 //

@@ -116,6 +116,14 @@ class MoELayer:
     __call__ = forward
 
 
+def moe_layer_fwd(x: torch.Tensor, logits: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,
+                  topk: int = 8, renorm: bool = True,
+                  expert_bias: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Functional form of MoELayer: one expert-layer forward, x [T,H] bf16,
+    logits [T,E] fp32, w1 [E,2F,H], w2 [E,H,F] bf16 -> [T,H] bf16."""
+    return MoELayer(MoEWeights(w1, w2), topk=topk, renorm=renorm, expert_bias=expert_bias)(x, logits)
+
+
 class HostPipeline:
     """Runs layer steps whose inputs and outputs live in pinned host memory.
 

@@ -390,6 +390,15 @@ def grouped_gemm(x: torch.Tensor, w: torch.Tensor,
     return out
 
 
+def unpermute_weighted(pin: torch.Tensor, row_id_map: torch.Tensor,
+                       probs: torch.Tensor) -> torch.Tensor:
+    """Prob-weighted combine: out[t] = bf16(sum over e ascending of
+    probs[t,e] * fp32(pin[row_id_map[e,t]])), probs dense [T,E] fp32 — the
+    unweighted unpermute of kernel_cases/case15_moe_unpermute_mask_fwd.py:
+    58-64 with each source row scaled by its gate (no reference code)."""
+    return unpermute(pin, row_id_map, probs, probs_mode="dense")
+
+
 def permute_backward(grad_permuted: torch.Tensor, row_id_map: torch.Tensor,
                      permuted_probs_grad: Optional[torch.Tensor] = None,
                      return_acc: bool = False):

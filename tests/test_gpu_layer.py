@@ -113,3 +113,17 @@ def test_layer_from_hidden_with_router_gemm(cuda_dev):
     assert torch.equal(out, layer(x, lg))
     with pytest.raises(ValueError):
         layer(x)
+
+
+def test_functional_layer_equals_module(cuda_dev):
+    """moe_layer_fwd (functional form) == MoELayer, bit for bit."""
+    import moe_b200
+    t, h, e, f, k = 256, 512, 16, 128, 4
+    g = torch.Generator().manual_seed(8)
+    x = torch.randn(t, h, generator=g).to(torch.bfloat16).to(cuda_dev)
+    lg = torch.randn(t, e, generator=g).to(cuda_dev)
+    w1 = (torch.randn(e, 2 * f, h, generator=g) * 0.02).to(torch.bfloat16).to(cuda_dev)
+    w2 = (torch.randn(e, h, f, generator=g) * 0.02).to(torch.bfloat16).to(cuda_dev)
+    a = moe_b200.moe_layer_fwd(x, lg, w1, w2, topk=k)
+    b = moe_b200.MoELayer(moe_b200.MoEWeights(w1, w2), topk=k)(x, lg)
+    assert torch.equal(a, b)

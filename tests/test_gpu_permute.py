@@ -158,6 +158,10 @@ def test_weighted_combine_golden(cuda_dev, golden):
                                   return_acc=True)
     np.testing.assert_array_equal(acc.cpu().numpy(), z["w_acc"])
     np.testing.assert_array_equal(u16(out), z["w_out"])
+    w = moe_b200.unpermute_weighted(from_u16(z["w_pin"], cuda_dev),
+                                    torch.from_numpy(z["w_map_et"]).to(cuda_dev),
+                                    torch.from_numpy(z["w_probs"]).to(cuda_dev))
+    np.testing.assert_array_equal(u16(w), z["w_out"])
 
 
 @pytest.mark.parametrize("t,h,e,k,mode", [(8192, 7168, 256, 8, "dense"),
