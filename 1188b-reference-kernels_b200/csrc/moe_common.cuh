@@ -368,6 +368,32 @@ MOE_DEVICE void umma_commit_pair(uint32_t bar, uint16_t cta_mask) {
       : "memory");
 }
 
+// ---------------------------------------------------------------------------
+// Top-k ranking keys (shared by the router kernels).
+// ---------------------------------------------------------------------------
+// Ranking key of (value, column): larger key = ranked first. The high word
+// maps floats to an unsigned order (NaN above everything, -0.0 == +0.0), the
+// low word is the inverted column so equal values rank the lower column first.
+// 0 is never a real key (the smallest real high word is that of -inf).
+MOE_DEVICE uint64_t rank_key(float v, int c) {
+  uint32_t hi;
+  if (isnan(v)) {
+    hi = 0xFFFFFFFFu;
+  } else {
+    const uint32_t u = __float_as_uint(v + 0.0f);  // -0.0 -> +0.0
+    hi = (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+  }
+  return (static_cast<uint64_t>(hi) << 32) | static_cast<uint32_t>(0xFFFFFFFFu - c);
+}
+MOE_DEVICE float key_value(uint64_t key) {
+  const uint32_t hi = static_cast<uint32_t>(key >> 32);
+  if (hi == 0xFFFFFFFFu) return __uint_as_float(0x7FC00000u);
+  return __uint_as_float((hi & 0x80000000u) ? (hi & 0x7FFFFFFFu) : ~hi);
+}
+MOE_DEVICE int key_column(uint64_t key) {
+  return static_cast<int>(0xFFFFFFFFu - static_cast<uint32_t>(key & 0xFFFFFFFFull));
+}
+
 MOE_DEVICE int warp_id() { return static_cast<int>(threadIdx.x >> 5); }
 MOE_DEVICE int lane_id() { return static_cast<int>(threadIdx.x & 31); }
 

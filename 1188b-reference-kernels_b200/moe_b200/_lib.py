@@ -43,6 +43,9 @@ _SIGNATURES = {
                         c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
     "moe_router_topk_placed": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int32, c_int32,
                                c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
+    "moe_router_gemm_topk": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int32,
+                             c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                             c_void_p, c_void_p],
     "moe_row_id_map_workspace_size": [c_int64, c_int64, POINTER(c_size_t)],
     "moe_row_id_map": [c_void_p, c_int64, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                        c_void_p, c_void_p, c_size_t, c_void_p],
@@ -93,6 +96,7 @@ EXPORTED = tuple(_SIGNATURES)
 # tiles, then the single-CTA kernel on the group remainders (one launch only
 # when CTA pairs are disabled with MOE_GEMM_PAIR=0 or MOE_GEMM_SPLIT=0).
 _LAUNCHES = {"moe_topk_f32": 1, "moe_router_topk": 1, "moe_router_topk_placed": 1,
+             "moe_router_gemm_topk": 1,
              "moe_row_id_map": 3,
              "moe_row_id_map_static_scratch": 3,
              "moe_permute_mask_map": 1, "moe_permute_mask_map_trans": 1, "moe_unpermute_mask": 1,

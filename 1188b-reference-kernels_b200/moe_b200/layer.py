@@ -82,21 +82,30 @@ class MoELayer:
     def forward(self, x: torch.Tensor, logits: Optional[torch.Tensor] = None,
                 return_intermediates: bool = False,
                 router_weight: Optional[torch.Tensor] = None):
-        """logits [T,E] fp32, or router_weight [E,H] bf16 to compute them first
-        with the router gate GEMM (ops.router_logits)."""
+        """logits [T,E] fp32, or router_weight [E,H] bf16: then the router gate
+        GEMM and the router run as one kernel (ops.router_gemm_topk) where it
+        covers the shape, else as ops.router_logits + ops.router_topk."""
         t, h = x.shape
         e = self.w.num_experts
+        if h != self.w.hidden:
+            raise ValueError(f"x hidden {h} != weights hidden {self.w.hidden}")
         if logits is None:
             if router_weight is None:
                 raise ValueError("pass logits or router_weight")
-            logits = ops.router_logits(x, router_weight)
-        if logits.shape != (t, e):
+            if router_weight.shape != (e, h):
+                raise ValueError(f"router_weight must be [{e},{h}]")
+        elif logits.shape != (t, e):
             raise ValueError(f"logits must be [{t},{e}]")
-        if h != self.w.hidden:
-            raise ValueError(f"x hidden {h} != weights hidden {self.w.hidden}")
         self._ev("start")
-        r = ops.router_topk(logits, self.k, "softmax", self.renorm, self.bias, outputs="maps",
-                            placement=self.placement)
+        if logits is None and self.placement is None and ops.router_gemm_fusable(
+                x, router_weight, self.k):
+            r = ops.router_gemm_topk(x, router_weight, self.k, "softmax", self.renorm, self.bias,
+                                     outputs="maps")
+        else:
+            if logits is None:
+                logits = ops.router_logits(x, router_weight)
+            r = ops.router_topk(logits, self.k, "softmax", self.renorm, self.bias, outputs="maps",
+                                placement=self.placement)
         rim = ops.row_id_map(r.routing_map, align=1, want_et=False)
         self._ev("routing")
         rows = t * self.k

@@ -510,6 +510,79 @@ def router_logits(x: torch.Tensor, weight: torch.Tensor,
 # on the row count, so repeated calls skip the planning launch.
 _ROUTER_PLANS: dict = {}
 
+# Device error words of router_gemm_topk, one zeroed int32 per device.
+_ROUTER_ERR: dict = {}
+
+
+def _router_err(dev: torch.device) -> torch.Tensor:
+    e = _ROUTER_ERR.get(dev)
+    if e is None:
+        e = torch.zeros(1, dtype=torch.int32, device=dev)
+        _ROUTER_ERR[dev] = e
+    return e
+
+
+def router_device_error(device) -> int:
+    """Error code left by router_gemm_topk on this device (0: none). Syncs."""
+    e = _ROUTER_ERR.get(torch.device(device))
+    return 0 if e is None else int(e.item())
+
+
+def router_gemm_fusable(x: torch.Tensor, weight: torch.Tensor, k: int) -> bool:
+    """Whether router_gemm_topk covers this shape (E a multiple of 32 up to
+    512, H a multiple of 8, k <= min(E, 16))."""
+    e, h = weight.shape[0], weight.shape[1]
+    return e % 32 == 0 and 32 <= e <= 512 and h % 8 == 0 and 1 <= k <= min(e, 16)
+
+
+def router_gemm_topk(x: torch.Tensor, weight: torch.Tensor, k: int, score: str = "softmax",
+                     renorm: bool = True, bias: Optional[torch.Tensor] = None,
+                     outputs: str = "maps", return_logits: bool = False):
+    """Router gate GEMM and router in one kernel: logits = x @ weight^T (fp32
+    accumulation on the tensor cores), then router_topk(logits, k, score,
+    renorm, bias) without the logits round trip through HBM; the routing
+    outputs are bit-identical to router_topk on the same logits.
+
+    Replaces kernel_cases/case38_ref_musa_asm_bf16_ssgemm_nt_320x256.py:51-59
+    followed by the softmax/top-k router. x [T,H] bf16, weight [E,H] bf16.
+    outputs="maps" (routing map + probs), "all" (+ topk_vals/topk_idx) or
+    "none" (only the logits, which then must be requested).
+    Returns RouterOutput, or (RouterOutput, logits) with return_logits.
+    """
+    for n_, t_ in (("x", x), ("weight", weight)):
+        _need_cuda(n_, t_)
+        _need_dtype(n_, t_, torch.bfloat16)
+    if x.dim() != 2 or weight.dim() != 2 or x.shape[1] != weight.shape[1]:
+        raise ValueError(f"shapes x {tuple(x.shape)} weight {tuple(weight.shape)}")
+    if score not in ("softmax", "logits"):
+        raise ValueError("score must be 'softmax' or 'logits'")
+    if outputs not in ("maps", "all", "none"):
+        raise ValueError("outputs must be 'maps', 'all' or 'none'")
+    if outputs == "none" and not return_logits:
+        raise ValueError("outputs='none' needs return_logits=True")
+    xc, wc = x.contiguous(), weight.contiguous()
+    t, e = xc.shape[0], wc.shape[0]
+    dev = xc.device
+    if bias is not None:
+        _need_cuda("bias", bias)
+        _need_dtype("bias", bias, torch.float32)
+        if bias.shape != (e,):
+            raise ValueError(f"bias must be [{e}]")
+        bias = bias.contiguous()
+    tv = ti = rmap = probs = None
+    if outputs == "all":
+        tv = torch.empty((t, k), dtype=torch.float32, device=dev)
+        ti = torch.empty((t, k), dtype=torch.int64, device=dev)
+    if outputs in ("all", "maps"):
+        rmap = torch.empty((t, e), dtype=torch.bool, device=dev)
+        probs = torch.empty((t, e), dtype=torch.float32, device=dev)
+    logits = torch.empty((t, e), dtype=torch.float32, device=dev) if return_logits else None
+    _lib.call("moe_router_gemm_topk", _p(xc), _p(wc), _p(bias), t, xc.shape[1], e, int(k),
+              1 if score == "softmax" else 0, 1 if renorm else 0, _p(logits), _p(tv), _p(ti),
+              _p(rmap), _p(probs), _p(_router_err(dev)), _stream(dev))
+    r = RouterOutput(tv, ti, rmap, probs)
+    return (r, logits) if return_logits else r
+
 
 def swiglu(y: torch.Tensor) -> torch.Tensor:
     """h = silu(y[:, :F]) * y[:, F:] for y [M,2F] bf16 (gate|up order)."""

@@ -337,6 +337,29 @@ def run_router_gemm(a):
     sampler.mark(wall0, time.time())
     launches = _lib.launch_count - launches0
     t = ev[0].elapsed_time(ev[1]) / 1e3 / a.steps
+
+    def timed(fn):
+        for _ in range(3):
+            fn()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(a.steps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / a.steps * 1e3  # us
+
+    # The whole router (gate GEMM + softmax/top-8/renorm -> routing map + probs):
+    # one fused kernel vs the GEMM followed by the standalone router kernel.
+    fused = {}
+    if n % 32 == 0 and n <= 512:
+        fused["router_us"] = round(timed(lambda: moe_b200.router_gemm_topk(
+            x, w, 8, "softmax", True, None, outputs="maps")), 2)
+        fused["gemm_logits_only_us"] = round(timed(lambda: moe_b200.router_gemm_topk(
+            x, w, 8, outputs="none", return_logits=True)), 2)
+        fused["unfused_router_us"] = round(timed(lambda: moe_b200.router_topk(
+            moe_b200.router_logits(x, w, out=out), 8, "softmax", True, outputs="maps")), 2)
+        fused["device_error"] = moe_b200.router_device_error(dev)
     clocks = sampler.stop()
     peaks, peak_kind = load_peaks()
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
@@ -352,7 +375,8 @@ def run_router_gemm(a):
             "hbm": {"achieved_gbs": round(nbytes / t / 1e9, 1), "peak_gbs": hbm,
                     "frac": round(nbytes / t / 1e9 / hbm, 4), "bytes": nbytes},
             "peak_kind": f"bf16 burst, of {peak_kind}",
-            "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clocks}
+            "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clocks,
+            "fused_router": fused}
     print(json.dumps(line), flush=True)
 
 

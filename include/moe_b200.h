@@ -78,6 +78,25 @@ int moe_router_topk_placed(const float* logits, const float* bias, const int32_t
                            float* topk_vals, int64_t* topk_idx, uint8_t* routing_map,
                            float* probs, moe_stream_t stream);
 
+/* f1  Router gate GEMM fused with the router above, one kernel:             */
+/*   logits = x @ w^T (x [T,H] bf16, w [E,H] bf16, fp32 accumulation on the */
+/*   tensor cores), then exactly moe_router_topk on those logits (same       */
+/*   selection, gate formula and summation order, so the same bits).         */
+/* Replaces kernel_cases/case38_ref_musa_asm_bf16_ssgemm_nt_320x256.py:51-59 */
+/* (the router gate GEMM) followed by moe_router_topk, without the [T,E]     */
+/* fp32 logits round trip through HBM.                                       */
+/* H % 8 == 0; E a multiple of 32 in [32, 512]; 1 <= k <= min(E, 16).        */
+/* Outputs are nullable: logits [T,E] fp32 (the unbiased GEMM result),       */
+/* topk_vals/topk_idx [T,k], routing_map [T,E] uint8, probs [T,E] fp32.      */
+/* With only logits requested this is the plain router GEMM. x, w, logits,   */
+/* routing_map and probs must be 16-byte aligned.                            */
+/* device_error: device int32, zero before the first call; a kernel whose    */
+/* bounded wait expired stores a nonzero code there (never cleared here).    */
+int moe_router_gemm_topk(const void* x, const void* w, const float* bias, int64_t T, int64_t H,
+                         int64_t E, int32_t k, int32_t score_mode, int32_t renorm, float* logits,
+                         float* topk_vals, int64_t* topk_idx, uint8_t* routing_map, float* probs,
+                         int32_t* device_error, moe_stream_t stream);
+
 /* ------------------------------------------------------------------------ */
 /* a3  routing_map [T,E] bool -> row_id_map, expert-major destinations:      */
 /*   row[t,e] = base[e] + #{t' <= t : map[t',e]} - 1 if map[t,e] else -1     */

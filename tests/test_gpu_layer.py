@@ -95,9 +95,9 @@ def test_layer_with_placement(cuda_dev):
 
 
 def test_layer_from_hidden_with_router_gemm(cuda_dev):
-    """router_weight path: logits from the router gate GEMM (fp32, case38 form),
-    then the same layer; equals feeding those logits in, bit for bit, and the
-    logits match the fp32 oracle."""
+    """router_weight path: the fused router (gate GEMM + top-k in one kernel)
+    then the same layer; equals feeding its logits in, bit for bit, and the
+    logits match the fp32 oracle and the grouped-GEMM router logits."""
     import moe_b200
     t, h, e, f, k = 512, 1024, 64, 256, 8
     g = torch.Generator().manual_seed(5)
@@ -107,9 +107,10 @@ def test_layer_from_hidden_with_router_gemm(cuda_dev):
     w2 = (torch.randn(e, h, f, generator=g) * 0.02).to(torch.bfloat16).to(cuda_dev)
     layer = moe_b200.MoELayer(moe_b200.MoEWeights(w1, w2), topk=k)
     out = layer(x, router_weight=rw)
-    lg = moe_b200.router_logits(x, rw)
-    np.testing.assert_allclose(lg.cpu().numpy(), orc.router_logits(u16(x), u16(rw)),
-                               rtol=1e-5, atol=1e-4)
+    _, lg = moe_b200.router_gemm_topk(x, rw, k, outputs="none", return_logits=True)
+    for logits in (lg, moe_b200.router_logits(x, rw)):
+        np.testing.assert_allclose(logits.cpu().numpy(), orc.router_logits(u16(x), u16(rw)),
+                                   rtol=1e-5, atol=1e-4)
     assert torch.equal(out, layer(x, lg))
     with pytest.raises(ValueError):
         layer(x)
