@@ -13,23 +13,27 @@
 // top-k with the case23 ordering, renormalisation), in one kernel, so the
 // [T,E] fp32 logits never travel through HBM unless the caller asks for them.
 //
-// One CTA owns 128 tokens and ALL E experts of them: E <= 512 fp32 columns of
-// TMEM (two accumulators when E <= 256, so the epilogue of one tile overlaps
-// the mainloop of the next). Warp 0 is the TMA producer (128 x 64 x-tile plus
-// E x 64 W-tile per stage, 128-byte swizzle, as many stages as fit), warp 1
-// allocates TMEM and issues tcgen05.mma (M=128, N = E in pieces of <= 256,
-// K=16), warps 2-5 are the epilogue: each thread owns one token's row of the
-// accumulator and reads it 32 columns at a time (tcgen05.ld 32x32b), keeping a
-// register-resident sorted top-k. The selection, the softmax maximum, the
-// normalisers (including their summation order) and the gate formula are
-// those of the warp-per-row router kernel in routing.cu, so both produce the
-// same bits from the same logits. Dense outputs are zero-filled by each warp
-// with coalesced 16-byte stores over its 32 contiguous rows, then each thread
-// writes its k selected entries.
+// A CTA pair (cluster of 2, tcgen05 cta_group::2) owns 256 tokens and ALL E
+// experts of them: each CTA stages its own 128 x-rows and half of W's rows per
+// k-block (so W crosses L2 once per pair, not once per CTA), the leader issues
+// M=256 MMAs (N = E in pieces of <= 256, K=16) and each CTA's TMEM receives
+// its 128 rows x E fp32 columns (two accumulators when E <= 256, so the
+// epilogue of one tile overlaps the mainloop of the next). Warp 0 is the TMA
+// producer, warp 1 owns TMEM and (in the leader) issues the MMAs, warps 2-17
+// are the epilogue: four warps per TMEM lane quadrant, each reading a quarter
+// of the columns of its 32 rows (tcgen05.ld 32x32b, one row per thread) and
+// keeping a register-resident sorted top-k of them. The quarters meet on a
+// per-quadrant mbarrier; the first merges the other three lists (keys are
+// unique, so the merged selection is exact), forms the normalisers and writes
+// the outputs. Selection, softmax maximum, normalisers (with their summation
+// order) and the gate formula are those of the warp-per-row router kernel in
+// routing.cu, so both produce the same bits from the same logits. Dense
+// outputs are zero-filled by the quadrant's warps with coalesced 16-byte
+// stores over its 32 contiguous rows before the selected entries are placed.
 //
 // Every wait is bounded (2 s); on timeout the kernel records an error code in
-// the caller's device word, drains its own copies and MMAs, frees TMEM and
-// returns.
+// the caller's device word, drains its own copies and MMAs, frees TMEM after a
+// cluster barrier and returns.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 
@@ -49,18 +53,28 @@ int make_tmap_box(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t oute
 
 namespace rg {
 
-constexpr int BM = 128;
+constexpr int BM = 128;            // token rows per CTA; a pair covers 256
+constexpr int kPairRows = 256;
 constexpr int BK = 64;
-constexpr int kThreads = 192;
+constexpr int kEpiWarps = 16;      // 4 per TMEM lane quadrant (column quarters)
+constexpr int kThreads = 64 + 32 * kEpiWarps;
 constexpr int kMaxE = 512;
 constexpr int kMaxStages = 8;
-constexpr uint32_t kABytes = BM * BK * 2;  // 16 KB
+constexpr uint32_t kABytes = BM * BK * 2;  // 16 KB: this CTA's x rows
 constexpr size_t kSmemMax = 232448;       // dynamic shared memory per block on sm_100
 constexpr size_t kSmemTail = 512;         // barriers, TMEM slot, abort flag
 
 constexpr int kErrTimeoutProducer = 1;
 constexpr int kErrTimeoutMma = 2;
 constexpr int kErrTimeoutEpilogue = 3;
+
+// Merge area: quarters 1-3 hand their top-k lists (key, exact score) and
+// maxima to quarter 0; [quarter-1][slot][row] so a warp's accesses are
+// contiguous. One buffer: a quarter writes the next tile's list only after
+// quarter 0 has released this one (per-quadrant "free" barrier).
+__host__ __device__ inline size_t merge_bytes(int k) {
+  return static_cast<size_t>(3 * k * BM) * (8 + 4) + static_cast<size_t>(3 * BM) * 4;
+}
 
 struct Params {
   const float* bias;  // [E] or null
@@ -77,12 +91,12 @@ struct Params {
   int renorm;
   int route;   // 0: logits only (no selection work)
   int num_kb;
-  int m_tiles;
+  int m_tiles;      // pair tiles of 256 rows
   int stages;
-  int b_box_rows;
-  int b_boxes;
-  int acc_stride;  // TMEM columns between the two accumulators
-  int n_acc;       // 1 or 2
+  int n_pieces;     // MMAs per k-slice (N = piece_n each)
+  int piece_n;      // columns per piece; each CTA stages piece_n / 2 W rows of it
+  int acc_stride;   // TMEM columns between the two accumulators
+  int n_acc;        // 1 or 2
   uint32_t tmem_cols;
 };
 
@@ -129,18 +143,31 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
   uint8_t* base_ptr = smem_raw + (base - raw_addr);
-  const uint32_t stage_bytes = kABytes + static_cast<uint32_t>(p.E) * (BK * 2);
+  const int E = p.E;
+  const uint32_t half_rows = static_cast<uint32_t>(p.piece_n / 2);
+  const uint32_t stage_bytes = kABytes + static_cast<uint32_t>(E / 2) * (BK * 2);
   const int S = p.stages;
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base_ptr + static_cast<size_t>(S) * stage_bytes);
+  const int K = p.k;
+  uint8_t* merge_ptr = base_ptr + static_cast<size_t>(S) * stage_bytes;
+  uint64_t* m_keys = reinterpret_cast<uint64_t*>(merge_ptr);  // [3][K][BM]
+  float* m_vals = reinterpret_cast<float*>(m_keys + 3 * K * BM);  // [3][K][BM]
+  float* m_max = m_vals + 3 * K * BM;                             // [3][BM]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(merge_ptr + ((merge_bytes(K) + 7) & ~size_t(7)));
   const uint32_t bar0 = smem_u32(bars);
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
   auto empty_bar = [&](int s) { return bar0 + 8u * (kMaxStages + s); };
   auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * kMaxStages + a); };
   auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * kMaxStages + 2 + a); };
-  const uint32_t drain_bar = bar0 + 8u * (2 * kMaxStages + 4);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 5);
+  auto quad_bar = [&](int q) { return bar0 + 8u * (2 * kMaxStages + 4 + q); };
+  auto free_bar = [&](int q) { return bar0 + 8u * (2 * kMaxStages + 8 + q); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * kMaxStages + 12);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kMaxStages + 13);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const int cid = static_cast<int>(cluster_id_x());
+  const int ncl = static_cast<int>(num_clusters_x());
   const int warp = warp_id();
   const int lane = lane_id();
 
@@ -151,7 +178,11 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(tfull_bar(a), 1);
-      mbar_init(tempty_bar(a), 4);
+      mbar_init(tempty_bar(a), 2 * kEpiWarps);  // every epilogue warp of both CTAs
+    }
+    for (int q = 0; q < 4; ++q) {
+      mbar_init(quad_bar(q), 4);
+      mbar_init(free_bar(q), 1);
     }
     mbar_init(drain_bar, 1);
     *abort_flag = 0;
@@ -162,27 +193,30 @@ __global__ void __launch_bounds__(kThreads, 1)
     tma_prefetch_desc(&tmap_w);
   }
   if (warp == 1) {
-    tmem_alloc(smem_u32(tmem_slot), p.tmem_cols);
-    tmem_relinquish();
+    tmem_alloc_pair(smem_u32(tmem_slot), p.tmem_cols);
+    tmem_relinquish_pair();
   }
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised before any remote use
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
   if (warp == 0) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------------ producer (both CTAs)
     if (lane == 0) {
-      const uint64_t pol_x = l2_policy_evict_first();   // every x row is read once
-      const uint64_t pol_w = l2_policy_evict_last();    // W is read by every CTA
+      const uint64_t pol_x = l2_policy_evict_first();  // every x row is read once
+      const uint64_t pol_w = l2_policy_evict_last();   // W is read by every pair
       int stage = 0;
       uint32_t phase = 0;
       int issued[kMaxStages];
 #pragma unroll
       for (int s = 0; s < kMaxStages; ++s) issued[s] = -1;
       bool ok = true;
-      for (int t = blockIdx.x; ok && t < p.m_tiles; t += gridDim.x) {
-        const int row0 = t * BM;
+      // Both CTAs' bytes per stage land on the leader's full barrier.
+      const uint32_t tx = 2u * stage_bytes;
+      for (int t = cid; ok && t < p.m_tiles; t += ncl) {
+        const int row0 = t * kPairRows + static_cast<int>(rank) * BM;
         for (int kb = 0; kb < p.num_kb; ++kb) {
           if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) {
             ok = false;
@@ -190,11 +224,13 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
           const uint32_t sa = base + static_cast<uint32_t>(stage) * stage_bytes;
           const uint32_t sb = sa + kABytes;
-          mbar_arrive_expect_tx(full_bar(stage), stage_bytes);
-          tma_load_2d(sa, &tmap_x, kb * BK, row0, full_bar(stage), pol_x);
-          for (int j = 0; j < p.b_boxes; ++j)
-            tma_load_2d(sb + static_cast<uint32_t>(j * p.b_box_rows) * (BK * 2), &tmap_w, kb * BK,
-                        j * p.b_box_rows, full_bar(stage), pol_w);
+          const uint32_t leader_full = map_to_rank(full_bar(stage), 0);
+          if (leader) mbar_arrive_expect_tx(full_bar(stage), tx);
+          tma_load_2d_pair(sa, &tmap_x, kb * BK, row0, leader_full, pol_x);
+          for (int pc = 0; pc < p.n_pieces; ++pc)  // this CTA's half of each piece's W rows
+            tma_load_2d_pair(sb + static_cast<uint32_t>(pc) * half_rows * (BK * 2), &tmap_w,
+                             kb * BK, pc * p.piece_n + static_cast<int>(rank * half_rows),
+                             leader_full, pol_w);
           issued[stage] = static_cast<int>(phase);
           if (++stage == S) {
             stage = 0;
@@ -202,34 +238,45 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
-      if (!ok) {
-        raise_abort(abort_flag, p.err, kErrTimeoutProducer);
+      if (ok) {
+        // The pair's MMA releases every stage with a commit that lands in this
+        // CTA's shared memory; wait for the last ones before exiting.
         for (int s = 0; s < S; ++s)
-          if (issued[s] >= 0) wait_drain(full_bar(s), static_cast<uint32_t>(issued[s]));
+          if (issued[s] >= 0) wait_drain(empty_bar(s), static_cast<uint32_t>(issued[s]));
+      } else {
+        raise_abort(abort_flag, p.err, kErrTimeoutProducer);
+        if (leader) {
+          for (int s = 0; s < S; ++s)
+            if (issued[s] >= 0) wait_drain(full_bar(s), static_cast<uint32_t>(issued[s]));
+        } else {
+          // Copies count on the leader's barrier; give them a bounded time to land.
+          const unsigned long long t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 200000ull) {
+          }
+        }
       }
     }
     __syncwarp();
   } else if (warp == 1) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      const int n_pieces = (p.E + 255) / 256;
+    // ------------------------------------------------------------ MMA issuer (leader)
+    if (leader && lane == 0) {
+      const uint32_t idesc = umma_idesc_bf16_f32(kPairRows, p.piece_n);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
       bool issued_any = false;
-      for (int t = blockIdx.x; ok && t < p.m_tiles; t += gridDim.x) {
+      for (int t = cid; ok && t < p.m_tiles; t += ncl) {
         const int acc = p.n_acc == 2 ? (it & 1) : 0;
-        const uint32_t aph =
-            static_cast<uint32_t>(p.n_acc == 2 ? ((it >> 1) & 1) : (it & 1));
-        if (!mbar_wait(tempty_bar(acc), aph ^ 1u, abort_flag)) {
+        const uint32_t aph = static_cast<uint32_t>(p.n_acc == 2 ? ((it >> 1) & 1) : (it & 1));
+        if (!mbar_wait_cluster(tempty_bar(acc), aph ^ 1u, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * p.acc_stride);
         for (int kb = 0; kb < p.num_kb; ++kb) {
-          if (!mbar_wait(full_bar(stage), phase, abort_flag)) {
+          if (!mbar_wait_cluster(full_bar(stage), phase, abort_flag)) {
             ok = false;
             break;
           }
@@ -237,51 +284,61 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sa = base + static_cast<uint32_t>(stage) * stage_bytes;
           const uint32_t sb = sa + kABytes;
           const uint64_t ad = umma_desc_k_sw128(sa);
-          for (int pc = 0; pc < n_pieces; ++pc) {
-            const int n0 = pc * 256;
-            const int nw = min(256, p.E - n0);
-            const uint32_t idesc = umma_idesc_bf16_f32(BM, nw);
-            const uint64_t bd = umma_desc_k_sw128(sb + static_cast<uint32_t>(n0) * (BK * 2));
+          for (int pc = 0; pc < p.n_pieces; ++pc) {
+            const uint64_t bd =
+                umma_desc_k_sw128(sb + static_cast<uint32_t>(pc) * half_rows * (BK * 2));
+            const uint32_t dcol = d_tmem + static_cast<uint32_t>(pc * p.piece_n);
 #pragma unroll
             for (int k = 0; k < BK / 16; ++k)
-              umma_bf16(d_tmem + static_cast<uint32_t>(n0), ad + 2ull * k, bd + 2ull * k, idesc,
-                        (kb | k) != 0 ? 1u : 0u);
+              umma_bf16_pair(dcol, ad + 2ull * k, bd + 2ull * k, idesc, (kb | k) != 0 ? 1u : 0u);
           }
           issued_any = true;
-          umma_commit(empty_bar(stage));
+          umma_commit_pair(empty_bar(stage), 0x3);
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
           }
         }
         if (!ok) break;
-        umma_commit(tfull_bar(acc));
+        umma_commit_pair(tfull_bar(acc), 0x3);
         ++it;
       }
       if (!ok) {
         raise_abort(abort_flag, p.err, kErrTimeoutMma);
         if (issued_any) {
-          umma_commit(drain_bar);
+          umma_commit_pair(drain_bar, 0x1);
           wait_drain(drain_bar, 0);
         }
       }
     }
     __syncwarp();
   } else {
-    // ------------------------------------------------------------ epilogue
-    const int quad = warp & 3;  // TMEM lanes 32*quad .. 32*quad+31
-    const int E = p.E;
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quad = warp & 3;                 // TMEM lanes 32*quad .. 32*quad+31
+    const int quarter = (warp - 2) >> 2;       // column quarter of this warp
+    const int r_in_cta = quad * 32 + lane;
+    const int nch = E / 32;
+    const int c_begin = (quarter * nch) / 4;
+    const int c_end = ((quarter + 1) * nch) / 4;
+    const uint32_t leader_tempty0 = map_to_rank(tempty_bar(0), 0);
+    const uint32_t leader_tempty1 = map_to_rank(tempty_bar(1), 0);
+    const bool full_sum = p.route && p.mode == 1 && !p.renorm;  // needs every column in order
     int it = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < p.m_tiles; t += gridDim.x) {
+    auto release_acc = [&](int acc) {
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc == 0 ? leader_tempty0 : leader_tempty1);
+    };
+    for (int t = cid; t < p.m_tiles; t += ncl) {
       const int acc = p.n_acc == 2 ? (it & 1) : 0;
       const uint32_t aph = static_cast<uint32_t>(p.n_acc == 2 ? ((it >> 1) & 1) : (it & 1));
-      if (!mbar_wait(tfull_bar(acc), aph, abort_flag)) {
+      if (!mbar_wait_cluster(tfull_bar(acc), aph, abort_flag)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const int64_t wrow0 = static_cast<int64_t>(t) * BM + quad * 32;  // warp's first token
+      const int64_t wrow0 = static_cast<int64_t>(t) * kPairRows + rank * BM + quad * 32;
       const int64_t row = wrow0 + lane;
       const bool rvalid = row < p.T;
       const uint32_t tbase = tmem_base + (static_cast<uint32_t>(quad * 32) << 16) +
@@ -295,9 +352,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         sv[j] = 0.f;
       }
       float m = -INFINITY;
-      // Pass 1: logits out, selection, row maximum of the scores.
+      // Pass 1 over this quarter's columns: logits out, selection, maximum.
 #pragma unroll 1
-      for (int c0 = 0; c0 < E; c0 += 32) {
+      for (int ch = c_begin; ch < c_end; ++ch) {
+        const int c0 = ch * 32;
         uint32_t r[32];
         tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c0), r);
         tmem_ld_wait();
@@ -318,11 +376,74 @@ __global__ void __launch_bounds__(kThreads, 1)
           }
         }
       }
+      if (!(quarter == 0 && full_sum)) release_acc(acc);
+      if (!p.route) {
+        ++it;
+        continue;
+      }
+
+      // Hand the list over, zero this quarter's share of the dense rows.
+      if (quarter != 0) {
+        // quarter 0 has finished reading the previous tile's lists
+        if (it > 0 && !mbar_wait(free_bar(quad), static_cast<uint32_t>((it - 1) & 1), abort_flag)) {
+          ok = false;
+          break;
+        }
+        const int q = quarter - 1;
+#pragma unroll
+        for (int j = 0; j < KMAX; ++j) {
+          if (j < K) {
+            m_keys[(q * K + j) * BM + r_in_cta] = sel[j];
+            m_vals[(q * K + j) * BM + r_in_cta] = sv[j];
+          }
+        }
+        m_max[q * BM + r_in_cta] = m;
+      }
+      const int64_t nrows = min(static_cast<int64_t>(32), p.T - wrow0);
+      if (nrows > 0) {
+        const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+        if (p.probs != nullptr) {
+          uint4* dst = reinterpret_cast<uint4*>(p.probs + wrow0 * E);
+          const int64_t n16 = nrows * E / 4;
+          for (int64_t i = quarter * 32 + lane; i < n16; i += 128) dst[i] = z;
+        }
+        if (p.rmap != nullptr) {
+          uint4* dst = reinterpret_cast<uint4*>(p.rmap + wrow0 * E);
+          const int64_t n16 = nrows * E / 16;
+          for (int64_t i = quarter * 32 + lane; i < n16; i += 128) dst[i] = z;
+        }
+      }
+      // Quadrant barrier (bounded): lists, maxima and zeros of all four
+      // quarters are visible to quarter 0 after it.
+      __threadfence_block();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(quad_bar(quad));
+      if (!mbar_wait(quad_bar(quad), static_cast<uint32_t>(it & 1), abort_flag)) {
+        ok = false;
+        break;
+      }
+      ++it;
+      if (quarter != 0) continue;
+
+#pragma unroll 1
+      for (int q = 0; q < 3; ++q) {
+        m = fmaxf(m, m_max[q * BM + r_in_cta]);
+#pragma unroll
+        for (int j = 0; j < KMAX; ++j) {
+          if (j < K) {
+            const uint64_t key = m_keys[(q * K + j) * BM + r_in_cta];
+            const float v = m_vals[(q * K + j) * BM + r_in_cta];
+            topk_insert<KMAX>(sel, sv, key, v);
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(free_bar(quad));  // the lists may be overwritten
       // Normalisers, in the summation order of the warp-per-row router:
       // lane l of that kernel sums columns l, l+32, ... in turn, then the 32
       // partial sums meet in an xor butterfly (offsets 16, 8, 4, 2, 1).
       float denom = 1.f, gsum = 1.f;
-      if (p.route && p.mode == 1) {
+      if (p.mode == 1) {
         if (p.renorm) {
           float s = 0.f;
 #pragma unroll
@@ -335,81 +456,55 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 32; ++j) part[j] = 0.f;
 #pragma unroll 1
           for (int c0 = 0; c0 < E; c0 += 32) {
-            uint32_t r[32];
-            tmem_ld_32x32b_x32(tbase + static_cast<uint32_t>(c0), r);
-            tmem_ld_wait();
 #pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              float x = __uint_as_float(r[j]);
-              if (p.bias != nullptr) x += __ldg(p.bias + c0 + j);
-              part[j] += expf(x - m);
+            for (int hh = 0; hh < 2; ++hh) {
+              uint32_t r[16];
+              tmem_ld_32x32b_x16(tbase + static_cast<uint32_t>(c0 + 16 * hh), r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int j = 0; j < 16; ++j) {
+                float x = __uint_as_float(r[j]);
+                if (p.bias != nullptr) x += __ldg(p.bias + c0 + 16 * hh + j);
+                part[16 * hh + j] += expf(x - m);
+              }
             }
           }
+          release_acc(acc);
 #pragma unroll
           for (int off = 16; off > 0; off >>= 1) {
-            float nxt[32];
 #pragma unroll
-            for (int j = 0; j < 32; ++j) nxt[j] = part[j] + part[j ^ off];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) part[j] = nxt[j];
+            for (int j = 0; j < 32; ++j) {
+              if (j < (j ^ off)) {
+                const float a = part[j], b = part[j ^ off];
+                part[j] = a + b;
+                part[j ^ off] = b + a;
+              }
+            }
           }
           denom = part[0];
         }
-      } else if (p.route && p.mode == 2 && p.renorm) {
+      } else if (p.mode == 2 && p.renorm) {
         float s = 0.f;
 #pragma unroll
         for (int j = 0; j < KMAX; ++j)
           if (j < p.k) s += key_value(sel[j]);
         gsum = s;
       }
-      // The accumulator is no longer needed: hand it back to the MMA warp.
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(tempty_bar(acc));
-      ++it;
-
-      if (p.route) {
-        auto gate_of = [&](float x) {
-          if (p.mode == 1) return expf(x - m) / denom;
-          if (p.mode == 2 && p.renorm) return x / gsum;
-          return x;
-        };
-        if (rvalid) {
+      auto gate_of = [&](float x) {
+        if (p.mode == 1) return expf(x - m) / denom;
+        if (p.mode == 2 && p.renorm) return x / gsum;
+        return x;
+      };
+      if (rvalid) {
 #pragma unroll
-          for (int j = 0; j < KMAX; ++j) {
-            if (j < p.k) {
-              if (p.vals != nullptr) p.vals[row * p.k + j] = gate_of(sv[j]);
-              if (p.idx != nullptr) p.idx[row * p.k + j] = key_column(sel[j]);
-            }
-          }
-        }
-        if (p.rmap != nullptr || p.probs != nullptr) {
-          // Zero the warp's contiguous rows with coalesced stores, then place
-          // each token's k entries (ordered after the zeros by __syncwarp).
-          const int64_t nrows = min(static_cast<int64_t>(32), p.T - wrow0);
-          if (nrows > 0) {
-            const uint4 z = make_uint4(0u, 0u, 0u, 0u);
-            if (p.probs != nullptr) {
-              uint4* dst = reinterpret_cast<uint4*>(p.probs + wrow0 * E);
-              const int64_t n16 = nrows * E / 4;
-              for (int64_t i = lane; i < n16; i += 32) dst[i] = z;
-            }
-            if (p.rmap != nullptr) {
-              uint4* dst = reinterpret_cast<uint4*>(p.rmap + wrow0 * E);
-              const int64_t n16 = nrows * E / 16;
-              for (int64_t i = lane; i < n16; i += 32) dst[i] = z;
-            }
-          }
-          __syncwarp();
-          if (rvalid) {
-#pragma unroll
-            for (int j = 0; j < KMAX; ++j) {
-              if (j < p.k) {
-                const int c = key_column(sel[j]);
-                if (p.probs != nullptr) p.probs[row * E + c] = gate_of(sv[j]);
-                if (p.rmap != nullptr) p.rmap[row * E + c] = 1;
-              }
-            }
+        for (int j = 0; j < KMAX; ++j) {
+          if (j < p.k) {
+            const int c = key_column(sel[j]);
+            const float gte = gate_of(sv[j]);
+            if (p.vals != nullptr) p.vals[row * p.k + j] = gte;
+            if (p.idx != nullptr) p.idx[row * p.k + j] = c;
+            if (p.probs != nullptr) p.probs[row * E + c] = gte;
+            if (p.rmap != nullptr) p.rmap[row * E + c] = 1;
           }
         }
       }
@@ -419,15 +514,37 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   tc_fence_before();
   __syncthreads();
+  cluster_sync();  // no CTA leaves while its partner may still touch its memory
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem_base, p.tmem_cols);
+    tmem_dealloc_pair(tmem_base, p.tmem_cols);
   }
 }
 
-size_t smem_bytes(int stages, int E) {
-  return 1024 + static_cast<size_t>(stages) * (kABytes + static_cast<size_t>(E) * BK * 2) +
-         kSmemTail;
+size_t smem_bytes(int stages, int E, int k) {
+  return 1024 + static_cast<size_t>(stages) * (kABytes + static_cast<size_t>(E / 2) * BK * 2) +
+         ((merge_bytes(k) + 7) & ~size_t(7)) + kSmemTail;
+}
+
+// Clusters of 2 that can be resident at once for this kernel and smem size.
+template <int KMAX>
+int max_clusters(size_t smem) {
+  int n = 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * 74);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaOccupancyMaxActiveClusters(&n, router_gemm_topk_kernel<KMAX>, &cfg) != cudaSuccess)
+    n = 0;
+  cudaGetLastError();  // clear a non-sticky error from an unsupported query
+  return n;
 }
 
 int ensure_attr() {
@@ -446,6 +563,61 @@ int ensure_attr() {
                                      static_cast<int>(kSmemMax)),
                 "cudaFuncSetAttribute(router_gemm_topk<16>)");
   if (dev < 64) done[dev] = true;
+  return MOE_OK;
+}
+
+template <int KMAX>
+int launch(const CUtensorMap& tx, const CUtensorMap& tw, Params p, cudaStream_t s) {
+  // Stages: as many x-tile + half-W-tile stages as fit beside the merge area.
+  const size_t stage_bytes = kABytes + static_cast<size_t>(p.E / 2) * (BK * 2);
+  const size_t merge = (merge_bytes(p.k) + 7) & ~size_t(7);
+  int stages = static_cast<int>((kSmemMax - 1024 - kSmemTail - merge) / stage_bytes);
+  stages = stages > kMaxStages ? kMaxStages : stages;
+  MOE_REQUIRE(stages >= 2, "router_gemm_topk: E=%d leaves fewer than two stages", p.E);
+  p.stages = stages;
+  const size_t smem = smem_bytes(stages, p.E, p.k);
+  int dev = 0;
+  MOE_CUDA_CALL(cudaGetDevice(&dev), "cudaGetDevice");
+  static std::mutex mu;
+  // Resident clusters depend only on the shared memory per CTA (one CTA per
+  // SM either way); cached per device and size.
+  static int cache[64][4];
+  static size_t cache_smem[64][4];
+  static int cache_n[64] = {};
+  int ncl = -1;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev >= 0 && dev < 64)
+      for (int i = 0; i < cache_n[dev]; ++i)
+        if (cache_smem[dev][i] == smem) ncl = cache[dev][i];
+    if (ncl < 0) {
+      ncl = max_clusters<KMAX>(smem);
+      if (dev >= 0 && dev < 64) {
+        const int i = cache_n[dev] < 4 ? cache_n[dev]++ : 3;
+        cache[dev][i] = ncl;
+        cache_smem[dev][i] = smem;
+      }
+    }
+  }
+  if (ncl <= 0) {
+    set_last_error("router_gemm_topk: CTA pairs cannot be scheduled (smem %zu)", smem);
+    return MOE_ERR_UNSUPPORTED;
+  }
+  const int clusters = p.m_tiles < ncl ? p.m_tiles : ncl;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * clusters);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  MOE_CUDA_CALL(cudaLaunchKernelEx(&cfg, router_gemm_topk_kernel<KMAX>, tx, tw, p),
+                "router_gemm_topk launch");
   return MOE_OK;
 }
 
@@ -480,15 +652,10 @@ extern "C" int moe_router_gemm_topk(const void* x, const void* w, const float* b
   int st = rg::ensure_attr();
   if (st) return st;
 
-  // Stages: as many x-tile + W-tile stages as fit in shared memory.
-  const uint32_t stage_bytes = rg::kABytes + static_cast<uint32_t>(E) * (rg::BK * 2);
-  int stages = static_cast<int>((rg::kSmemMax - 1024 - rg::kSmemTail) / stage_bytes);
-  stages = stages > rg::kMaxStages ? rg::kMaxStages : stages;
-  MOE_REQUIRE(stages >= 2, "router_gemm_topk: E=%lld leaves fewer than two stages",
-              (long long)E);
-  // W boxes: the largest power of two <= 256 rows that divides E.
-  int bbr = 256;
-  while (E % bbr != 0) bbr >>= 1;
+  // N pieces of at most 256 columns; each CTA of the pair stages half of a
+  // piece's W rows (a multiple of 8 rows, whole 128-byte swizzle atoms).
+  const int n_pieces = static_cast<int>((E + 255) / 256);
+  const int piece_n = static_cast<int>(E / n_pieces);
 
   CUtensorMap tx, tw;
   st = gg::make_tmap_box(&tx, x, static_cast<uint64_t>(H), static_cast<uint64_t>(T),
@@ -496,7 +663,7 @@ extern "C" int moe_router_gemm_topk(const void* x, const void* w, const float* b
                          CU_TENSOR_MAP_SWIZZLE_128B, false);
   if (st) return st;
   st = gg::make_tmap_box(&tw, w, static_cast<uint64_t>(H), static_cast<uint64_t>(E),
-                         static_cast<uint32_t>(rg::BK), static_cast<uint32_t>(bbr),
+                         static_cast<uint32_t>(rg::BK), static_cast<uint32_t>(piece_n / 2),
                          CU_TENSOR_MAP_SWIZZLE_128B, false);
   if (st) return st;
 
@@ -515,26 +682,16 @@ extern "C" int moe_router_gemm_topk(const void* x, const void* w, const float* b
   p.renorm = renorm ? 1 : 0;
   p.route = route ? 1 : 0;
   p.num_kb = static_cast<int>((H + rg::BK - 1) / rg::BK);
-  p.m_tiles = static_cast<int>((T + rg::BM - 1) / rg::BM);
-  p.stages = stages;
-  p.b_box_rows = bbr;
-  p.b_boxes = static_cast<int>(E / bbr);
+  p.m_tiles = static_cast<int>((T + rg::kPairRows - 1) / rg::kPairRows);
+  p.stages = 0;
+  p.n_pieces = n_pieces;
+  p.piece_n = piece_n;
   int acc = 32;
   while (acc < E) acc <<= 1;
   p.acc_stride = acc;
   p.n_acc = 2 * acc <= 512 ? 2 : 1;
   p.tmem_cols = static_cast<uint32_t>(p.n_acc * acc);
 
-  int dev = 0;
-  MOE_CUDA_CALL(cudaGetDevice(&dev), "cudaGetDevice");
-  const int sms = num_sms(dev);
-  const int grid = p.m_tiles < sms ? p.m_tiles : sms;
-  const size_t smem = rg::smem_bytes(stages, p.E);
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
-  if (k <= 8)
-    rg::router_gemm_topk_kernel<8><<<grid, rg::kThreads, smem, s>>>(tx, tw, p);
-  else
-    rg::router_gemm_topk_kernel<16><<<grid, rg::kThreads, smem, s>>>(tx, tw, p);
-  MOE_CUDA_CHECK_LAUNCH("router_gemm_topk launch");
-  return MOE_OK;
+  return k <= 8 ? rg::launch<8>(tx, tw, p, s) : rg::launch<16>(tx, tw, p, s);
 }
