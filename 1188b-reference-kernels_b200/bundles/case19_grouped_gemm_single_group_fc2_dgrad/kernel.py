@@ -1,0 +1,17 @@
+"""Drop-in for kernel_cases/case19_grouped_gemm_single_group_fc2_dgrad.py:57-64:
+dx [T,K] = dy [T,N] @ w[0] with the forward weight w [1,N,K] bf16 as it is
+("NN"), fp32 accumulation, bf16 out. Any G works, with uniform group_sizes
+(:43-46) unless m_splits is given.
+"""
+import sys
+from pathlib import Path
+
+_PKG = str(Path(__file__).resolve().parents[2])
+if _PKG not in sys.path:
+    sys.path.insert(0, _PKG)
+
+import moe_b200  # noqa: E402
+
+
+def kernel_function(dy, w, m_splits=None):
+    return moe_b200.grouped_gemm(dy, w, m_splits, w_layout="KN")

@@ -243,6 +243,18 @@ def gen_gemm(root: Path) -> None:
     inp = torch.randn(80, 512, generator=gen).to(torch.bfloat16)
     wt = torch.randn(c38.N, 512, generator=gen).to(torch.bfloat16)
     out.update(c38_x=bits(inp), c38_w=bits(wt), c38_y=c38.reference_fp32(inp, wt).numpy())
+    # One-group fc2 forward (case14's own Model) and the single NN GEMM of case37.
+    c14 = load_case(root, "case14_grouped_gemm_single_group_fc2_fwd")
+    gen = torch.Generator().manual_seed(14)
+    x = torch.randn(150, 96, generator=gen).to(torch.bfloat16)
+    w = (torch.randn(1, 192, 96, generator=gen) * 0.05).to(torch.bfloat16)
+    out.update(c14_x=bits(x), c14_w=bits(w), c14_y=bits(c14.Model(1, 150)(x, w)),
+               c14_splits=np.array(c14.group_sizes(150, 1)))
+    c37 = load_case(root, "case37_ref_musa_asm_bf16_gemm_nn_256x384")
+    gen = torch.Generator().manual_seed(37)
+    go = torch.randn(72, 320, generator=gen).to(torch.bfloat16)
+    wt = torch.randn(320, 256, generator=gen).to(torch.bfloat16)
+    out.update(c37_x=bits(go), c37_w=bits(wt), c37_y=c37.reference_fp32(go, wt).numpy())
     # Build-only ops (no reference code): torch fp32 restatements pin the numpy oracle.
     gen = torch.Generator().manual_seed(8)
     y = torch.randn(64, 2 * 96, generator=gen).to(torch.bfloat16)

@@ -58,7 +58,9 @@ def test_reference_models_golden(cuda_dev, golden):
     z = golden("gemm_swiglu.npz")
     for tag, case in (("c03", "case03_moe_grouped_gemm_fc1_fwd"),
                       ("c04", "case04_moe_grouped_gemm_fc2_fwd"),
-                      ("c10", "case03_moe_grouped_gemm_fc1_fwd")):
+                      ("c10", "case03_moe_grouped_gemm_fc1_fwd"),
+                      ("c10", "case10_grouped_gemm_single_group_fc1_fwd"),
+                      ("c14", "case14_grouped_gemm_single_group_fc2_fwd")):
         y = load_bundle(case).kernel_function(from_u16(z[f"{tag}_x"], cuda_dev),
                                               from_u16(z[f"{tag}_w"], cuda_dev))
         assert y.dtype == torch.bfloat16 and y.shape == z[f"{tag}_y"].shape
@@ -71,6 +73,15 @@ def test_single_expert_fp32_golden(cuda_dev, golden):
     y = load_bundle("case35_bf16_gemm_nt").kernel_function(from_u16(z["c35_x"], cuda_dev),
                                                            from_u16(z["c35_w"], cuda_dev))
     assert_gemm_close(y, z["c35_y"], "c35")
+
+
+def test_single_expert_nn_fp32_golden(cuda_dev, golden):
+    """case37 bundle (grad_output @ weight, "NN") vs reference_fp32."""
+    z = golden("gemm_swiglu.npz")
+    y = load_bundle("case37_bf16_gemm_nn").kernel_function(from_u16(z["c37_x"], cuda_dev),
+                                                           from_u16(z["c37_w"], cuda_dev))
+    assert y.dtype == torch.bfloat16 and y.shape == z["c37_y"].shape
+    assert_gemm_close(y, z["c37_y"], "c37")
 
 
 def _rand_bf16(g, *shape, std=1.0):
@@ -120,7 +131,9 @@ def test_dgrad_reference_models_golden(cuda_dev, golden):
     for tag, case in (("c07", "case07_moe_grouped_gemm_fc1_dgrad"),
                       ("c08", "case08_moe_grouped_gemm_fc2_dgrad"),
                       ("c13", "case07_moe_grouped_gemm_fc1_dgrad"),
-                      ("c19", "case08_moe_grouped_gemm_fc2_dgrad")):
+                      ("c19", "case08_moe_grouped_gemm_fc2_dgrad"),
+                      ("c13", "case13_grouped_gemm_single_group_fc1_dgrad"),
+                      ("c19", "case19_grouped_gemm_single_group_fc2_dgrad")):
         dx = load_bundle(case).kernel_function(from_u16(z[f"{tag}_dy"], cuda_dev),
                                                from_u16(z[f"{tag}_w"], cuda_dev))
         assert dx.dtype == torch.bfloat16 and dx.shape == z[f"{tag}_dx"].shape

@@ -191,7 +191,7 @@ def _gemm_close(got_u16, ref_f32):
 
 def test_grouped_gemm_against_reference_models(golden):
     z = golden("gemm_swiglu.npz")
-    for tag in ("c03", "c04", "c10"):
+    for tag in ("c03", "c04", "c10", "c14"):
         y = orc.grouped_gemm(z[f"{tag}_x"], z[f"{tag}_w"], z[f"{tag}_splits"])
         ref = orc.bf16_to_f32(z[f"{tag}_y"])
         _gemm_close(y, ref)
@@ -204,6 +204,13 @@ def test_single_expert_gemm_fp32_golden(golden):
     z = golden("gemm_swiglu.npz")
     y = orc.grouped_gemm(z["c35_x"], z["c35_w"][None], [z["c35_x"].shape[0]])
     _gemm_close(y, z["c35_y"])
+
+
+def test_single_expert_nn_gemm_fp32_golden(golden):
+    """case37: out = grad_output @ weight ("NN"), the one-group dgrad form."""
+    z = golden("gemm_swiglu.npz")
+    y = orc.grouped_gemm(z["c37_x"], z["c37_w"][None], [z["c37_x"].shape[0]], w_layout="KN")
+    _gemm_close(y, z["c37_y"])
 
 
 def test_grouped_dgrad_against_reference_models(golden):
