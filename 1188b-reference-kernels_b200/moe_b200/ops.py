@@ -515,6 +515,8 @@ _ROUTER_ERR: dict = {}
 
 
 def _router_err(dev: torch.device) -> torch.Tensor:
+    if dev.index is None:
+        dev = torch.device(dev.type, torch.cuda.current_device())
     e = _ROUTER_ERR.get(dev)
     if e is None:
         e = torch.zeros(1, dtype=torch.int32, device=dev)
@@ -524,7 +526,10 @@ def _router_err(dev: torch.device) -> torch.Tensor:
 
 def router_device_error(device) -> int:
     """Error code left by router_gemm_topk on this device (0: none). Syncs."""
-    e = _ROUTER_ERR.get(torch.device(device))
+    dev = torch.device(device)
+    if dev.index is None:
+        dev = torch.device(dev.type, torch.cuda.current_device())
+    e = _ROUTER_ERR.get(dev)
     return 0 if e is None else int(e.item())
 
 
