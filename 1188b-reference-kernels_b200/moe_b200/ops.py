@@ -21,7 +21,9 @@ from . import _lib
 
 __all__ = [
     "topk", "router_topk", "RouterOutput", "row_id_map", "RowIdMap", "permute",
-    "permute_trans", "unpermute", "grouped_gemm", "GroupedGemmPlan", "swiglu",
+    "permute_trans", "unpermute", "unpermute_weighted", "grouped_gemm", "GroupedGemmPlan",
+    "grouped_wgrad", "swiglu", "router_logits", "router_gemm_topk", "router_gemm_fusable",
+    "router_device_error", "permute_backward",
 ]
 
 
