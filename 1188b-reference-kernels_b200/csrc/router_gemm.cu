@@ -135,6 +135,50 @@ MOE_DEVICE void topk_insert(uint64_t (&sel)[KMAX], float (&sv)[KMAX], uint64_t k
   }
 }
 
+// Compare-exchange of two (key, score) pairs: the larger key first.
+MOE_DEVICE void ce_desc(uint64_t& ka, float& va, uint64_t& kb, float& vb) {
+  const bool sw = kb > ka;
+  const uint64_t k0 = sw ? kb : ka, k1 = sw ? ka : kb;
+  const float v0 = sw ? vb : va, v1 = sw ? va : vb;
+  ka = k0;
+  kb = k1;
+  va = v0;
+  vb = v1;
+}
+
+// Sorting network for 8 elements (19 comparators, depth 6) and the bitonic
+// half-cleaner cascade that sorts an 8-element bitonic sequence (12).
+__device__ constexpr int kSort8[19][2] = {{0, 2}, {1, 3}, {4, 6}, {5, 7}, {0, 4}, {1, 5}, {2, 6},
+                                          {3, 7}, {0, 1}, {2, 3}, {4, 5}, {6, 7}, {2, 4}, {3, 5},
+                                          {1, 4}, {3, 6}, {1, 2}, {3, 4}, {5, 6}};
+__device__ constexpr int kBitonic8[12][2] = {{0, 4}, {1, 5}, {2, 6}, {3, 7}, {0, 2}, {1, 3},
+                                             {4, 6}, {5, 7}, {0, 1}, {2, 3}, {4, 5}, {6, 7}};
+
+// Merges 8 (key, score) pairs, sorted descending, into the descending top-8
+// (sel, sv): the larger of sel[i] and new[7-i] form a bitonic sequence that
+// holds the top 8 of both lists, which the cascade sorts. Branch-free, so the
+// 32 rows of a warp never diverge.
+MOE_DEVICE void top8_merge_sorted(uint64_t (&sel)[8], float (&sv)[8], const uint64_t (&nk)[8],
+                                  const float (&nv)[8]) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const bool t = nk[7 - i] > sel[i];
+    sel[i] = t ? nk[7 - i] : sel[i];
+    sv[i] = t ? nv[7 - i] : sv[i];
+  }
+#pragma unroll
+  for (int c = 0; c < 12; ++c)
+    ce_desc(sel[kBitonic8[c][0]], sv[kBitonic8[c][0]], sel[kBitonic8[c][1]], sv[kBitonic8[c][1]]);
+}
+
+// Same for 8 unsorted pairs (sorted first by the 19-comparator network).
+MOE_DEVICE void top8_merge8(uint64_t (&sel)[8], float (&sv)[8], uint64_t (&nk)[8], float (&nv)[8]) {
+#pragma unroll
+  for (int c = 0; c < 19; ++c)
+    ce_desc(nk[kSort8[c][0]], nv[kSort8[c][0]], nk[kSort8[c][1]], nv[kSort8[c][1]]);
+  top8_merge_sorted(sel, sv, nk, nv);
+}
+
 template <int KMAX>
 __global__ void __launch_bounds__(kThreads, 1)
     router_gemm_topk_kernel(const __grid_constant__ CUtensorMap tmap_x,
@@ -367,12 +411,31 @@ __global__ void __launch_bounds__(kThreads, 1)
                 make_uint4(r[v * 4], r[v * 4 + 1], r[v * 4 + 2], r[v * 4 + 3]);
         }
         if (p.route) {
+          if constexpr (KMAX == 8) {
+            // eight columns at a time through the branch-free merge network
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float x = __uint_as_float(r[j]);
-            if (p.bias != nullptr) x += __ldg(p.bias + c0 + j);
-            m = fmaxf(m, x);
-            topk_insert<KMAX>(sel, sv, rank_key(x, c0 + j), x);
+            for (int g8 = 0; g8 < 4; ++g8) {
+              uint64_t nk[8];
+              float nv[8];
+#pragma unroll
+              for (int j = 0; j < 8; ++j) {
+                const int c = c0 + 8 * g8 + j;
+                float x = __uint_as_float(r[8 * g8 + j]);
+                if (p.bias != nullptr) x += __ldg(p.bias + c);
+                m = fmaxf(m, x);
+                nk[j] = rank_key(x, c);
+                nv[j] = x;
+              }
+              top8_merge8(sel, sv, nk, nv);
+            }
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) {
+              float x = __uint_as_float(r[j]);
+              if (p.bias != nullptr) x += __ldg(p.bias + c0 + j);
+              m = fmaxf(m, x);
+              topk_insert<KMAX>(sel, sv, rank_key(x, c0 + j), x);
+            }
           }
         }
       }
@@ -428,12 +491,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll 1
       for (int q = 0; q < 3; ++q) {
         m = fmaxf(m, m_max[q * BM + r_in_cta]);
+        if constexpr (KMAX == 8) {
+          uint64_t nk[8];
+          float nv[8];
 #pragma unroll
-        for (int j = 0; j < KMAX; ++j) {
-          if (j < K) {
-            const uint64_t key = m_keys[(q * K + j) * BM + r_in_cta];
-            const float v = m_vals[(q * K + j) * BM + r_in_cta];
-            topk_insert<KMAX>(sel, sv, key, v);
+          for (int j = 0; j < 8; ++j) {  // a sorted list; slots past k are empty
+            nk[j] = j < K ? m_keys[(q * K + j) * BM + r_in_cta] : 0ull;
+            nv[j] = j < K ? m_vals[(q * K + j) * BM + r_in_cta] : 0.f;
+          }
+          top8_merge_sorted(sel, sv, nk, nv);
+        } else {
+#pragma unroll
+          for (int j = 0; j < KMAX; ++j) {
+            if (j < K) {
+              const uint64_t key = m_keys[(q * K + j) * BM + r_in_cta];
+              const float v = m_vals[(q * K + j) * BM + r_in_cta];
+              topk_insert<KMAX>(sel, sv, key, v);
+            }
           }
         }
       }
