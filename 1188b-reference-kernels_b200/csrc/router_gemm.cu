@@ -22,7 +22,9 @@
 // producer, warp 1 owns TMEM and (in the leader) issues the MMAs, warps 2-17
 // are the epilogue: four warps per TMEM lane quadrant, each reading a quarter
 // of the columns of its 32 rows (tcgen05.ld 32x32b, one row per thread) and
-// keeping a register-resident sorted top-k of them. The quarters meet on a
+// keeping a register-resident sorted top-k of them (for k <= 8 through a
+// branch-free sort-and-merge network, eight columns at a time, so the rows
+// of a warp never diverge; for larger k by insertion). The quarters meet on a
 // per-quadrant mbarrier; the first merges the other three lists (keys are
 // unique, so the merged selection is exact), forms the normalisers and writes
 // the outputs. Selection, softmax maximum, normalisers (with their summation
