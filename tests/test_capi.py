@@ -66,6 +66,20 @@ def test_invalid_arguments_are_rejected_without_launch(lib):
     # GEMM argument checks
     assert lib.moe_grouped_gemm(None, None, None, 10, 4, 4, 256, 12, 0, None, 0, None) == 1
     assert lib.moe_grouped_gemm(None, None, None, 10, 4, 4, 256, 64, 2, None, 0, None) == 1
+    # fused router: E must be a multiple of 32 up to 512, 1 <= k <= 16, an
+    # error word is required, and at least one output must be asked for
+    rg = lib.moe_router_gemm_topk
+    assert rg(16, 16, None, 16, 64, 48, 4, 1, 1, None, None, None, 16, 16, 16, None) == 1
+    assert b"multiple of 32" in lib.moe_b200_last_error()
+    assert rg(16, 16, None, 16, 64, 1024, 4, 1, 1, None, None, None, 16, 16, 16, None) == 1
+    assert rg(16, 16, None, 16, 64, 64, 17, 1, 1, None, None, None, 16, 16, 16, None) == 1
+    assert rg(16, 16, None, 16, 64, 64, 4, 1, 1, None, None, None, 16, 16, None, None) == 1
+    assert b"device_error" in lib.moe_b200_last_error()
+    assert rg(16, 16, None, 16, 64, 64, 4, 1, 1, None, None, None, None, None, 16, None) == 1
+    assert b"no output" in lib.moe_b200_last_error()
+    assert rg(16, 16, None, 16, 60, 64, 4, 1, 1, None, None, None, 16, 16, 16, None) == 1
+    assert rg(16, 16, None, 16, 64, 64, 4, 2, 1, None, None, None, 16, 16, 16, None) == 1
+    assert rg(None, None, None, 0, 64, 64, 4, 1, 1, None, None, None, None, None, 16, None) == 0
 
 
 def test_ops_refuse_cpu_tensors():
@@ -79,6 +93,18 @@ def test_ops_refuse_cpu_tensors():
     with pytest.raises(ValueError):
         moe_b200.grouped_gemm(torch.zeros(4, 8, dtype=torch.bfloat16),
                               torch.zeros(1, 8, 8, dtype=torch.bfloat16))
+    x16 = torch.zeros(4, 64, dtype=torch.bfloat16)
+    w16 = torch.zeros(32, 64, dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        moe_b200.router_gemm_topk(x16, w16, 4)
+    with pytest.raises(ValueError):
+        moe_b200.router_logits(x16, w16)
+    with pytest.raises(ValueError):
+        moe_b200.grouped_wgrad(torch.zeros(4, 8, dtype=torch.bfloat16),
+                               torch.zeros(4, 8, dtype=torch.bfloat16), [4])
+    with pytest.raises(ValueError):
+        moe_b200.permute_backward(torch.zeros(4, 8, dtype=torch.bfloat16),
+                                  torch.zeros(2, 4, dtype=torch.int64))
 
 
 def test_product_package_does_not_import_oracle():
