@@ -16,14 +16,16 @@
 // partial 64-row block is zero-filled by TMA instead of reaching into the next
 // group. A group with no rows gets a zero dW[g], like torch.mm over zero rows.
 //
-// Kernel structure (one persistent CTA per SM, 192 threads), as the forward
-// single-CTA kernel: warp 0 TMA producer (4-stage ring, 16 KB dy + 32 KB x per
-// stage), warp 1 TMEM owner and single-thread MMA issuer (M=128 dW rows,
-// N=256 dW columns, K=16), warps 2-5 epilogue. With few rows per group the
-// tile's mainloop is short and dW's bytes dominate, so the epilogue moves 64
-// columns per step (two TMEM loads under one wait, one 32 x 64 TMA tile store
-// from a 128B-swizzled buffer, four stores in flight per warp). Every wait is
-// bounded (2 s).
+// Two kernels, chosen per call from the mean rows per group:
+//   grouped_wgrad_pair_kernel (deep groups): CTA pairs (cta_group::2) on
+//     256 x 256 tiles of dW[g], 5-stage ring of 32 KB per CTA;
+//   grouped_wgrad_kernel (shallow groups, where writing dW dominates): one
+//     persistent CTA per SM on 128 x 256 tiles, 3-stage ring of 16 KB dy +
+//     32 KB x.
+// Both: warp 0 TMA producer, warp 1 TMEM owner and single-thread MMA issuer,
+// warps 2-5 epilogue. The epilogue moves 64 columns per step (two TMEM loads
+// under one wait, one 32 x 64 TMA tile store from a 128B-swizzled buffer,
+// four stores in flight per warp). Every wait is bounded (2 s).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <string.h>
@@ -335,6 +337,293 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
 }
 
+// ---------------------------------------------------------------------------
+// CTA-pair variant (tcgen05 cta_group::2, clusters of 2): a pair owns a
+// 256 x 256 tile of dW[g]. Each CTA stages 128 columns of dy (its 128 dW
+// rows) and half of the tile's 256 x columns per reduction block, 32 KB a
+// stage, so per SM the operand traffic is two thirds of the single-CTA
+// kernel's and the ring is five stages deep beside the same epilogue buffers.
+// The leader issues M=256, N=256 MMAs with both operands MN-major; each CTA's
+// TMEM receives its 128 dW rows. TMA bytes of both CTAs count on the leader's
+// full barrier, the commits release both CTAs' stages, both CTAs' epilogue
+// warps arrive on the leader's accumulator-empty barrier. Waits bounded as in
+// the single-CTA kernel; a cluster barrier precedes the pair TMEM release.
+// ---------------------------------------------------------------------------
+constexpr int kPairTile = 256;
+constexpr int kPairStages = 5;
+constexpr int64_t kPairMinRows = 384;  // mean rows per group with rows for the pair kernel
+constexpr uint32_t kPairHalfBytes = 2 * kBox;                    // 128 columns x 64 rows
+constexpr uint32_t kPairStageBytes = 2 * kPairHalfBytes;          // dy half + x half: 32 KB
+constexpr size_t kPairSmemBytes =
+    1024 + kPairStages * kPairStageBytes + 1024 + 4 * kEpiBufs * kEpiBoxBytes;
+
+__global__ void __launch_bounds__(kThreads, 1)
+    grouped_wgrad_pair_kernel(const __grid_constant__ CUtensorMap tmap_out, const Params p) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw_addr = smem_u32(smem_raw);
+  const uint32_t base = (raw_addr + 1023u) & ~1023u;
+  uint8_t* base_ptr = smem_raw + (base - raw_addr);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base_ptr + kPairStages * kPairStageBytes);
+  const uint32_t bar0 = smem_u32(bars);
+  auto full_bar = [&](int s) { return bar0 + 8u * s; };
+  auto empty_bar = [&](int s) { return bar0 + 8u * (kPairStages + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * kPairStages + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * kPairStages + 2 + a); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * kPairStages + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kPairStages + 5);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  const long long cid = cluster_id_x();
+  const long long ncl = num_clusters_x();
+  const int warp = warp_id();
+  const int lane = lane_id();
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(full_bar(s), 1);
+      mbar_init(empty_bar(s), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(tfull_bar(a), 1);
+      mbar_init(tempty_bar(a), 8);  // 4 epilogue warps in each of the 2 CTAs
+    }
+    mbar_init(drain_bar, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc_pair(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // barriers of both CTAs initialised before any remote use
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const long long per_g = static_cast<long long>(p.m_tiles) * p.n_tiles;
+  const long long total = per_g * p.G;
+  auto locate = [&](long long t, int& g, int& mi, int& ni) {
+    g = static_cast<int>(t / per_g);
+    const int r = static_cast<int>(t - g * per_g);
+    mi = r / p.n_tiles;
+    ni = r - mi * p.n_tiles;
+  };
+  auto nkb_of = [&](int g) { return (max(p.rows[g], 0) + BK - 1) / BK; };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      const uint64_t pol = l2_policy_evict_normal();
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued[kPairStages];
+#pragma unroll
+      for (int s = 0; s < kPairStages; ++s) issued[s] = -1;
+      bool ok = true;
+      int last_g = -1;
+      const int half = static_cast<int>(rank) * (kPairTile / 2);
+      for (long long t = cid; t < total && ok; t += ncl) {
+        int g, mi, ni;
+        locate(t, g, mi, ni);
+        const CUtensorMap* ma = p.maps + 2 * g;  // dy rows of group g
+        const CUtensorMap* mb = ma + 1;          // x rows of group g
+        if (g != last_g) {
+          tensormap_acquire(ma);
+          tensormap_acquire(mb);
+          last_g = g;
+        }
+        const int nkb = nkb_of(g);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait(empty_bar(stage), phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const uint32_t sa = base + stage * kPairStageBytes;
+          const uint32_t sb = sa + kPairHalfBytes;
+          const uint32_t leader_full = map_to_rank(full_bar(stage), 0);
+          if (leader) mbar_arrive_expect_tx(full_bar(stage), 2u * kPairStageBytes);
+#pragma unroll
+          for (int j = 0; j < 2; ++j) {
+            tma_load_2d_pair(sa + j * kBox, ma, mi * kPairTile + half + j * 64, kb * BK,
+                             leader_full, pol);
+            tma_load_2d_pair(sb + j * kBox, mb, ni * kPairTile + half + j * 64, kb * BK,
+                             leader_full, pol);
+          }
+          issued[stage] = static_cast<int>(phase);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      if (ok) {
+        // The pair's MMA releases every stage with a commit that lands in this
+        // CTA's shared memory; wait for the last ones before exiting.
+        for (int s = 0; s < kPairStages; ++s)
+          if (issued[s] >= 0) wait_drain(empty_bar(s), static_cast<uint32_t>(issued[s]));
+      } else {
+        raise_abort(abort_flag, p.err, kErrTimeoutProducer);
+        if (leader) {
+          for (int s = 0; s < kPairStages; ++s)
+            if (issued[s] >= 0) wait_drain(full_bar(s), static_cast<uint32_t>(issued[s]));
+        } else {
+          // Copies count on the leader's barrier; give them a bounded time to land.
+          const unsigned long long t0 = globaltimer_ns();
+          while (globaltimer_ns() - t0 < 200000ull) {
+          }
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader)
+    if (leader && lane == 0) {
+      const uint32_t idesc =
+          umma_idesc_bf16_f32(kPairTile, kPairTile) | (1u << 15) | kIdescBMajorMN;
+      int stage = 0;
+      uint32_t phase = 0;
+      int it = 0;
+      bool ok = true;
+      bool issued_any = false;
+      for (long long t = cid; t < total && ok; t += ncl) {
+        int g, mi, ni;
+        locate(t, g, mi, ni);
+        const int acc = it & 1;
+        const uint32_t aph = static_cast<uint32_t>((it >> 1) & 1);
+        if (!mbar_wait_cluster(tempty_bar(acc), aph ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        const int nkb = nkb_of(g);
+        for (int kb = 0; kb < nkb; ++kb) {
+          if (!mbar_wait_cluster(full_bar(stage), phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t sa = base + stage * kPairStageBytes;
+          const uint32_t sb = sa + kPairHalfBytes;
+          const uint64_t ad = umma_desc_mn_sw128(sa, kBox);
+          const uint64_t bd = umma_desc_mn_sw128(sb, kBox);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k)
+            umma_bf16_pair(d_tmem, ad + 128ull * k, bd + 128ull * k, idesc,
+                           (kb | k) != 0 ? 1u : 0u);
+          issued_any = true;
+          umma_commit_pair(empty_bar(stage), 0x3);
+          if (++stage == kPairStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(tfull_bar(acc), 0x3);
+        ++it;
+      }
+      if (!ok) {
+        raise_abort(abort_flag, p.err, kErrTimeoutMma);
+        if (issued_any) {
+          umma_commit_pair(drain_bar, 0x1);
+          wait_drain(drain_bar, 0);
+        }
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int quad = warp & 3;  // TMEM lanes this warp may access: 32*quad ..
+    const uint32_t epi_base = ((bar0 + 512u + 1023u) & ~1023u) +
+                              static_cast<uint32_t>(quad) * kEpiBufs * kEpiBoxBytes;
+    const uint32_t leader_tempty0 = map_to_rank(tempty_bar(0), 0);
+    const uint32_t leader_tempty1 = map_to_rank(tempty_bar(1), 0);
+    uint32_t chunk_no = 0;
+    int it = 0;
+    bool ok = true;
+    for (long long t = cid; t < total; t += ncl) {
+      int g, mi, ni;
+      locate(t, g, mi, ni);
+      const int acc = it & 1;
+      const uint32_t aph = static_cast<uint32_t>((it >> 1) & 1);
+      if (!mbar_wait_cluster(tfull_bar(acc), aph, abort_flag)) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+      const int row_in_tile = static_cast<int>(rank) * 128 + quad * 32;
+      const int rowl = mi * kPairTile + row_in_tile + lane;  // row of dW[g]
+      const bool rvalid = rowl < p.N;
+      const bool tma = __all_sync(0xffffffffu, rvalid);
+      const int gd = p.gid[g];
+      const int warp_row0 = gd * p.N + mi * kPairTile + row_in_tile;  // in the [G*N, K] view
+      __nv_bfloat16* orow = p.out + (static_cast<int64_t>(gd) * p.N + rowl) * p.K;
+      const uint32_t tbase =
+          tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
+#pragma unroll 1
+      for (int c = 0; c < BN / 64; ++c) {
+        const int col = ni * kPairTile + c * 64;
+        if (col >= p.K) break;  // warp-uniform
+        uint32_t r[64];
+        uint32_t (&r0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[0]);
+        uint32_t (&r1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[32]);
+        tmem_ld_32x32b_x32(tbase + c * 64, r0);
+        tmem_ld_32x32b_x32(tbase + c * 64 + 32, r1);
+        tmem_ld_wait();
+        uint32_t o[32];  // this lane's row: 64 bf16 = 128 bytes
+#pragma unroll
+        for (int q = 0; q < 32; ++q)
+          o[q] = pack_bf16x2(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1]));
+        if (tma) {
+          const uint32_t buf = epi_base + (chunk_no % kEpiBufs) * kEpiBoxBytes;
+          ++chunk_no;
+          if (lane == 0) bulk_wait_read<kEpiBufs - 1>();
+          __syncwarp();
+          // 128-byte swizzle: 16-byte chunk j of row r lives at chunk j ^ (r & 7).
+          const uint32_t sw = static_cast<uint32_t>(lane & 7);
+#pragma unroll
+          for (int j = 0; j < 8; ++j) {
+            const uint32_t dst =
+                buf + static_cast<uint32_t>(lane) * 128u + ((static_cast<uint32_t>(j) ^ sw) << 4);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(o[4 * j]),
+                         "r"(o[4 * j + 1]), "r"(o[4 * j + 2]), "r"(o[4 * j + 3])
+                         : "memory");
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmap_out, col, warp_row0, buf);
+            bulk_commit();
+          }
+        } else if (rvalid) {
+#pragma unroll
+          for (int v = 0; v < 8; ++v)
+            if (col + v * 8 + 8 <= p.K)
+              *reinterpret_cast<uint4*>(orow + col + v * 8) =
+                  make_uint4(o[4 * v], o[4 * v + 1], o[4 * v + 2], o[4 * v + 3]);
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(acc == 0 ? leader_tempty0 : leader_tempty1);
+      ++it;
+    }
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+    if (!ok && lane == 0) raise_abort(abort_flag, p.err, kErrTimeoutEpilogue);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  cluster_sync();  // no CTA leaves while its partner may still touch its memory
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, kTmemCols);
+  }
+}
+
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
   static std::once_flag once;
@@ -387,8 +676,43 @@ int ensure_smem_attr() {
                                      cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      static_cast<int>(kSmemBytes)),
                 "cudaFuncSetAttribute(grouped_wgrad)");
+  MOE_CUDA_CALL(cudaFuncSetAttribute(grouped_wgrad_pair_kernel,
+                                     cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     static_cast<int>(kPairSmemBytes)),
+                "cudaFuncSetAttribute(grouped_wgrad_pair)");
   if (dev < 64) done[dev] = true;
   return MOE_OK;
+}
+
+// Clusters of 2 that can be resident at once (0: the pair kernel cannot run,
+// or MOE_WGRAD_PAIR=0 asks for the single-CTA kernel).
+int pair_clusters(int dev) {
+  static std::mutex mu;
+  static int cache[64];
+  static bool init[64] = {};
+  const char* e = getenv("MOE_WGRAD_PAIR");
+  if (e != nullptr && e[0] == '0') return 0;
+  std::lock_guard<std::mutex> lock(mu);
+  if (dev >= 0 && dev < 64 && init[dev]) return cache[dev];
+  int n = 0;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * 74);
+  cfg.blockDim = dim3(kThreads);
+  cfg.dynamicSmemBytes = kPairSmemBytes;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaOccupancyMaxActiveClusters(&n, grouped_wgrad_pair_kernel, &cfg) != cudaSuccess) n = 0;
+  cudaGetLastError();  // clear a non-sticky error from an unsupported query
+  if (dev >= 0 && dev < 64) {
+    cache[dev] = n;
+    init[dev] = true;
+  }
+  return n;
 }
 
 }  // namespace gw
@@ -497,10 +821,36 @@ extern "C" int moe_grouped_wgrad(const void* dy, const void* x, void* dw, int64_
   p.G = static_cast<int>(gnz);
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
-  p.m_tiles = static_cast<int>((N + gw::BM - 1) / gw::BM);
-  p.n_tiles = static_cast<int>((K + gw::BN - 1) / gw::BN);
   int dev = 0;
   MOE_CUDA_CALL(cudaGetDevice(&dev), "cudaGetDevice");
+  // CTA pairs when the groups are deep enough for the MMA to dominate (a
+  // 256 x 256 pair tile moves two thirds of the operand bytes per SM of the
+  // single-CTA tile); with a few k-blocks per tile the kernel is bound by
+  // writing dW, where the single-CTA kernel measured faster (case09's ~100
+  // rows per group: 686 vs 1016 us).
+  const int clusters = gw::pair_clusters(dev);
+  if (clusters > 0 && sum >= gw::kPairMinRows * gnz) {  // 256 x 256 tiles on CTA pairs
+    p.m_tiles = static_cast<int>((N + gw::kPairTile - 1) / gw::kPairTile);
+    p.n_tiles = static_cast<int>((K + gw::kPairTile - 1) / gw::kPairTile);
+    const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles * gnz;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(static_cast<unsigned>(2 * std::min<int64_t>(tiles, clusters)));
+    cfg.blockDim = dim3(gw::kThreads);
+    cfg.dynamicSmemBytes = gw::kPairSmemBytes;
+    cfg.stream = s;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    MOE_CUDA_CALL(cudaLaunchKernelEx(&cfg, gw::grouped_wgrad_pair_kernel, tout, p),
+                  "grouped_wgrad pair launch");
+    return MOE_OK;
+  }
+  p.m_tiles = static_cast<int>((N + gw::BM - 1) / gw::BM);
+  p.n_tiles = static_cast<int>((K + gw::BN - 1) / gw::BN);
   const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles * gnz;
   const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms(dev)));
   gw::grouped_wgrad_kernel<<<grid, gw::kThreads, gw::kSmemBytes, s>>>(tout, p);

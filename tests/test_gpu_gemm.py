@@ -228,6 +228,7 @@ def _wgrad_f32(dy_u16, x_u16, splits):
     ([700, 33, 513], 512, 768),
     ([10, 0, 250], 200, 72),                       # N, K off the 128 x 256 tile
     ([5], 128, 8192),
+    ([300, 77, 0, 1000], 384, 320),                # partial 256 x 256 pair tiles both ways
 ])
 def test_wgrad_ragged_vs_oracle(cuda_dev, splits, n, k):
     import moe_b200
@@ -418,12 +419,14 @@ def test_bad_arguments(cuda_dev):
         moe_b200.grouped_gemm(x.float(), w, [8])
 
 
-@pytest.mark.parametrize("env", [{"MOE_GEMM_PAIR": "0"}, {"MOE_GEMM_SPLIT": "0"}],
+@pytest.mark.parametrize("env", [{"MOE_GEMM_PAIR": "0", "MOE_WGRAD_PAIR": "0"},
+                                 {"MOE_GEMM_SPLIT": "0"}],
                          ids=["single_cta", "pair_padded_tails"])
 def test_kernel_variants(cuda_dev, env):
     """The non-default kernel paths, each in a fresh process, on ragged groups
     with the bf16, SwiGLU and fp32 epilogues: the single-CTA kernel alone (used
-    when CTA pairs cannot be scheduled, or with MOE_GEMM_PAIR=0), and the pair
+    when CTA pairs cannot be scheduled, or with MOE_GEMM_PAIR=0; with
+    MOE_WGRAD_PAIR=0 the wgrad's single-CTA kernel too), and the pair
     kernel with each group's last partial tile padded to 256 rows instead of
     handed to the single-CTA kernel (MOE_GEMM_SPLIT=0)."""
     import os
@@ -449,6 +452,10 @@ np.testing.assert_allclose(f.cpu().numpy(), fp32_ref(u16(x), u16(w), splits), rt
 wt = _rand_bf16(g, 8, 256, 384, std=0.05)  # [G,K,N]: dgrad form, weight staged MN-major
 d = moe_b200.grouped_gemm(x.to(dev), wt.to(dev), splits, w_layout="KN")
 assert_gemm_close(d, fp32_ref(u16(x), u16(wt), splits, w_layout="KN"), "variant KN")
+from test_gpu_gemm import _wgrad_f32
+dy = _rand_bf16(g, sum(splits), 384)
+dw = moe_b200.grouped_wgrad(dy.to(dev), x.to(dev), splits)
+assert_gemm_close(dw, _wgrad_f32(u16(dy), u16(x), splits), "variant wgrad")
 print("OK")
 '''
     env = dict(os.environ, **env)
