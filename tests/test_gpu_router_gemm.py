@@ -74,6 +74,23 @@ def test_fused_router_equals_router_on_its_logits(cuda_dev, t, h, e, k, score, r
     assert moe_b200.router_device_error(cuda_dev) == 0
 
 
+@pytest.mark.parametrize("e,k,renorm", [(96, 8, True), (320, 8, False), (256, 16, True)])
+def test_fused_router_several_tiles_per_pair(cuda_dev, e, k, renorm):
+    """More 256-token tiles than CTA pairs (40000 tokens: 157 tiles), so each
+    pair walks several tiles: accumulator reuse (one accumulator at E=320, two
+    at E<=256) and the per-quadrant list hand-over across tiles."""
+    import moe_b200
+    t, h = 40000, 512
+    x, w = _inputs(cuda_dev, t, h, e, seed=e + k)
+    g = torch.Generator().manual_seed(3)
+    bias = (torch.randn(e, generator=g) * 0.5).to(cuda_dev)
+    _, lg = _check_against_router(moe_b200, x, w, k, "softmax", renorm, bias)
+    rows = np.unique(np.concatenate([[0, 255, 256, t // 2, t - 1],
+                                     np.random.default_rng(4).integers(0, t, 59)]))
+    _logits_bound_check(x, w, lg, rows)
+    assert moe_b200.router_device_error(cuda_dev) == 0
+
+
 def test_fused_router_case38_golden(cuda_dev, golden):
     """Logits-only call vs the reference's reference_fp32 golden (case38)."""
     import moe_b200
