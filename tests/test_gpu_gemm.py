@@ -244,6 +244,20 @@ def test_wgrad_ragged_vs_oracle(cuda_dev, splits, n, k):
             assert int(dw[gi].view(torch.int16).abs().sum()) == 0  # zeros, like torch.mm
 
 
+def test_wgrad_pair_kernel_many_tiles(cuda_dev):
+    """Deep groups (the CTA-pair wgrad kernel) with more 256 x 256 tiles than
+    CTA pairs, so every pair walks several tiles and groups: checked in full."""
+    import moe_b200
+    g = torch.Generator().manual_seed(77)
+    splits = [600, 700, 0, 523, 640]
+    n, k = 1024, 2048
+    dy = _rand_bf16(g, sum(splits), n)
+    x = _rand_bf16(g, sum(splits), k)
+    dw = moe_b200.grouped_wgrad(dy.to(cuda_dev), x.to(cuda_dev), splits)
+    assert_gemm_close(dw, _wgrad_f32(u16(dy), u16(x), splits), "pair wgrad")
+    assert int(dw[2].view(torch.int16).abs().sum()) == 0
+
+
 def test_wgrad_reference_shape_spot_check(cuda_dev):
     """case09's traced shape: 40 groups over 4096 rows, N=5120, K=8192;
     dW[g] checked on sampled 64 x 64 blocks of sampled groups."""
