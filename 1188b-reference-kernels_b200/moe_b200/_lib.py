@@ -61,6 +61,9 @@ _SIGNATURES = {
                                        c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p],
     "moe_permute_backward": [c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
                              c_int64, c_int64, c_int64, c_int64, c_void_p],
+    "moe_combine_backward": [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                             c_int64, c_int64, c_int64, c_int64, c_void_p],
+    "moe_swiglu_backward": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_void_p],
     "moe_grouped_gemm_workspace_size": [c_int64, POINTER(c_size_t)],
     "moe_grouped_gemm_plan_splits": [c_void_p, c_int64, c_int64, c_void_p, c_size_t, c_void_p],
     "moe_grouped_gemm_plan_ep": [c_void_p, c_int64, c_int64, c_void_p, c_size_t, c_void_p],
@@ -102,6 +105,7 @@ _LAUNCHES = {"moe_topk_f32": 1, "moe_router_topk": 1, "moe_router_topk_placed": 
              "moe_permute_mask_map": 1, "moe_permute_mask_map_trans": 1, "moe_unpermute_mask": 1,
              "moe_unpermute_mask_token_major": 1, "moe_ep_dispatch": 1, "moe_ep_combine": 1,
              "moe_permute_backward": 1, "moe_ep_dispatch_dedup": 1, "moe_ep_expand": 1,
+             "moe_combine_backward": 1, "moe_swiglu_backward": 1,
              "moe_grouped_gemm_plan_splits": 1, "moe_grouped_gemm_plan_ep": 1,
              "moe_grouped_gemm": 2, "moe_grouped_gemm_nn": 2, "moe_grouped_wgrad": 1,
              "moe_swiglu": 1}

@@ -81,10 +81,15 @@ class MoELayer:
 
     def forward(self, x: torch.Tensor, logits: Optional[torch.Tensor] = None,
                 return_intermediates: bool = False,
-                router_weight: Optional[torch.Tensor] = None):
+                router_weight: Optional[torch.Tensor] = None,
+                save_for_backward: bool = False):
         """logits [T,E] fp32, or router_weight [E,H] bf16: then the router gate
         GEMM and the router run as one kernel (ops.router_gemm_topk) where it
-        covers the shape, else as ops.router_logits + ops.router_topk."""
+        covers the shape, else as ops.router_logits + ops.router_topk.
+
+        save_for_backward: return (out, ctx) with what backward() needs; fc1
+        then keeps its gate|up output (GEMM with a plain epilogue followed by
+        the SwiGLU kernel, the same bits as the fused epilogue)."""
         t, h = x.shape
         e = self.w.num_experts
         if h != self.w.hidden:
@@ -112,17 +117,50 @@ class MoELayer:
         xp, _ = ops.permute(x, rim.map_te, None, num_out=rows)
         self._ev("permute")
         self.plan.from_splits(rim.counts, 1)
-        hmid = ops.grouped_gemm(xp, self.w.w1, epilogue="swiglu", plan=self.plan)
+        y1 = None
+        if save_for_backward:
+            y1 = ops.grouped_gemm(xp, self.w.w1, plan=self.plan)
+            hmid = ops.swiglu(y1)
+        else:
+            hmid = ops.grouped_gemm(xp, self.w.w1, epilogue="swiglu", plan=self.plan)
         self._ev("fc1")
         y = ops.grouped_gemm(hmid, self.w.w2, plan=self.plan)
         self._ev("fc2")
         out = ops.unpermute(y, rim.map_te, r.probs, probs_mode="dense", token_major=True)
         self._ev("combine")
-        if return_intermediates:
-            return out, dict(routing=r, rim=rim, xp=xp, h=hmid, y=y)
+        if return_intermediates or save_for_backward:
+            return out, dict(routing=r, rim=rim, xp=xp, y1=y1, h=hmid, y=y)
         return out
 
     __call__ = forward
+
+    def backward(self, grad_out: torch.Tensor, ctx: dict):
+        """Backward of one forward(..., save_for_backward=True), given the
+        output gradient grad_out [T,H] bf16. Returns (grad_x [T,H] bf16,
+        grad_probs [T,E] fp32 (the gradient of the dense gate matrix, zero
+        where a token is not routed), dw1 [E,2F,H] bf16, dw2 [E,H,F] bf16).
+
+        The chain, every GEMM grouped by expert on the forward's row layout:
+        combine backward -> fc2 dgrad (dh = dy2 @ W2[e]) and wgrad
+        (dW2[e] = dy2^T @ h) -> SwiGLU backward -> fc1 dgrad (dxp = dy1 @
+        W1[e]) and wgrad (dW1[e] = dy1^T @ xp) -> permute backward (grad_x[t]
+        = sum over the token's experts of dxp rows). The router's own backward
+        (through softmax, top-k and renormalisation) is the caller's."""
+        if ctx.get("y1") is None:
+            raise ValueError("ctx must come from forward(..., save_for_backward=True)")
+        r, rim = ctx["routing"], ctx["rim"]
+        t, h = ctx["xp"].shape[0] // self.k, ctx["xp"].shape[1]
+        if grad_out.shape != (t, h):
+            raise ValueError(f"grad_out must be [{t},{h}]")
+        splits = rim.counts.cpu().tolist()  # host row counts for the wgrad tensor maps
+        dy2, grad_probs = ops.combine_backward(grad_out, ctx["y"], rim.map_te, r.probs)
+        dh = ops.grouped_gemm(dy2, self.w.w2, plan=self.plan, w_layout="KN")
+        dw2 = ops.grouped_wgrad(dy2, ctx["h"], splits)
+        dy1 = ops.swiglu_backward(ctx["y1"], dh)
+        dxp = ops.grouped_gemm(dy1, self.w.w1, plan=self.plan, w_layout="KN")
+        dw1 = ops.grouped_wgrad(dy1, ctx["xp"], splits)
+        grad_x = ops.unpermute(dxp, rim.map_te, None, token_major=True)
+        return grad_x, grad_probs, dw1, dw2
 
 
 def moe_layer_fwd(x: torch.Tensor, logits: torch.Tensor, w1: torch.Tensor, w2: torch.Tensor,

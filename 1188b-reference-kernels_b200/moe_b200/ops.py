@@ -23,7 +23,7 @@ __all__ = [
     "topk", "router_topk", "RouterOutput", "row_id_map", "RowIdMap", "permute",
     "permute_trans", "unpermute", "unpermute_weighted", "grouped_gemm", "GroupedGemmPlan",
     "grouped_wgrad", "swiglu", "router_logits", "router_gemm_topk", "router_gemm_fusable",
-    "router_device_error", "permute_backward",
+    "router_device_error", "permute_backward", "combine_backward", "swiglu_backward",
 ]
 
 
@@ -442,6 +442,51 @@ def permute_backward(grad_permuted: torch.Tensor, row_id_map: torch.Tensor,
     _lib.call("moe_permute_backward", _p(gc), _p(mc), 64 if mc.dtype == torch.int64 else 32,
               _p(pg), _p(gx), _p(acc), _p(gp), t, h, e, rows, _stream(gc.device))
     return (acc, gx, gp) if return_acc else (gx, gp)
+
+
+def combine_backward(grad_out: torch.Tensor, rows: torch.Tensor, row_id_map: torch.Tensor,
+                     probs: torch.Tensor):
+    """Backward of the prob-weighted combine out[t] = sum_e probs[t,e] *
+    rows[row_id_map[t,e]] (token-major [T,E] int64 map, dense probs [T,E]):
+    grad_rows[row_id_map[t,e]] = bf16(probs[t,e] * grad_out[t]) and
+    grad_probs[t,e] = <grad_out[t], rows[row_id_map[t,e]]> (fp32), 0 where the
+    token is not routed. Returns (grad_rows [R,H] bf16, grad_probs [T,E] fp32).
+    Rows no token references stay uninitialised."""
+    for n_, t_ in (("grad_out", grad_out), ("rows", rows), ("row_id_map", row_id_map),
+                   ("probs", probs)):
+        _need_cuda(n_, t_)
+    _need_dtype("grad_out", grad_out, torch.bfloat16)
+    _need_dtype("rows", rows, torch.bfloat16)
+    _need_dtype("row_id_map", row_id_map, torch.int64)
+    _need_dtype("probs", probs, torch.float32)
+    if grad_out.dim() != 2 or rows.dim() != 2 or rows.shape[1] != grad_out.shape[1]:
+        raise ValueError(f"shapes grad_out {tuple(grad_out.shape)} rows {tuple(rows.shape)}")
+    t, h = grad_out.shape
+    if row_id_map.shape[0] != t or probs.shape != row_id_map.shape:
+        raise ValueError("row_id_map and probs must both be [T,E]")
+    e = row_id_map.shape[1]
+    go, rc, mc, pc = (v.contiguous() for v in (grad_out, rows, row_id_map, probs))
+    grad_rows = torch.empty_like(rc)
+    grad_probs = torch.empty((t, e), dtype=torch.float32, device=go.device)
+    _lib.call("moe_combine_backward", _p(go), _p(rc), _p(mc), _p(pc), _p(grad_rows),
+              _p(grad_probs), t, h, e, rc.shape[0], _stream(go.device))
+    return grad_rows, grad_probs
+
+
+def swiglu_backward(y: torch.Tensor, dh: torch.Tensor) -> torch.Tensor:
+    """Backward of h = silu(g) * u for y = [g | u] [M,2F] bf16 and dh [M,F]
+    bf16: returns dy = [dh * u * silu'(g) | dh * silu(g)] [M,2F] bf16."""
+    _need_cuda("y", y)
+    _need_cuda("dh", dh)
+    _need_dtype("y", y, torch.bfloat16)
+    _need_dtype("dh", dh, torch.bfloat16)
+    if y.dim() != 2 or dh.dim() != 2 or y.shape[0] != dh.shape[0] or y.shape[1] != 2 * dh.shape[1]:
+        raise ValueError(f"shapes y {tuple(y.shape)} dh {tuple(dh.shape)}")
+    yc, dc = y.contiguous(), dh.contiguous()
+    dy = torch.empty_like(yc)
+    _lib.call("moe_swiglu_backward", _p(yc), _p(dc), _p(dy), yc.shape[0], dc.shape[1],
+              _stream(yc.device))
+    return dy
 
 
 def grouped_wgrad(dy: torch.Tensor, x: torch.Tensor,

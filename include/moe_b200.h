@@ -172,6 +172,24 @@ int moe_permute_backward(const void* grad_permuted, const void* row_id_map_et, i
                          float* grad_probs, int64_t T, int64_t H, int64_t E, int64_t num_rows,
                          moe_stream_t stream);
 
+/* f3  Backward of the prob-weighted combine (the forward is                 */
+/* moe_unpermute_mask_token_major with dense probs; no reference kernel,     */
+/* the chain rule of out[t] = sum_e probs[t,e] * rows[map[t,e]]):            */
+/*   grad_rows[map[t,e]] = bf16(probs[t,e] * grad_out[t])                    */
+/*   grad_probs[t,e] = <grad_out[t], rows[map[t,e]]> in fp32, 0 if unrouted. */
+/* grad_out [T,H] bf16, rows [num_rows,H] bf16 (the forward's fc2 output),   */
+/* row_id_map_te [T,E] int64, probs [T,E] fp32; E <= 1024. Rows that no      */
+/* token references are not written.                                         */
+int moe_combine_backward(const void* grad_out, const void* rows, const int64_t* row_id_map_te,
+                         const float* probs, void* grad_rows, float* grad_probs, int64_t T,
+                         int64_t H, int64_t E, int64_t num_rows, moe_stream_t stream);
+
+/* f3  Backward of SwiGLU (h = silu(g) * u, y = [g | u] per row):            */
+/* dy = [dh * u * silu'(g) | dh * silu(g)] in fp32 from bf16 inputs, rounded */
+/* to bf16. y [M,2F], dh [M,F], dy [M,2F] bf16, F % 8 == 0, 16-byte aligned. */
+int moe_swiglu_backward(const void* y, const void* dh, void* dy, int64_t M, int64_t F,
+                        moe_stream_t stream);
+
 /* Same combine driven by the token-major [T,E] int64 map (the layout         */
 /* kernel_cases/case12_moe_row_id_map_pass2.py:61 returns second), whose     */
 /* entries for one token are contiguous. Identical results. E <= 1024.       */

@@ -293,6 +293,68 @@ def grouped_wgrad(dy_u16: np.ndarray, x_u16: np.ndarray, m_splits) -> np.ndarray
     return out
 
 
+def combine_backward(grad_out_u16: np.ndarray, rows_u16: np.ndarray, row_te: np.ndarray,
+                     probs: np.ndarray):
+    """Backward of the prob-weighted combine out[t] = sum_e probs[t,e] *
+    rows[row_te[t,e]] (no reference kernel; the chain rule of the build's
+    weighted combine, as torch.autograd forms it):
+    grad_rows[r] = bf16(probs[t,e] * grad_out[t]) for r = row_te[t,e],
+    grad_probs[t,e] = <grad_out[t], rows[r]> (fp32; 0 where not routed).
+    Returns (grad_rows bf16 bits [R,H], grad_probs fp32 [T,E])."""
+    g = bf16_to_f32(grad_out_u16)
+    rows = bf16_to_f32(rows_u16)
+    t, e = row_te.shape
+    grad_rows = np.zeros(rows_u16.shape, np.uint16)
+    grad_probs = np.zeros((t, e), np.float32)
+    ti, ei = np.nonzero(row_te >= 0)
+    r = row_te[ti, ei]
+    p = probs[ti, ei].astype(np.float32)[:, None]
+    grad_rows[r] = f32_to_bf16((p * g[ti]).astype(np.float32))
+    grad_probs[ti, ei] = np.einsum("ij,ij->i", g[ti].astype(np.float64),
+                                   rows[r].astype(np.float64)).astype(np.float32)
+    return grad_rows, grad_probs
+
+
+def swiglu_backward(y_u16: np.ndarray, dh_u16: np.ndarray) -> np.ndarray:
+    """Backward of h = silu(g) * u, y = [g | u]: dg = dh * u * silu'(g),
+    du = dh * silu(g), silu'(g) = s (1 + g (1 - s)), s = sigmoid(g); fp32
+    from bf16 inputs, bf16 out (no reference; SwiGLU is only named upstream)."""
+    f = dh_u16.shape[1]
+    g = bf16_to_f32(y_u16[:, :f])
+    u = bf16_to_f32(y_u16[:, f:])
+    d = bf16_to_f32(dh_u16)
+    den = (np.float32(1.0) + np.exp(-g, dtype=np.float32)).astype(np.float32)
+    sig = (np.float32(1.0) / den).astype(np.float32)
+    silu = (g / den).astype(np.float32)
+    dsilu = (sig * (np.float32(1.0) + g * (np.float32(1.0) - sig))).astype(np.float32)
+    dg = (d * u * dsilu).astype(np.float32)
+    du = (d * silu).astype(np.float32)
+    return np.concatenate([f32_to_bf16(dg), f32_to_bf16(du)], axis=1)
+
+
+def moe_layer_backward(x_u16, logits, w1_u16, w2_u16, k, grad_out_u16, bias=None, renorm=True):
+    """Backward of moe_layer for the output gradient grad_out, with the same
+    bf16 roundings as the device chain (every GEMM output and every
+    elementwise result rounded to bf16): combine backward -> fc2 dgrad and
+    wgrad -> SwiGLU backward -> fc1 dgrad and wgrad -> permute backward.
+    Returns (grad_x bf16 bits [T,H], grad_probs fp32 [T,E], dw1 bf16 bits
+    [E,2F,H], dw2 bf16 bits [E,H,F])."""
+    _, _, rmap, probs = router(logits, k, bias, "softmax", renorm)
+    map_et, map_te, counts, num_out = row_id_map(rmap)
+    xp, _ = permute(x_u16, map_te, None, num_out)
+    y1 = grouped_gemm(xp, w1_u16, counts)
+    h = swiglu(y1)
+    y = grouped_gemm(h, w2_u16, counts)
+    dy2, grad_probs = combine_backward(grad_out_u16, y, map_te, probs)
+    dh = grouped_gemm(dy2, w2_u16, counts, w_layout="KN")
+    dw2 = grouped_wgrad(dy2, h, counts)
+    dy1 = swiglu_backward(y1, dh)
+    dxp = grouped_gemm(dy1, w1_u16, counts, w_layout="KN")
+    dw1 = grouped_wgrad(dy1, xp, counts)
+    _, grad_x, _ = permute_backward(dxp, map_et)
+    return grad_x, grad_probs, dw1, dw2
+
+
 def router_logits(x_u16: np.ndarray, w_u16: np.ndarray) -> np.ndarray:
     """Router gate GEMM, logits fp32 = x @ w.T accumulated in fp32, unrounded.
 
