@@ -443,6 +443,24 @@ def run_backward(a):
     sampler.mark(wall0, time.time())
     launches = _lib.launch_count - launches0
     clocks = sampler.stop()
+    # The whole layer backward (MoELayer.backward: combine backward, the four
+    # GEMMs, SwiGLU backward, permute backward) on the same routing.
+    del dy, dz, xp, hm, dh, dx, dw2, dw1
+    layer = moe_b200.MoELayer(w, topk=k, expert_bias=zipf_bias(e, a.routing).to(dev))
+    x = torch.randn(t, h, device=dev, generator=g).to(torch.bfloat16)
+    go = torch.randn(t, h, device=dev, generator=g).to(torch.bfloat16)
+    _, ctx = layer.forward(x, logits, save_for_backward=True)
+    for _ in range(max(a.warmup, 1)):
+        layer.backward(go, ctx)
+    torch.cuda.synchronize()
+    lb0, lb1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    lb0.record()
+    for _ in range(a.steps):
+        layer.backward(go, ctx)
+    lb1.record()
+    torch.cuda.synchronize()
+    assert layer.plan.device_error() == 0
+    layer_bwd_ms = lb0.elapsed_time(lb1) / a.steps
     sec = {n: v / a.steps for n, v in zip(names, tot)}
     flops = {"fc2_dgrad": 2.0 * rows * h * f, "fc2_wgrad": 2.0 * rows * h * f,
              "fc1_dgrad": 2.0 * rows * 2 * f * h, "fc1_wgrad": 2.0 * rows * 2 * f * h}
@@ -465,6 +483,7 @@ def run_backward(a):
             "stages_ms": {n: round(v * 1e3, 4) for n, v in sec.items()},
             "stage_tflops": {n: round(flops[n] / sec[n] / 1e12, 1) for n in names},
             "wgrad_write_gbs": round(wg_bytes / (sec["fc1_wgrad"] + sec["fc2_wgrad"]) / 1e9, 1),
+            "layer_backward_ms": round(layer_bwd_ms, 3),
             "hbm_peak_gbs": hbm, "peak_kind": f"bf16 sustained, of {peak_kind}",
             "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clocks}
     print(json.dumps(line), flush=True)
