@@ -152,7 +152,11 @@ class MoELayer:
         t, h = ctx["xp"].shape[0] // self.k, ctx["xp"].shape[1]
         if grad_out.shape != (t, h):
             raise ValueError(f"grad_out must be [{t},{h}]")
-        splits = rim.counts.cpu().tolist()  # host row counts for the wgrad tensor maps
+        # The group table of this forward's routing (another forward since may
+        # have replaced the layer's), and its row counts on the host for the
+        # wgrad tensor maps.
+        self.plan.from_splits(rim.counts, 1)
+        splits = rim.counts.cpu().tolist()
         dy2, grad_probs = ops.combine_backward(grad_out, ctx["y"], rim.map_te, r.probs)
         dh = ops.grouped_gemm(dy2, self.w.w2, plan=self.plan, w_layout="KN")
         dw2 = ops.grouped_wgrad(dy2, ctx["h"], splits)

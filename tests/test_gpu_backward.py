@@ -61,6 +61,8 @@ def test_layer_backward_vs_oracle(cuda_dev):
     out, ctx = layer.forward(x.to(cuda_dev), lg.to(cuda_dev), save_for_backward=True)
     # same output bits as the fused-SwiGLU forward
     assert torch.equal(out, layer(x.to(cuda_dev), lg.to(cuda_dev)))
+    # another forward in between (different routing) must not disturb ctx
+    layer(x.to(cuda_dev), torch.randn(t, e, generator=g).to(cuda_dev))
     gx, gp, dw1, dw2 = layer.backward(go.to(cuda_dev), ctx)
     torch.cuda.synchronize()
     assert layer.plan.device_error() == 0
