@@ -80,6 +80,16 @@ def test_invalid_arguments_are_rejected_without_launch(lib):
     assert rg(16, 16, None, 16, 60, 64, 4, 1, 1, None, None, None, 16, 16, 16, None) == 1
     assert rg(16, 16, None, 16, 64, 64, 4, 2, 1, None, None, None, 16, 16, 16, None) == 1
     assert rg(None, None, None, 0, 64, 64, 4, 1, 1, None, None, None, None, None, 16, None) == 0
+    # backward of the combine and of SwiGLU
+    cb = lib.moe_combine_backward
+    assert cb(16, 16, 16, 16, 16, 16, 4, 8, 2048, 8, None) == 1  # E above 1024
+    assert cb(None, None, None, None, None, None, 4, 8, 4, 8, None) == 1  # null pointers
+    assert cb(None, None, None, None, None, None, 0, 8, 4, 0, None) == 0  # no tokens
+    sb = lib.moe_swiglu_backward
+    assert sb(16, 16, 16, 4, 12, None) == 1  # F not a multiple of 8
+    assert b"multiple of 8" in lib.moe_b200_last_error()
+    assert sb(17, 16, 16, 4, 16, None) == 1  # misaligned
+    assert sb(None, None, None, 0, 16, None) == 0
 
 
 def test_ops_refuse_cpu_tensors():
@@ -105,6 +115,13 @@ def test_ops_refuse_cpu_tensors():
     with pytest.raises(ValueError):
         moe_b200.permute_backward(torch.zeros(4, 8, dtype=torch.bfloat16),
                                   torch.zeros(2, 4, dtype=torch.int64))
+    with pytest.raises(ValueError):
+        moe_b200.combine_backward(torch.zeros(4, 8, dtype=torch.bfloat16),
+                                  torch.zeros(8, 8, dtype=torch.bfloat16),
+                                  torch.zeros(4, 2, dtype=torch.int64), torch.zeros(4, 2))
+    with pytest.raises(ValueError):
+        moe_b200.swiglu_backward(torch.zeros(4, 16, dtype=torch.bfloat16),
+                                 torch.zeros(4, 8, dtype=torch.bfloat16))
 
 
 def test_product_package_does_not_import_oracle():
