@@ -128,3 +128,21 @@ def test_product_package_does_not_import_oracle():
     pat = re.compile(r"^\s*(from\s+oracle\b|import\s+oracle\b)|moe_oracle", re.M)
     for p in PKG.rglob("*.py"):
         assert not pat.search(p.read_text()), p
+
+
+def test_plain_c_consumer(lib, tmp_path):
+    """The header and library are usable from C alone: gcc compiles
+    tests/capi_consumer.c against include/moe_b200.h (no CUDA headers) and
+    links the built library; the program checks calls that need no GPU."""
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc")
+    if gcc is None:
+        pytest.skip("gcc not available")
+    libdir = PKG / "lib"
+    exe = tmp_path / "capi_consumer"
+    subprocess.run([gcc, "-std=c99", "-Wall", "-Werror", f"-I{ROOT / 'include'}",
+                    str(ROOT / "tests" / "capi_consumer.c"), f"-L{libdir}", "-lmoe_b200",
+                    f"-Wl,-rpath,{libdir}", "-o", str(exe)], check=True, timeout=120)
+    r = subprocess.run([str(exe)], capture_output=True, text=True, timeout=60)
+    assert r.returncode == 0 and "C consumer OK" in r.stdout, r.stdout + r.stderr
