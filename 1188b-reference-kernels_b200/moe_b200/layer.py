@@ -138,7 +138,8 @@ class MoELayer:
         """Backward of one forward(..., save_for_backward=True), given the
         output gradient grad_out [T,H] bf16. Returns (grad_x [T,H] bf16,
         grad_probs [T,E] fp32 (the gradient of the dense gate matrix, zero
-        where a token is not routed), dw1 [E,2F,H] bf16, dw2 [E,H,F] bf16).
+        where a token is not routed; columns in slot order when the layer has
+        a placement), dw1 [E,2F,H] bf16, dw2 [E,H,F] bf16).
 
         The chain, every GEMM grouped by expert on the forward's row layout:
         combine backward -> fc2 dgrad (dh = dy2 @ W2[e]) and wgrad
