@@ -568,8 +568,14 @@ extern "C" int moe_row_id_map(const uint8_t* routing_map, int64_t T, int64_t E, 
 // Host code cannot pass the array's name to a kernel (on the host it is only
 // a stand-in symbol, not a device address), so the first call on each device
 // looks up the real address with cudaGetSymbolAddress, with that device
-// current, and caches it. That first call should therefore happen before any
-// stream capture.
+// current, and caches it for the life of the process. That first call should
+// therefore happen before any stream capture, and the library must not be
+// used across a cudaDeviceReset of the device (the cached address would be
+// that of the destroyed context).
+//
+// A call needs roundup(E * ceil(T/64) * 4, 256) bytes of per-chunk counts plus
+// roundup(E * 8, 256) bytes of expert offsets; at E = 256 that fits for
+// T <= 65408 tokens.
 //
 // All calls on a device share the one array and it keeps whatever the last
 // call left there. Nothing in it needs to start at zero: the count kernel

@@ -117,10 +117,14 @@ int moe_row_id_map(const uint8_t* routing_map, int64_t T, int64_t E, int64_t ali
 /* memory (a runtime that owns a fixed HBM budget, or a path where          */
 /* cudaMalloc's implicit synchronisation is not allowed). No counterpart in  */
 /* the reference. Its scratch is a 1 MiB file-scope device array held by     */
-/* every GPU that loads the library; sizes needing more are rejected with    */
-/* MOE_ERR_INVALID (at E=256 that is T > about 63000 tokens). The first call */
-/* on a device looks the array's address up (do it before any stream         */
-/* capture). Calls share the array: calls that overlap on the GPU race.      */
+/* every GPU that loads the library. A call needs                           */
+/*   roundup(E * ceil(T/64) * 4, 256) + roundup(E * 8, 256) <= 1 MiB         */
+/* bytes of it (at E=256: T <= 65408); larger sizes are rejected with        */
+/* MOE_ERR_INVALID before any device work. The first call on a device looks  */
+/* the array's address up and caches it for the life of the process (make   */
+/* that call before any stream capture, and do not use the library across a */
+/* cudaDeviceReset of that device). Calls share the array: calls that        */
+/* overlap on the GPU race.                                                  */
 int moe_row_id_map_static_scratch(const uint8_t* routing_map, int64_t T, int64_t E,
                                   int64_t align, int64_t* row_id_map_et, int64_t* row_id_map_te,
                                   int32_t* expert_counts, int64_t* num_out, moe_stream_t stream);

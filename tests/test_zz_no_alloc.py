@@ -4,7 +4,8 @@ It serves callers that may not allocate device memory when they build the
 routing maps (a runtime that owns a fixed HBM budget, or a path where
 cudaMalloc's implicit synchronisation is not allowed): its scratch is a
 1 MiB device array inside the library. The GPU test calls it through the C
-ABI twice in a row, on different problem sizes, and checks every output
+ABI several times in a row, on different problem sizes (up to the largest
+the array accepts), and checks every output
 against the workspace-based moe_row_id_map (integer outputs: bit-exact, the
 tolerance used for all map tests). This file is collected last so that a
 stop-at-first-failure run has already run every other test.
@@ -35,9 +36,14 @@ def test_static_scratch_matches_workspace_entry_point(cuda_dev):
     lib = _lib()
     stream = torch.cuda.current_stream(cuda_dev).cuda_stream
     g = torch.Generator().manual_seed(2024)
-    # Two calls in a row: the second is smaller and reuses the same scratch,
-    # so stale counts from the first call would show up in its maps.
-    for t, e, align, p in ((16384, 256, 1, 8 / 256), (777, 300, 16, 0.05), (16384, 256, 128, 0.03)):
+    # Calls in a row on the one shared array: each later call is smaller than
+    # some earlier one, so stale counts left behind would show up in its maps.
+    # (65408, 256) is the largest size the 1 MiB array accepts at E=256 (its
+    # scratch ends exactly at the array's end); (64, 4096) takes the
+    # single-block expert scan used for E > 2048.
+    for t, e, align, p in ((16384, 256, 1, 8 / 256), (777, 300, 16, 0.05),
+                           (65408, 256, 1, 8 / 256), (16384, 256, 128, 0.03),
+                           (64, 4096, 1, 0.002)):
         rm = (torch.rand(t, e, generator=g) < p).to(cuda_dev)
         et_s, te_s, c_s, n_s = _outputs(t, e, cuda_dev)
         st = lib.moe_row_id_map_static_scratch(rm.data_ptr(), t, e, align, et_s.data_ptr(),
@@ -63,8 +69,9 @@ def test_static_scratch_rejects_sizes_beyond_the_array():
     """Rejected before any device work, so this runs without a GPU."""
     lib = _lib()
     dummy = 256  # never dereferenced: the size check comes first
-    st = lib.moe_row_id_map_static_scratch(dummy, 1 << 17, 256, 1, dummy, dummy, dummy, dummy,
-                                           None)
-    assert st == 1
-    msg = lib.moe_b200_last_error()
-    assert b"static array" in msg and b"moe_row_id_map" in msg
+    for t in (1 << 17, 65409):  # far past the limit, and one token past it at E=256
+        st = lib.moe_row_id_map_static_scratch(dummy, t, 256, 1, dummy, dummy, dummy, dummy,
+                                               None)
+        assert st == 1, t
+        msg = lib.moe_b200_last_error()
+        assert b"static array" in msg and b"moe_row_id_map" in msg
