@@ -86,7 +86,8 @@ struct Params {
   int k_rows;    // K: reduction rows of one weight matrix when b_mn
   int epilogue;  // 0 bf16 out, 1 SwiGLU -> bf16, 2 fp32 out
   int raster;   // pair kernel: pair M-tiles per raster super-row
-  int l2_mode;  // pair kernel: 0 both evict_normal, 1 B evict_first, 2 A evict_last + B evict_first
+  int l2_mode;  // pair kernel: 0 both evict_normal, 1 B evict_first, 2 A evict_last + B evict_first,
+                //   3 A evict_first + B evict_last, 4 B evict_last
 };
 
 struct Tile {
@@ -536,9 +537,16 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (lane == 0) {
       // Weight slabs are read by the few M-tiles of one super-row and then not
       // again until the next super-row; activation rows are reused by every
-      // N-tile of the super-row. Mode 1/2 let L2 drop the weights first.
-      const uint64_t pol_a = p.l2_mode == 2 ? l2_policy_evict_last() : l2_policy_evict_normal();
-      const uint64_t pol_b = p.l2_mode >= 1 ? l2_policy_evict_first() : l2_policy_evict_normal();
+      // N-tile of the super-row. Mode 1/2 let L2 drop the weights first;
+      // modes 3/4 keep them (with one-M-tile super-rows every M-tile of a
+      // group reads the whole weight slab, while its rows die after the
+      // group's N-tiles, which run at about the same time).
+      const uint64_t pol_a = p.l2_mode == 2   ? l2_policy_evict_last()
+                             : p.l2_mode == 3 ? l2_policy_evict_first()
+                                              : l2_policy_evict_normal();
+      const uint64_t pol_b = (p.l2_mode == 1 || p.l2_mode == 2) ? l2_policy_evict_first()
+                             : p.l2_mode >= 3                  ? l2_policy_evict_last()
+                                                               : l2_policy_evict_normal();
       int stage = 0;
       uint32_t phase = 0;
       int issued[pairk::kPairStages];
@@ -1140,7 +1148,7 @@ static int grouped_gemm_run(const void* x, const void* w, void* out, int64_t x_r
   p.k_rows = static_cast<int>(K);
   p.num_kb = static_cast<int>((K + gg::BK - 1) / gg::BK);
   static const int raster = gg::env_int("MOE_GEMM_RASTER", gg::pairk::kPairRaster, 1, 64);
-  static const int l2_mode = gg::env_int("MOE_GEMM_L2", 0, 0, 2);
+  static const int l2_mode = gg::env_int("MOE_GEMM_L2", 0, 0, 4);
   p.raster = raster;
   p.l2_mode = l2_mode;
 

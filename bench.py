@@ -50,7 +50,7 @@ def resolve_transport(transport: str, world: int) -> str:
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["b200", "reference"], default="b200")
     ap.add_argument("--tokens", type=int, default=16384, help="tokens per GPU")
@@ -63,6 +63,12 @@ def parse_args():
                     help="token sample of the CPU baseline (per step for --impl reference)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-check", action="store_true",
+                    help="skip the post-timing correctness check of the expert-parallel layer "
+                         "(the single-GPU layer is always checked)")
+    ap.add_argument("--settle-s", type=float, default=2.0,
+                    help="untimed layer steps after the warm-up, in seconds of GPU time, so "
+                         "the timed windows run at the power-capped sustained clock")
     ap.add_argument("--placement", choices=["balanced", "contiguous"], default="balanced",
                     help="EP expert placement: load-balanced (E/G experts per GPU, chosen from "
                          "the routing of the benchmark's own logits) or contiguous id ranges")
@@ -119,9 +125,10 @@ def zipf_bias(e, routing):
 class ClockSampler:
     """nvidia-smi clock/throttle sampling (50 ms) around the measurement.
 
-    Samples are time-stamped on the host; the summary uses the samples that
-    fall inside the device-timed window, or, when that window is shorter than
-    the sampling period, the whole measurement (warm-up + timed + e2e steps).
+    Samples are time-stamped on the host. Each timed window is marked with a
+    label (device-only or e2e); the summary covers the samples inside all
+    marked windows (or the whole run when no sample falls inside one) and
+    gives the median SM clock of every label separately.
     """
     FIELDS = ("timestamp,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
@@ -132,7 +139,7 @@ class ClockSampler:
         self.device_index = device_index
         self.proc = None
         self.path = None
-        self.window = None
+        self.windows = []  # (label, t0, t1)
 
     def start(self):
         try:
@@ -148,8 +155,15 @@ class ClockSampler:
         except Exception:
             self.proc = None
 
-    def mark(self, t0, t1):
-        self.window = (t0, t1)
+    def mark(self, t0, t1, label="device"):
+        self.windows.append((label, t0, t1))
+
+    @staticmethod
+    def _num(v):
+        try:
+            return float(v)
+        except ValueError:
+            return None
 
     def stop(self):
         if self.proc is None:
@@ -174,26 +188,32 @@ class ClockSampler:
         os.unlink(self.path)
         if not rows:
             return None
-        scope = "bench run"
-        if self.window:
-            inside = [r for r in rows if r[0] is not None and
-                      self.window[0] - 0.05 <= r[0] <= self.window[1] + 0.05]
-            if inside:
-                rows, scope = inside, "timed window"
 
-        def num(v):
-            try:
-                return float(v)
-            except ValueError:
-                return None
-        sm = [v for v in (num(p[1]) for _, p in rows) if v is not None]
-        mx = [v for v in (num(p[2]) for _, p in rows) if v is not None]
-        pw = [v for v in (num(p[3]) for _, p in rows) if v is not None]
-        reasons = sorted({n for _, p in rows for n, v in zip(self.NAMES, p[5:9]) if v == "Active"})
-        return {"sm_mhz": statistics.median(sm) if sm else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
-                "samples": len(rows), "scope": scope,
-                "power_w_max": max(pw) if pw else None}
+        def inside(r, w):
+            return r[0] is not None and w[1] - 0.05 <= r[0] <= w[2] + 0.05
+
+        per = {}
+        for w in self.windows:
+            per.setdefault(w[0], []).extend(r for r in rows if inside(r, w))
+        timed = [r for r in rows if any(inside(r, w) for w in self.windows)]
+        scope = "timed windows"
+        if not timed:
+            timed, scope = rows, "bench run"
+        sm = [v for v in (self._num(p[1]) for _, p in timed) if v is not None]
+        mx = [v for v in (self._num(p[2]) for _, p in timed) if v is not None]
+        pw = [v for v in (self._num(p[3]) for _, p in timed) if v is not None]
+        reasons = sorted({n for _, p in timed for n, v in zip(self.NAMES, p[5:9]) if v == "Active"})
+        out = {"sm_mhz": statistics.median(sm) if sm else None,
+               "sm_max_mhz": max(mx) if mx else None, "reasons": reasons,
+               "samples": len(timed), "scope": scope,
+               "power_w_max": max(pw) if pw else None}
+        wins = {}
+        for label, rs in per.items():
+            v = [x for x in (self._num(p[1]) for _, p in rs) if x is not None]
+            wins[label] = {"sm_mhz": statistics.median(v) if v else None, "samples": len(v)}
+        if wins:
+            out["windows"] = wins
+        return out
 
 
 # --------------------------------------------------------------------------- CPU port
@@ -245,6 +265,48 @@ def cpu_threads():
     except Exception:
         pass
     return os.cpu_count() or 1
+
+
+def cpu_baseline_sample(a):
+    """The cpu_baseline object of the GPU arm's line: one bounded sample of the
+    layer on this host's cores."""
+    use_all_cores()
+    dt, n = cpu_layer_sample(a, a.cpu_tokens)
+    return {"value": n / dt, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+            "sample": f"{n} tokens of the {a.tokens}-token layer (same H/E/F/top-k, {a.routing} "
+                      f"routing), numpy restatement, expert weights from an fp32 pool of 8"}
+
+
+def check_ep(layer, x, logits, bias, w, k, placement, world, rank, dev):
+    """Expert-parallel check (outside the timed windows): every rank's EP output
+    equals, bit for bit, the single-GPU layer run on that rank with all
+    experts' weights (gathered from the ranks, slot order) and the same
+    placement; the single-GPU forward also passes check_layer. Collective:
+    every rank calls it."""
+    import torch
+    import torch.distributed as dist
+    import moe_b200
+    out_ep = layer(x, logits)
+    el = w.w1.shape[0]
+    w1_all = torch.empty((world * el,) + tuple(w.w1.shape[1:]), dtype=w.w1.dtype, device=dev)
+    w2_all = torch.empty((world * el,) + tuple(w.w2.shape[1:]), dtype=w.w2.dtype, device=dev)
+    dist.all_gather_into_tensor(w1_all, w.w1.contiguous())
+    dist.all_gather_into_tensor(w2_all, w.w2.contiguous())
+    full = moe_b200.MoELayer(moe_b200.MoEWeights(w1_all, w2_all), topk=k, expert_bias=bias,
+                             placement=placement)
+    out, mid = full.forward(x, logits, return_intermediates=True)
+    torch.cuda.synchronize()
+    same = bool(torch.equal(out, out_ep))
+    chk = check_layer(out, mid, x, logits, bias, w1_all, w2_all, k, placement)
+    derr = layer.plan.device_error() + full.plan.device_error()
+    ok = torch.tensor([1 if (same and chk["ok"] and derr == 0) else 0], device=dev)
+    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    del out, mid, full, w1_all, w2_all, out_ep
+    torch.cuda.empty_cache()
+    chk.update({"ok": bool(ok.item()), "ep_equals_single_gpu_rank0": same,
+                "scope": "every rank's tokens vs the single-GPU layer bit for bit (ok = all "
+                         "ranks); rank 0's details shown"})
+    return chk
 
 
 def run_reference_arm(a, world, rank):
@@ -556,6 +618,108 @@ def read_traffic():
     return None
 
 
+def layer_inputs(t, h, e, f, routing, dev, rank=0, num_w=None):
+    """The benchmark's seeded synthetic layer inputs on `dev` for rank `rank`:
+    x [t,h] bf16 ~N(0,1), router logits [t,e] fp32 ~N(0,1) (device generator,
+    seed 1000+rank), the Zipf expert bias and num_w experts' weights ~N(0,0.02)
+    (seed 77+rank). The full-size parity test builds the same inputs."""
+    import torch
+    import moe_b200
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000 + rank)
+    x = torch.randn(t, h, device=dev, generator=g).to(torch.bfloat16)
+    logits = torch.randn(t, e, device=dev, generator=g)
+    bias = zipf_bias(e, routing).to(dev)
+    w = moe_b200.MoEWeights.random(e if num_w is None else num_w, h, f, dev, seed=77 + rank)
+    return x, logits, bias, w
+
+
+def sample_tokens(counts, map_te, n_random=12, seed=0):
+    """Tokens whose outputs the check recomputes: the first and last token, a
+    token of the busiest expert, a token of the least-used expert that has
+    rows, and n_random seeded others."""
+    import torch
+    t = map_te.shape[0]
+    c = counts.to(torch.int64)
+    busiest = int(torch.argmax(c))
+    pos = torch.where(c > 0, c, torch.full_like(c, 1 << 40))
+    rarest = int(torch.argmin(pos))
+    picks = [0, t - 1]
+    for e_ in (busiest, rarest):
+        ts = torch.nonzero(map_te[:, e_] >= 0).flatten()
+        picks.append(int(ts[len(ts) // 2]))
+    g = torch.Generator().manual_seed(seed)
+    picks += torch.randint(0, t, (n_random,), generator=g).tolist()
+    return sorted(set(picks))
+
+
+def check_layer(out, mid, x, logits, bias, w1, w2, k, placement=None):
+    """Checks one layer forward against a plain torch reference computed on the
+    device (outside every timed region): the routing map (top-k of logits +
+    bias), the row_id_map (per-expert cumsum + exclusive offsets) and every
+    permuted row exactly; the gates within rtol 1e-5; and the outputs of
+    sampled tokens, recomputed in fp32 from their own rows with the chain's
+    bf16 roundings, within rtol 2e-2 / atol 1e-2. Returns a summary dict."""
+    import torch
+    import torch.nn.functional as F
+    prev_tf32 = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    try:
+        r, rim, xp = mid["routing"], mid["rim"], mid["xp"]
+        lb = logits + bias[None, :]
+        if placement is not None:
+            lb = lb[:, placement.long()]
+        idx = torch.topk(lb, k, dim=1).indices
+        ref_map = torch.zeros_like(r.routing_map)
+        ref_map.scatter_(1, idx, True)
+        maps_ok = bool(torch.equal(ref_map, r.routing_map))
+        p = torch.softmax(lb, dim=1).gather(1, idx)
+        p = p / p.sum(dim=1, keepdim=True)
+        ref_probs = torch.zeros_like(r.probs).scatter_(1, idx, p)
+        probs_ok = bool(torch.allclose(r.probs, ref_probs, rtol=1e-5, atol=1e-7))
+        m = ref_map.to(torch.int64)
+        cnt = m.sum(dim=0)
+        ref_te = torch.where(m > 0, torch.cumsum(m, dim=0) - 1 + (torch.cumsum(cnt, 0) - cnt)[None, :],
+                             torch.full_like(m, -1))
+        rim_ok = bool(torch.equal(ref_te, rim.map_te))
+        ti, ei = torch.nonzero(ref_te >= 0, as_tuple=True)
+        dst = ref_te[ti, ei]
+        perm_ok = True
+        for c0 in range(0, dst.numel(), 16384):  # chunks keep the gathers small
+            sl = slice(c0, c0 + 16384)
+            perm_ok &= bool(torch.equal(xp[dst[sl]], x[ti[sl]]))
+        tokens = sample_tokens(cnt, ref_te)
+        fdim = w2.shape[2]
+        worst = 0.0
+        out_ok = True
+        for tok in tokens:
+            acc = torch.zeros(x.shape[1], dtype=torch.float32, device=x.device)
+            for e_ in sorted(int(v) for v in torch.nonzero(ref_map[tok]).flatten()):
+                y1 = (x[tok].float() @ w1[e_].float().t()).to(torch.bfloat16).float()
+                hm = (F.silu(y1[:fdim]) * y1[fdim:]).to(torch.bfloat16).float()
+                y = (hm @ w2[e_].float().t()).to(torch.bfloat16).float()
+                acc = acc + r.probs[tok, e_] * y
+            ref = acc.to(torch.bfloat16).float()
+            got = out[tok].float()
+            err = (got - ref).abs()
+            worst = max(worst, float(err.max()))
+            out_ok &= bool(torch.all(err <= 1e-2 + 2e-2 * ref.abs()))
+        ok = maps_ok and probs_ok and rim_ok and perm_ok and out_ok
+        return {"ok": ok, "routing_map": maps_ok, "gates_rtol_1e-5": probs_ok,
+                "row_id_map": rim_ok, "permuted_rows": perm_ok, "rows": int(dst.numel()),
+                "tokens": len(tokens), "token_max_abs_err": round(worst, 6),
+                "token_tolerance": "rtol 2e-2, atol 1e-2", "outputs_ok": out_ok,
+                "reference": "torch on the device: top-k/softmax/cumsum/gather for the maps and "
+                             "rows, fp32 per-token FFN with bf16 roundings for the outputs"}
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev_tf32
+
+
+def split_blocks(steps, nblk):
+    base, rem = divmod(steps, nblk)
+    return [base + (1 if i < rem else 0) for i in range(nblk)]
+
+
 def main():
     a = parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -590,18 +754,13 @@ def main():
 
     t, h, e, f, k = a.tokens, a.hidden, a.experts, a.ffn, a.topk
     e_loc = e // world
-    g = torch.Generator(device=dev)
-    g.manual_seed(1000 + rank)
-    x = torch.randn(t, h, device=dev, generator=g).to(torch.bfloat16)
-    logits = torch.randn(t, e, device=dev, generator=g)
-    bias = zipf_bias(e, a.routing).to(dev)
-    w = moe_b200.MoEWeights.random(e_loc, h, f, dev, seed=77 + rank)
+    x, logits, bias, w = layer_inputs(t, h, e, f, a.routing, dev, rank, num_w=e_loc)
+    placement = None
     if world == 1:
         layer = moe_b200.MoELayer(w, topk=k, expert_bias=bias)
         stage_names = ["start", "routing", "permute", "fc1", "fc2", "combine"]
     else:
         from moe_b200.ep import MoELayerEP, balanced_placement
-        placement = None
         if a.placement == "balanced":
             # Calibration (untimed): expert loads of this job's routing, summed over ranks.
             r0 = moe_b200.router_topk(logits, k, "softmax", True, bias, outputs="maps")
@@ -619,6 +778,13 @@ def main():
         if world > 1:
             dist.barrier(device_ids=[local_rank])
 
+    def agree_max(v):
+        if world == 1:
+            return v
+        tv = torch.tensor([float(v)], device=dev)
+        dist.all_reduce(tv, op=dist.ReduceOp.MAX)
+        return float(tv.item())
+
     vis = os.environ.get("CUDA_VISIBLE_DEVICES")
     smi_index = vis.split(",")[local_rank] if vis else str(local_rank)
     sampler = ClockSampler(smi_index)
@@ -628,46 +794,8 @@ def main():
     torch.cuda.synchronize()
     assert layer.plan.device_error() == 0, "grouped GEMM reported a device error"
 
-    # ---- device-timed region: inputs resident in HBM
-    events = [{n: torch.cuda.Event(enable_timing=True) for n in stage_names}
-              for _ in range(a.steps)]
-    barrier()
-    torch.cuda.synchronize()
-    launches0 = _lib.launch_count
-    wall0 = time.time()
-    t_start = torch.cuda.Event(enable_timing=True)
-    t_end = torch.cuda.Event(enable_timing=True)
-    t_start.record()
-    for s in range(a.steps):
-        layer.events = events[s]
-        layer(x, logits)
-    t_end.record()
-    torch.cuda.synchronize()
-    sampler.mark(wall0, time.time())
-    barrier()
-    launches = _lib.launch_count - launches0
-    layer.events = None
-    ms_total = t_start.elapsed_time(t_end)
-    stage_ms = {}
-    for i in range(1, len(stage_names)):
-        n0, n1 = stage_names[i - 1], stage_names[i]
-        stage_ms[n1] = sum(ev[n0].elapsed_time(ev[n1]) for ev in events) / a.steps
-    fc1_ms = stage_ms["fc1"]
-    fc1_rows = t * k if world == 1 else int(layer.plan._keep.sum().item())
-    fc2_ms = stage_ms["fc2"]
-
-    ms_step = ms_total / a.steps
-    if world > 1:
-        v = torch.tensor([ms_step], device=dev)
-        dist.all_reduce(v, op=dist.ReduceOp.MAX)
-        ms_step = float(v.item())
-    value = world * t / (ms_step / 1e3)
-
-    # ---- end-to-end through the public API with host buffers: every step
-    # uploads its x and logits from pinned host memory and downloads its
-    # output; moe_b200.HostPipeline overlaps those copies with the kernels of
-    # the neighbouring steps.
-    e2e = None
+    # Host-buffer copies of the inputs for the end-to-end windows.
+    pipe = None
     if not a.no_e2e:
         x_h = x.cpu().pin_memory()
         lg_h = logits.cpu().pin_memory()
@@ -676,26 +804,96 @@ def main():
         for i in range(3):
             pipe.submit(x_h, lg_h, outs_h[i % 2])
         pipe.synchronize()
-        barrier()
-        torch.cuda.synchronize()
-        e0 = torch.cuda.Event(enable_timing=True)
-        e1 = torch.cuda.Event(enable_timing=True)
-        e0.record(pipe.up)
-        pipe.run([(x_h, lg_h, outs_h[i % 2]) for i in range(a.steps)])
-        e1.record(pipe.down)
-        torch.cuda.synchronize()
-        barrier()
-        e2e_ms = e0.elapsed_time(e1) / a.steps
-        if world > 1:
-            v = torch.tensor([e2e_ms], device=dev)
-            dist.all_reduce(v, op=dist.ReduceOp.MAX)
-            e2e_ms = float(v.item())
-        e2e = {"value": world * t / (e2e_ms / 1e3), "unit": UNIT,
-               "h2d_bytes_per_step": x.numel() * 2 + logits.numel() * 4,
-               "d2h_bytes_per_step": t * h * 2, "ms_per_step": e2e_ms,
-               "api": "moe_b200.HostPipeline.run (copies overlapped with compute)"}
 
+    # Settle (untimed): keep stepping until the GPU has run the layer for
+    # --settle-s seconds, so the timed windows see the clock the power cap
+    # holds under sustained load rather than the first seconds' boost.
+    settle_steps = 0
+    if a.settle_s > 0:
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        layer(x, logits)
+        e1.record()
+        torch.cuda.synchronize()
+        per = max(e0.elapsed_time(e1), 0.1)
+        settle_steps = int(agree_max(min(2000, max(0, int(a.settle_s * 1e3 / per)))))
+        for _ in range(settle_steps):
+            layer(x, logits)
+        torch.cuda.synchronize()
+
+    # ---- timed windows. K device-only steps (inputs resident in HBM) and K
+    # end-to-end steps (public API with host buffers) run in interleaved
+    # blocks so both see the same clock; each block is bracketed by a barrier
+    # and a synchronize on both sides.
+    events = [{n: torch.cuda.Event(enable_timing=True) for n in stage_names}
+              for _ in range(a.steps)]
+    nblk = 2 if (pipe is not None and a.steps >= 8) else 1
+    dev_ms = e2e_ms = 0.0
+    launches = 0
+    step_i = 0
+    for nb in split_blocks(a.steps, nblk):
+        barrier()
+        torch.cuda.synchronize()
+        l0 = _lib.launch_count
+        w0 = time.time()
+        t_start = torch.cuda.Event(enable_timing=True)
+        t_end = torch.cuda.Event(enable_timing=True)
+        t_start.record()
+        for _ in range(nb):
+            layer.events = events[step_i]
+            step_i += 1
+            layer(x, logits)
+        t_end.record()
+        torch.cuda.synchronize()
+        sampler.mark(w0, time.time(), "device")
+        barrier()
+        launches += _lib.launch_count - l0
+        layer.events = None
+        dev_ms += t_start.elapsed_time(t_end)
+        if pipe is not None:
+            barrier()
+            torch.cuda.synchronize()
+            q0 = torch.cuda.Event(enable_timing=True)
+            q1 = torch.cuda.Event(enable_timing=True)
+            w0 = time.time()
+            q0.record(pipe.up)
+            pipe.run([(x_h, lg_h, outs_h[i % 2]) for i in range(nb)])
+            q1.record(pipe.down)
+            torch.cuda.synchronize()
+            sampler.mark(w0, time.time(), "e2e")
+            barrier()
+            e2e_ms += q0.elapsed_time(q1)
+    stage_ms = {}
+    for i in range(1, len(stage_names)):
+        n0, n1 = stage_names[i - 1], stage_names[i]
+        stage_ms[n1] = sum(ev[n0].elapsed_time(ev[n1]) for ev in events) / a.steps
+    fc1_ms = stage_ms["fc1"]
+    fc1_rows = t * k if world == 1 else int(layer.plan._keep.sum().item())
+    fc2_ms = stage_ms["fc2"]
+
+    ms_step = agree_max(dev_ms / a.steps)
+    value = world * t / (ms_step / 1e3)
+    e2e = None
+    if pipe is not None:
+        e2e_step = agree_max(e2e_ms / a.steps)
+        e2e = {"value": world * t / (e2e_step / 1e3), "unit": UNIT,
+               "h2d_bytes_per_step": x.numel() * 2 + logits.numel() * 4,
+               "d2h_bytes_per_step": t * h * 2, "ms_per_step": e2e_step,
+               "api": "moe_b200.HostPipeline.run (copies overlapped with compute)"}
     clocks = sampler.stop()
+
+    # ---- correctness of the measured configuration (outside the timed windows)
+    check = None
+    if world == 1:
+        out, mid = layer.forward(x, logits, return_intermediates=True)
+        torch.cuda.synchronize()
+        check = check_layer(out, mid, x, logits, bias, w.w1, w.w2, k)
+        check["device_error"] = layer.plan.device_error()
+        check["ok"] = check["ok"] and check["device_error"] == 0
+        del out, mid
+    elif not a.no_check:
+        check = check_ep(layer, x, logits, bias, w, k, placement, world, rank, dev)
+
     peaks, peak_kind = load_peaks()
     fc1_flops = 2.0 * fc1_rows * (2 * f) * h
     fc2_flops = 2.0 * fc1_rows * h * f
@@ -714,18 +912,26 @@ def main():
         "gemm_frac_of_peak": round((fc1_flops + fc2_flops) / ((fc1_ms + fc2_ms) / 1e3) / 1e12 / peak, 4),
         "peak_kind": f"bf16 sustained, of {peak_kind}",
         "hbm_peak_gbs": hbm,
+        "settle_steps": settle_steps,
+        "timed_blocks": nblk,
     }
     if world == 1:
         extra["permute_gbs"] = round(perm_bytes / (stage_ms["permute"] / 1e3) / 1e9, 1)
         extra["combine_gbs"] = round(comb_bytes / (stage_ms["combine"] / 1e3) / 1e9, 1)
+    if clocks and clocks.get("windows"):
+        # Clock-normalised step cost: ms per step x median SM MHz of its window
+        # (millions of SM cycles per step), comparable across power-capped runs.
+        wn = clocks["windows"]
+        norm = {}
+        if wn.get("device", {}).get("sm_mhz"):
+            norm["value_mcycles_per_step"] = round(ms_step * wn["device"]["sm_mhz"] / 1e3, 3)
+        if e2e and wn.get("e2e", {}).get("sm_mhz"):
+            norm["e2e_mcycles_per_step"] = round(e2e["ms_per_step"] * wn["e2e"]["sm_mhz"] / 1e3, 3)
+        extra["clock_normalised"] = norm
 
     cpu = None
     if world == 1 and rank == 0 and not a.no_cpu_baseline:
-        use_all_cores()
-        dt, n = cpu_layer_sample(a, a.cpu_tokens)
-        cpu = {"value": n / dt, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
-               "sample": f"{n} tokens of the {t}-token layer (same H/E/F/top-k, {a.routing} "
-                         f"routing), numpy restatement, expert weights from an fp32 pool of 8"}
+        cpu = cpu_baseline_sample(a)
 
     if rank == 0:
         line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
@@ -737,7 +943,8 @@ def main():
                 "roofline": {"bound": "tensor", "kernel": "grouped_gemm fc1 stage (tcgen05 pair kernel + remainder kernel, fused SwiGLU)",
                              "achieved": round(achieved, 2), "peak": peak, "unit": "TFLOP/s",
                              "frac": round(achieved / peak, 4), "traffic": traffic},
-                "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks}
+                "cpu_baseline": cpu, "e2e": e2e, "gpu_launches": launches, "clocks": clocks,
+                "checked": None if check is None else bool(check["ok"]), "check": check}
         line.update(extra)
         print(json.dumps(line), flush=True)
     if world > 1:

@@ -381,3 +381,40 @@ def moe_layer(x_u16, logits, w1_u16, w2_u16, k, bias=None, renorm=True, tokens=N
     y = grouped_gemm(h, w2_u16, counts)
     _, out = unpermute(y, map_et, probs, "dense", tokens=tokens)
     return out
+
+
+def moe_layer_tokens(x_u16, probs, tokens, w1_of, w2_of):
+    """The layer output of `tokens` only, computed from each token's own rows.
+
+    The same chain as moe_layer for the selected tokens: for every expert e a
+    token is routed to (probs[t,e] != 0, ascending e, which is the combine's
+    order), y1 = bf16(x[t] @ w1[e].T), h = bf16(silu(gate) * up), y =
+    bf16(h @ w2[e].T), then acc = acc + probs[t,e] * y in fp32 and out =
+    bf16(acc) -- kernel_cases/case17…:58-71 (permute) -> case03…:57-64 (fc1)
+    -> case04…:57-64 (fc2) -> case15…:58-64 (combine, weighted). A GEMM row
+    depends only on its own input row, so this equals the grouped chain up to
+    fp32 summation order inside each dot product. w1_of(e) / w2_of(e) return
+    expert e's weights as bf16 bits ([2F,H] / [H,F]); each expert is fetched
+    once, so a full-size layer can be checked on a few tokens without holding
+    every expert's weights on the host.
+    Returns out bf16 bits [len(tokens), H].
+    """
+    tokens = np.asarray(tokens, dtype=np.int64)
+    p = np.asarray(probs, dtype=np.float32)[tokens]
+    h_dim = x_u16.shape[1]
+    ys = {}
+    for e in np.unique(np.nonzero(p)[1]):
+        sel = np.nonzero(p[:, e])[0]
+        xs = bf16_to_f32(x_u16[tokens[sel]])
+        w1 = bf16_to_f32(w1_of(int(e)))
+        f = w1.shape[0] // 2
+        y1 = bf16_to_f32(f32_to_bf16(xs @ w1.T))
+        hm = bf16_to_f32(f32_to_bf16(swiglu_f32(y1[:, :f], y1[:, f:])))
+        y = bf16_to_f32(f32_to_bf16(hm @ bf16_to_f32(w2_of(int(e))).T))
+        for i, s in enumerate(sel):
+            ys[(int(s), int(e))] = y[i]
+    acc = np.zeros((len(tokens), h_dim), dtype=np.float32)
+    for i in range(len(tokens)):
+        for e in np.nonzero(p[i])[0]:  # ascending expert order
+            acc[i] = acc[i] + (p[i, e] * ys[(i, int(e))]).astype(np.float32)
+    return f32_to_bf16(acc)

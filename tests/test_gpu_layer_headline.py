@@ -1,0 +1,68 @@
+"""Full-size parity of the single-GPU layer at the benchmark's headline
+configuration (T=16384 tokens, H=7168, E=256 experts, top-8, F=2048, Zipf
+expert bias), on the benchmark's own seeded inputs (bench.layer_inputs).
+
+Against the CPU oracle: the routing map, the row_id_map [T,E] and the
+per-expert counts exactly, the dense gates within rtol 1e-5, all T*k = 131072
+permuted rows bit for bit, and the outputs of sampled tokens within
+rtol 2e-2 / atol 1e-2 (the north-star GEMM tolerance). The sampled tokens are
+the first and last token, a token of the busiest expert, a token of the
+least-used expert that has rows, and twelve seeded others; their outputs are
+recomputed by moe_layer_tokens from each token's own rows, fetching only the
+weights of the experts those tokens reach. The chain is kernel_cases/
+case17…:58-71 (permute) -> case03…:57-64 (fc1) -> SwiGLU -> case04…:57-64
+(fc2) -> case15…:58-64 (combine, weighted by the gates).
+"""
+import numpy as np
+import pytest
+import torch
+
+from conftest import u16
+from oracle import moe_oracle as orc
+
+pytestmark = pytest.mark.gpu
+
+T, H, E, F, K = 16384, 7168, 256, 2048, 8
+
+
+def _tokens(counts, te, seed=0):
+    busiest = int(np.argmax(counts))
+    rarest = int(np.argmin(np.where(counts > 0, counts, np.iinfo(np.int64).max)))
+    picks = [0, T - 1]
+    for e in (busiest, rarest):
+        ts = np.nonzero(te[:, e] >= 0)[0]
+        picks.append(int(ts[len(ts) // 2]))
+    picks += np.random.default_rng(seed).integers(0, T, 12).tolist()
+    return np.array(sorted(set(picks))), busiest, rarest
+
+
+def test_headline_layer_vs_oracle(cuda_dev):
+    import bench
+    import moe_b200
+    x, logits, bias, w = bench.layer_inputs(T, H, E, F, "zipf", cuda_dev)
+    layer = moe_b200.MoELayer(w, topk=K, expert_bias=bias)
+    out, mid = layer.forward(x, logits, return_intermediates=True)
+    torch.cuda.synchronize()
+    assert layer.plan.device_error() == 0
+
+    _, _, rmap, probs = orc.router(logits.cpu().numpy(), K, bias.cpu().numpy())
+    r = mid["routing"]
+    np.testing.assert_array_equal(r.routing_map.cpu().numpy(), rmap)
+    np.testing.assert_allclose(r.probs.cpu().numpy(), probs, rtol=1e-5, atol=1e-8)
+    _, te, counts, n = orc.row_id_map(rmap)
+    assert n == T * K
+    np.testing.assert_array_equal(mid["rim"].counts.cpu().numpy(), counts)
+    np.testing.assert_array_equal(mid["rim"].map_te.cpu().numpy(), te)
+
+    xu = u16(x)
+    xp_ref, _ = orc.permute(xu, te, None, n)
+    xp = mid["xp"]
+    for c0 in range(0, n, 8192):
+        np.testing.assert_array_equal(u16(xp[c0:c0 + 8192]), xp_ref[c0:c0 + 8192])
+    del xp_ref
+
+    tokens, busiest, rarest = _tokens(counts, te)
+    assert counts[busiest] > 256 and counts[rarest] < 256  # a multi-tile and a remainder-only expert
+    ref = orc.moe_layer_tokens(xu, probs, tokens, lambda e: u16(w.w1[e]), lambda e: u16(w.w2[e]))
+    got = u16(out[torch.as_tensor(tokens, device=cuda_dev)])
+    np.testing.assert_allclose(orc.bf16_to_f32(got), orc.bf16_to_f32(ref), rtol=2e-2, atol=1e-2)
