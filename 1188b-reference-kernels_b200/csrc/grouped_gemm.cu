@@ -827,7 +827,8 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
                                                     int32_t* __restrict__ tmp,
                                                     int32_t* __restrict__ rows_body,
                                                     int32_t* __restrict__ tail_start,
-                                                    int32_t* __restrict__ rows_tail) {
+                                                    int32_t* __restrict__ rows_tail,
+                                                    int fold_min) {
   __shared__ int64_t warp_sums[32];
   __shared__ int64_t carry_s;
   const int lane = lane_id(), wid = warp_id();
@@ -876,7 +877,10 @@ __global__ void __launch_bounds__(1024) plan_kernel(const int32_t* __restrict__ 
       w = e;
     }
     const int32_t m = max(counts[f], 0);
-    const int32_t body = (m / pairk::kPairTileM) * pairk::kPairTileM;
+    // A group of at least fold_min rows keeps its remainder on the pair
+    // kernel as a row-predicated last tile, computed while its weight slab is
+    // still in L2; smaller groups split as below.
+    const int32_t body = m >= fold_min ? m : (m / pairk::kPairTileM) * pairk::kPairTileM;
     row_start[g] = tmp[f];
     rows[g] = m;
     widx[g] = w;
@@ -1005,6 +1009,14 @@ int env_int(const char* name, int def, int lo, int hi) {
   return (v < lo || v > hi) ? def : v;
 }
 
+// Smallest group whose remainder (rows beyond its whole 256-row tiles) stays
+// on the pair kernel: MOE_GEMM_FOLD=1 folds the remainder of every group
+// that has whole tiles; 0 hands every remainder to the single-CTA kernel.
+int fold_min() {
+  static const int v = env_int("MOE_GEMM_FOLD", 0, 0, 1) == 1 ? pairk::kPairTileM : 0x7fffffff;
+  return v;
+}
+
 bool pair_enabled() {
   static int v = -1;
   if (v < 0) {
@@ -1061,7 +1073,7 @@ extern "C" int moe_grouped_gemm_plan_splits(const int32_t* m_splits, int64_t G, 
   gg::WsLayout l = gg::ws_layout(workspace, G);
   gg::plan_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       m_splits, static_cast<int>(G), 0, 1, static_cast<int>(G), align, l.err, l.row_start, l.rows,
-      l.widx, l.tmp, l.rows_body, l.tail_start, l.rows_tail);
+      l.widx, l.tmp, l.rows_body, l.tail_start, l.rows_tail, gg::fold_min());
   MOE_CUDA_CHECK_LAUNCH("grouped_gemm plan");
   return MOE_OK;
 }
@@ -1079,7 +1091,8 @@ extern "C" int moe_grouped_gemm_plan_ep(const int32_t* counts, int64_t num_src, 
   gg::WsLayout l = gg::ws_layout(workspace, G);
   gg::plan_kernel<<<1, 1024, 0, reinterpret_cast<cudaStream_t>(stream)>>>(
       counts, static_cast<int>(G), 1, static_cast<int>(num_src), static_cast<int>(num_w), 1,
-      l.err, l.row_start, l.rows, l.widx, l.tmp, l.rows_body, l.tail_start, l.rows_tail);
+      l.err, l.row_start, l.rows, l.widx, l.tmp, l.rows_body, l.tail_start, l.rows_tail,
+      gg::fold_min());
   MOE_CUDA_CHECK_LAUNCH("grouped_gemm plan_ep");
   return MOE_OK;
 }
