@@ -14,10 +14,13 @@ split evenly, NCCL all-to-all dispatch/combine. Prints one JSON line on rank 0.
          H2D of x and logits and D2H of the output inside every timed step;
   roofline  the dominant kernel (fc1 grouped GEMM, tcgen05) against the
          measured bf16 peak; stages  per-stage device times;
-  cpu_baseline  the numpy restatement of the same layer (oracle/) on this
-         host's cores over a bounded token sample (rank 0, N=1 only).
---impl reference times that CPU restatement alone (the reference's own path
-is PyTorch-on-CPU code that cannot run without its sources).
+  cpu_baseline  the reference's layer chain restated in torch on the CPU
+         (oracle/torch_ref.py: the cases' Model.forward ops) on this host's
+         cores over a bounded token sample (rank 0, N=1 only);
+  checked  the measured configuration's maps, permuted rows and sampled
+         token outputs against a torch reference, after the timed windows.
+--impl reference times that CPU restatement alone (the reference's own case
+files cannot travel to the GPU host; its ops are restated op for op).
 """
 from __future__ import annotations
 
@@ -59,7 +62,7 @@ def parse_args():
     ap.add_argument("--ffn", type=int, default=2048)
     ap.add_argument("--topk", type=int, default=8)
     ap.add_argument("--routing", choices=["zipf", "uniform"], default="zipf")
-    ap.add_argument("--cpu-tokens", type=int, default=1024,
+    ap.add_argument("--cpu-tokens", type=int, default=4096,
                     help="token sample of the CPU baseline (per step for --impl reference)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true")
@@ -217,31 +220,51 @@ class ClockSampler:
 
 
 # --------------------------------------------------------------------------- CPU port
-def cpu_layer_sample(a, tokens, seed=0):
-    """Times the numpy restatement of the layer on `tokens` tokens with the
-    bench's shapes. Expert weights come from a pool of 8 fp32 matrices (the
-    per-token work is unchanged; 256 distinct fp32 experts would need 45 GB of
-    host memory). Returns (seconds, tokens)."""
-    import numpy as np
-    from oracle import moe_oracle as orc
-    rng = np.random.default_rng(seed)
+def cpu_layer_setup(a, tokens, seed=0):
+    """Inputs of one bounded CPU sample of the layer: `tokens` tokens with the
+    bench's shapes and Zipf routing, and bf16 weights for the experts those
+    tokens reach (the others are never read). Each expert's weights are a
+    distinct window of one seeded N(0,1) pool scaled by 0.02: generating
+    ~90 x 88 MB of fresh normals per run would take longer than the sample,
+    and the values do not change the work."""
+    import torch
+    from oracle import torch_ref as tr
     h, e, f, k = a.hidden, a.experts, a.ffn, a.topk
-    x = orc.f32_to_bf16(rng.standard_normal((tokens, h), dtype=np.float32))
-    bias = zipf_bias(e, a.routing).numpy()
-    lg = rng.standard_normal((tokens, e), dtype=np.float32)
-    pool = 8
-    w1p = [(rng.standard_normal((2 * f, h), dtype=np.float32) * 0.02) for _ in range(pool)]
-    w2p = [(rng.standard_normal((h, f), dtype=np.float32) * 0.02) for _ in range(pool)]
-    w1 = [w1p[i % pool] for i in range(e)]
-    w2 = [w2p[i % pool] for i in range(e)]
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(tokens, h, generator=g).to(torch.bfloat16)
+    lg = torch.randn(tokens, e, generator=g)
+    bias = zipf_bias(e, a.routing)
+    rmap, _ = tr.route(lg, bias, k)
+    hit = rmap.any(dim=0).nonzero().flatten().tolist()
+    torch.manual_seed(seed)
+    pool = torch.randn(1 << 26)
+    n1, n2 = 2 * f * h, h * f
+
+    def window(i, n):
+        off = (i * 1000003) % (pool.numel() - n // 2)
+        return pool[off:off + n // 2].repeat(2)[:n].mul(0.02).to(torch.bfloat16)
+
+    w1 = {i: window(2 * i, n1).view(2 * f, h) for i in hit}
+    w2 = {i: window(2 * i + 1, n2).view(h, f) for i in hit}
+    return x, lg, bias, w1, w2
+
+
+def cpu_layer_time(a, setup):
+    """Seconds for one forward of the torch CPU restatement of the
+    reference's layer chain (oracle/torch_ref.py) on one sample."""
+    from oracle import torch_ref as tr
+    x, lg, bias, w1, w2 = setup
     t0 = time.perf_counter()
-    _, _, rmap, probs = orc.router(lg, k, bias, "softmax", True)
-    map_et, map_te, counts, n = orc.row_id_map(rmap)
-    xp, _ = orc.permute(x, map_te, None, n)
-    hmid = orc.grouped_gemm(xp, w1, counts, "swiglu")
-    y = orc.grouped_gemm(hmid, w2, counts)
-    orc.unpermute(y, map_et, probs, "dense")
-    return time.perf_counter() - t0, tokens
+    tr.layer(x, lg, bias, w1.__getitem__, w2.__getitem__, a.topk)
+    return time.perf_counter() - t0
+
+
+def cpu_sample_desc(a):
+    return (f"{a.cpu_tokens} tokens per step of the {a.tokens}-token layer (same H/E/F/top-k, "
+            f"{a.routing} routing): the reference's torch chain restated on the CPU "
+            f"(sort top-k, case12 cumsum row_id_map, case17 index_copy_ permute, case03/case04 "
+            f"bf16 torch.mm per expert, SwiGLU, weighted case15 index_add_ combine), bf16 "
+            f"weights of every expert the sample reaches")
 
 
 def use_all_cores():
@@ -253,28 +276,25 @@ def use_all_cores():
         threadpool_limits(limits=n)
     except Exception:
         pass
+    import torch
+    torch.set_num_threads(n)
     return n
 
 
 def cpu_threads():
-    try:
-        from threadpoolctl import threadpool_info
-        n = [i.get("num_threads", 0) for i in threadpool_info() if i.get("user_api") == "blas"]
-        if n:
-            return int(max(n))
-    except Exception:
-        pass
-    return os.cpu_count() or 1
+    import torch
+    return torch.get_num_threads()
 
 
 def cpu_baseline_sample(a):
-    """The cpu_baseline object of the GPU arm's line: one bounded sample of the
-    layer on this host's cores."""
+    """The cpu_baseline object of the GPU arm's line: the reference's layer
+    chain on this host's cores, one warm-up and two timed runs of one sample."""
     use_all_cores()
-    dt, n = cpu_layer_sample(a, a.cpu_tokens)
-    return {"value": n / dt, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
-            "sample": f"{n} tokens of the {a.tokens}-token layer (same H/E/F/top-k, {a.routing} "
-                      f"routing), numpy restatement, expert weights from an fp32 pool of 8"}
+    setup = cpu_layer_setup(a, a.cpu_tokens)
+    cpu_layer_time(a, setup)
+    dt = min(cpu_layer_time(a, setup) for _ in range(2))
+    return {"value": a.cpu_tokens / dt, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
+            "sample": cpu_sample_desc(a)}
 
 
 def check_ep(layer, x, logits, bias, w, k, placement, world, rank, dev):
@@ -313,22 +333,18 @@ def run_reference_arm(a, world, rank):
     if rank != 0:
         return
     use_all_cores()
+    setup = cpu_layer_setup(a, a.cpu_tokens, seed=1)
     for _ in range(a.warmup):
-        cpu_layer_sample(a, a.cpu_tokens, seed=1)
-    times = []
-    for s in range(a.steps):
-        dt, n = cpu_layer_sample(a, a.cpu_tokens, seed=2 + s)
-        times.append(dt)
+        cpu_layer_time(a, setup)
+    times = [cpu_layer_time(a, setup) for _ in range(a.steps)]
     total = sum(times)
     value = a.cpu_tokens * a.steps / total
-    sample = (f"{a.cpu_tokens} tokens per step of the {a.tokens}-token layer (same H/E/F/top-k, "
-              f"{a.routing} routing), numpy restatement, expert weights from an fp32 pool of 8")
     line = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": a.steps,
             "warmup": a.warmup, "ms_per_step": 1e3 * total / a.steps, "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
             "impl": "reference", "config": config_dict(a, world),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": cpu_threads(), "kind": "port",
-                             "sample": sample},
+                             "sample": cpu_sample_desc(a)},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     print(json.dumps(line), flush=True)
