@@ -219,6 +219,32 @@ class ClockSampler:
         return out
 
 
+class EnergyMeter:
+    """The GPU's cumulative energy counter (NVML, millijoules), read around each
+    timed window: joules per step is the figure that decides speed when the
+    step runs at the board's power cap. Reading the counter changes nothing."""
+
+    def __init__(self, device_index):
+        self.h = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(int(device_index))
+            self.read()
+        except Exception:
+            self.h = None
+
+    def read(self):
+        if self.h is None:
+            return None
+        try:
+            return float(self._nvml.nvmlDeviceGetTotalEnergyConsumption(self.h))
+        except Exception:
+            self.h = None
+            return None
+
+
 # --------------------------------------------------------------------------- CPU port
 def cpu_layer_setup(a, tokens, seed=0):
     """Inputs of one bounded CPU sample of the layer: `tokens` tokens with the
@@ -805,6 +831,8 @@ def main():
     smi_index = vis.split(",")[local_rank] if vis else str(local_rank)
     sampler = ClockSampler(smi_index)
     sampler.start()
+    meter = EnergyMeter(smi_index)
+    energy_mj = {"device": 0.0, "e2e": 0.0}
     for _ in range(a.warmup):
         layer(x, logits)
     torch.cuda.synchronize()
@@ -851,6 +879,7 @@ def main():
         barrier()
         torch.cuda.synchronize()
         l0 = _lib.launch_count
+        j0 = meter.read()
         w0 = time.time()
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
@@ -861,7 +890,10 @@ def main():
             layer(x, logits)
         t_end.record()
         torch.cuda.synchronize()
+        j1 = meter.read()
         sampler.mark(w0, time.time(), "device")
+        if j0 is not None and j1 is not None:
+            energy_mj["device"] += j1 - j0
         barrier()
         launches += _lib.launch_count - l0
         layer.events = None
@@ -871,12 +903,16 @@ def main():
             torch.cuda.synchronize()
             q0 = torch.cuda.Event(enable_timing=True)
             q1 = torch.cuda.Event(enable_timing=True)
+            j0 = meter.read()
             w0 = time.time()
             q0.record(pipe.up)
             pipe.run([(x_h, lg_h, outs_h[i % 2]) for i in range(nb)])
             q1.record(pipe.down)
             torch.cuda.synchronize()
+            j1 = meter.read()
             sampler.mark(w0, time.time(), "e2e")
+            if j0 is not None and j1 is not None:
+                energy_mj["e2e"] += j1 - j0
             barrier()
             e2e_ms += q0.elapsed_time(q1)
     stage_ms = {}
@@ -944,6 +980,14 @@ def main():
         if e2e and wn.get("e2e", {}).get("sm_mhz"):
             norm["e2e_mcycles_per_step"] = round(e2e["ms_per_step"] * wn["e2e"]["sm_mhz"] / 1e3, 3)
         extra["clock_normalised"] = norm
+    if meter.h is not None and energy_mj["device"] > 0:
+        # This GPU's energy (rank 0's at N > 1): the timed device-only and e2e
+        # windows, from the board's counter, which includes the idle host gaps.
+        extra["energy"] = {"j_per_step": round(energy_mj["device"] / 1e3 / a.steps, 4),
+                           "e2e_j_per_step": round(energy_mj["e2e"] / 1e3 / a.steps, 4)
+                           if energy_mj["e2e"] > 0 else None,
+                           "tokens_per_joule": round(t * a.steps / (energy_mj["device"] / 1e3), 1),
+                           "source": "NVML total energy counter, timed windows"}
 
     cpu = None
     if world == 1 and rank == 0 and not a.no_cpu_baseline:

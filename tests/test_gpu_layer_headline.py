@@ -26,8 +26,9 @@ T, H, E, F, K = 16384, 7168, 256, 2048, 8
 
 
 def _tokens(counts, te, seed=0):
-    busiest = int(np.argmax(counts))
-    rarest = int(np.argmin(np.where(counts > 0, counts, np.iinfo(np.int64).max)))
+    c = np.asarray(counts, dtype=np.int64)
+    busiest = int(np.argmax(c))
+    rarest = int(np.argmin(np.where(c > 0, c, np.int64(1) << 40)))
     picks = [0, T - 1]
     for e in (busiest, rarest):
         ts = np.nonzero(te[:, e] >= 0)[0]
