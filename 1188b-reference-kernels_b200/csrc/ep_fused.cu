@@ -18,6 +18,8 @@
 // The reference names this hop (deep_ep intranode FusedDispatch /
 // FusedCombine, kernel_cases/case22_ref_moe_permute_mask_kernel_true.py:3-6,
 // case24_ref_moe_unpermute_mask_kernel_false.py:3-6) but does not contain it.
+#include <algorithm>
+
 #include "moe_common.cuh"
 #include "rowcopy.cuh"
 
@@ -79,6 +81,61 @@ __global__ void __launch_bounds__(kRowThreads) ep_dispatch_kernel(
       }
     }
     __syncthreads();
+  }
+}
+
+// One chunk of the dispatch: as ep_dispatch_kernel, but only the (t, e) whose
+// local expert index e % experts_per_rank lies in [le_lo, le_hi) are sent, and
+// the grid is persistent over tokens (blockIdx.x, blockIdx.x + gridDim.x, ...).
+// With a grid of about one 128-thread CTA per SM and ~1 KB of shared memory,
+// its CTAs fit on the SMs beside a running grouped-GEMM CTA, so the next
+// chunk's rows can move over NVLink while the GEMMs of this chunk run (the
+// two launches share no data and neither waits for the other). A token
+// whose map has no entry in the chunk is not read.
+template <int VPT, typename V>
+__global__ void __launch_bounds__(kRowThreads) ep_dispatch_range_kernel(
+    const V* __restrict__ x, const int64_t* __restrict__ map_te, const PeerRows pr, int64_t T,
+    int E, int nvec, int64_t num_rows, int le_lo, int le_hi) {
+  __shared__ long long s_dst[kRowThreads];  // destination row address
+  __shared__ int s_wcnt[kRowWarps];
+  const int tid = threadIdx.x;
+  const int el = pr.experts_per_rank;
+  for (int64_t t = blockIdx.x; t < T; t += gridDim.x) {
+    const V* src = x + t * nvec;
+    V r[VPT];
+    bool loaded = false;
+    for (int e0 = 0; e0 < E; e0 += kRowThreads) {
+      const int e = e0 + tid;
+      int64_t row = -1;
+      if (e < E) {
+        const int le = e % el;
+        if (le >= le_lo && le < le_hi) row = __ldg(map_te + t * E + e);
+      }
+      long long base = 0;
+      int64_t rr = 0;
+      const bool valid = row >= 0 && row < num_rows && peer_row(pr, e, row, base, rr);
+      int pos;
+      const int total = compact_window(valid, s_wcnt, pos);
+      if (valid) s_dst[pos] = base + rr * nvec * static_cast<long long>(sizeof(V));
+      __syncthreads();
+      if (total > 0 && !loaded) {  // block-uniform
+#pragma unroll
+        for (int v = 0; v < VPT; ++v) {
+          const int i = tid + v * kRowThreads;
+          if (i < nvec) r[v] = __ldg(src + i);
+        }
+        loaded = true;
+      }
+      for (int j = 0; j < total; ++j) {
+        V* o = reinterpret_cast<V*>(s_dst[j]);
+#pragma unroll
+        for (int v = 0; v < VPT; ++v) {
+          const int i = tid + v * kRowThreads;
+          if (i < nvec) o[i] = r[v];
+        }
+      }
+      __syncthreads();
+    }
   }
 }
 
@@ -314,6 +371,49 @@ extern "C" int moe_ep_dispatch(const void* x, const int64_t* row_id_map_te,
     ep_dispatch_kernel<16, uint16_t><<<grid, kRowThreads, 0, s>>>(xv, row_id_map_te, pr, T, (int)E, nvec, num_rows);
   }
   MOE_CUDA_CHECK_LAUNCH("ep_dispatch launch");
+  return MOE_OK;
+}
+
+extern "C" int moe_ep_dispatch_range(const void* x, const int64_t* row_id_map_te,
+                                     const int64_t* peer_bases, const int64_t* expert_deltas,
+                                     int32_t ranks, int32_t experts_per_rank, int64_t cap_rows,
+                                     int64_t T, int64_t H, int64_t E, int64_t num_rows,
+                                     int32_t local_lo, int32_t local_hi, int32_t max_ctas,
+                                     moe_stream_t stream) {
+  MOE_REQUIRE(T >= 0 && H >= 0 && E >= 1, "ep_dispatch_range: bad shape");
+  MOE_REQUIRE(local_lo >= 0 && local_lo <= local_hi && local_hi <= experts_per_rank,
+              "ep_dispatch_range: local expert range [%d,%d) outside [0,%d)", local_lo, local_hi,
+              experts_per_rank);
+  MOE_REQUIRE(max_ctas >= 0, "ep_dispatch_range: max_ctas=%d", max_ctas);
+  if (T == 0 || H == 0 || local_lo == local_hi) return MOE_OK;
+  MOE_REQUIRE(x && row_id_map_te, "ep_dispatch_range: null pointer");
+  PeerRows pr;
+  int vb = 16;
+  int st = make_peer_rows(pr, peer_bases, expert_deltas, ranks, experts_per_rank, cap_rows, E, H,
+                          vb, "ep_dispatch_range");
+  if (st) return st;
+  if ((reinterpret_cast<uintptr_t>(x) & 15) != 0) vb = 2;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned grid = static_cast<unsigned>(
+      max_ctas > 0 ? std::min<int64_t>(T, max_ctas) : T);
+  const int lo = local_lo, hi = local_hi;
+  if (vb == 16) {
+    const int nvec = static_cast<int>(H / 8);
+    const int vpt = (nvec + kRowThreads - 1) / kRowThreads;
+    MOE_REQUIRE(vpt <= 8, "ep_dispatch_range: H=%lld above 8192", (long long)H);
+    const uint4* xv = static_cast<const uint4*>(x);
+    if (vpt <= 2) ep_dispatch_range_kernel<2, uint4><<<grid, kRowThreads, 0, s>>>(xv, row_id_map_te, pr, T, (int)E, nvec, num_rows, lo, hi);
+    else if (vpt <= 4) ep_dispatch_range_kernel<4, uint4><<<grid, kRowThreads, 0, s>>>(xv, row_id_map_te, pr, T, (int)E, nvec, num_rows, lo, hi);
+    else ep_dispatch_range_kernel<8, uint4><<<grid, kRowThreads, 0, s>>>(xv, row_id_map_te, pr, T, (int)E, nvec, num_rows, lo, hi);
+  } else {
+    const int nvec = static_cast<int>(H);
+    const int vpt = (nvec + kRowThreads - 1) / kRowThreads;
+    MOE_REQUIRE(vpt <= 16, "ep_dispatch_range: H=%lld above 2048 for unaligned rows",
+                (long long)H);
+    ep_dispatch_range_kernel<16, uint16_t><<<grid, kRowThreads, 0, s>>>(
+        static_cast<const uint16_t*>(x), row_id_map_te, pr, T, (int)E, nvec, num_rows, lo, hi);
+  }
+  MOE_CUDA_CHECK_LAUNCH("ep_dispatch_range launch");
   return MOE_OK;
 }
 

@@ -364,6 +364,19 @@ class EPPeerExchange:
         self.barrier()
         return self.recv_buf[:nrecv]
 
+    def dispatch_range(self, x: torch.Tensor, map_te: torch.Tensor, deltas: torch.Tensor,
+                       nsend: int, local_lo: int, local_hi: int, max_ctas: int) -> None:
+        """One chunk of the fused dispatch on the current stream, no barrier:
+        the rows of every (t, e) whose local expert index e % E_loc is in
+        [local_lo, local_hi), stored straight into the owners' receive
+        buffers by a persistent kernel of at most max_ctas CTAs."""
+        t, h = x.shape
+        bases = (ctypes.c_int64 * self.world)(*self.peer_recv)
+        _lib.call("moe_ep_dispatch_range", x.data_ptr(), map_te.data_ptr(), bases,
+                  deltas.data_ptr(), self.world, self.local_experts, self.recv_cap, t, h,
+                  self.num_experts, nsend, int(local_lo), int(local_hi), int(max_ctas),
+                  torch.cuda.current_stream(self.device).cuda_stream)
+
     def fused_dispatch_dedup(self, x: torch.Tensor, map_te: torch.Tensor, deltas: torch.Tensor,
                              nsend: int, nrecv: int) -> torch.Tensor:
         """Token rows once per destination rank into the peers' staging rows
@@ -415,14 +428,25 @@ class MoELayerEP:
     def __init__(self, local_weights: MoEWeights, num_experts: int, topk: int = 8,
                  renorm: bool = True, expert_bias: Optional[torch.Tensor] = None,
                  group: Optional[dist.ProcessGroup] = None, transport: str = "nccl",
-                 tokens: Optional[int] = None, placement: Optional[torch.Tensor] = None):
+                 tokens: Optional[int] = None, placement: Optional[torch.Tensor] = None,
+                 overlap_chunks: int = 1):
         """transport "nccl": all_to_all_single of counts and rows; "peer": IPC-mapped
         buffers filled by copy-engine pushes; "fused": the dispatch and combine
         kernels store / load rows in the peers' buffers directly; "fused_dedup":
         as "fused", with each token row sent once per destination rank and
         expanded there. "peer" and "fused*" need `tokens`, the per-rank T. placement (int32 [E] permutation):
         slot c is model expert placement[c]; this rank holds the weights of
-        slots [rank*E_loc, (rank+1)*E_loc) (e.g. from balanced_placement)."""
+        slots [rank*E_loc, (rank+1)*E_loc) (e.g. from balanced_placement).
+
+        overlap_chunks (transport "fused" only): C > 1 splits every rank's local
+        experts into C contiguous chunks. Chunk c's rows are dispatched and
+        barriered on a side stream; chunk c's fc1/fc2 run on the caller's
+        stream once its barrier has passed, while chunk c+1's rows already
+        cross NVLink. The dispatch kernel is persistent with about one small
+        CTA per SM, so it fits beside the GEMM's CTAs; the two kernels share
+        no data and never wait on each other on the device. The output is the
+        same, bit for bit, as with C = 1 (same receive rows, same GEMM
+        groups, same combine)."""
         self.placement = placement
         self.disp = EPDispatcher(num_experts, group)
         self.peer = None
@@ -447,6 +471,17 @@ class MoELayerEP:
         self.plan = ops.GroupedGemmPlan(groups, local_weights.w1.device)
         self._deltas = None
         self.events = None  # optional dict of CUDA events for stage timing
+        self.chunks = int(overlap_chunks)
+        if self.chunks < 1 or self.chunks > self.disp.local_experts:
+            raise ValueError(f"overlap_chunks must be in [1, {self.disp.local_experts}]")
+        if self.chunks > 1 and transport != "fused":
+            raise ValueError("overlap_chunks > 1 needs transport='fused'")
+        self._bounds = self.chunk_bounds(self.disp.local_experts, self.chunks)
+        self._chunk_plans = [ops.GroupedGemmPlan(hi - lo, local_weights.w1.device)
+                             for lo, hi in self._bounds] if self.chunks > 1 else []
+        self._comm = None
+        self._sms = 0
+        self.last_recv_rows = 0  # rows this rank's experts received in the last forward
 
     def _ev(self, name: str):
         if self.events is not None:
@@ -473,6 +508,7 @@ class MoELayerEP:
             xr = self.disp.dispatch(xp, send, recv)
         self._ev("a2a_dispatch")
         self.plan.from_ep_counts(recv_counts, self.disp.world, self.disp.local_experts)
+        self.last_recv_rows = int(xr.shape[0])
         hmid = ops.grouped_gemm(xr, self.w.w1, epilogue="swiglu", plan=self.plan)
         self._ev("fc1")
         y = ops.grouped_gemm(hmid, self.w.w2, plan=self.plan)
@@ -493,22 +529,85 @@ class MoELayerEP:
         self._deltas = deltas  # read by both fused kernels of this forward
         nsend = int(sum(host[self.peer.rank]))
         nrecv = int(sum(lay.splits))
-        if self.peer.dedup:
-            xr = self.peer.fused_dispatch_dedup(x, rim.map_te, deltas, nsend, nrecv)
+        self.last_recv_rows = nrecv
+        if self.chunks > 1:
+            self._chunked_experts(x, rim.map_te, deltas, nsend, lay.splits)
         else:
-            xr = self.peer.fused_dispatch(x, rim.map_te, deltas, nsend, nrecv)
-        self._ev("a2a_dispatch")
-        self.plan.from_splits(torch.tensor(lay.splits, dtype=torch.int32))
-        hmid = ops.grouped_gemm(xr, self.w.w1, epilogue="swiglu", plan=self.plan)
-        self._ev("fc1")
-        y = ops.grouped_gemm(hmid, self.w.w2, plan=self.plan,
-                             out=self.peer.y_buf[:xr.shape[0]])
+            if self.peer.dedup:
+                xr = self.peer.fused_dispatch_dedup(x, rim.map_te, deltas, nsend, nrecv)
+            else:
+                xr = self.peer.fused_dispatch(x, rim.map_te, deltas, nsend, nrecv)
+            self._ev("a2a_dispatch")
+            self.plan.from_splits(torch.tensor(lay.splits, dtype=torch.int32))
+            hmid = ops.grouped_gemm(xr, self.w.w1, epilogue="swiglu", plan=self.plan)
+            self._ev("fc1")
+            ops.grouped_gemm(hmid, self.w.w2, plan=self.plan, out=self.peer.y_buf[:xr.shape[0]])
         self._ev("fc2")
         self.peer.barrier()
         self._ev("a2a_combine")
         out = self.peer.fused_combine(rim.map_te, r.probs, deltas, nsend, t, h)
         self._ev("combine")
         return out
+
+    @staticmethod
+    def chunk_bounds(local_experts: int, chunks: int):
+        """[lo, hi) local-expert ranges of the overlap chunks: contiguous, in
+        order, sizes differing by at most one."""
+        el = int(local_experts)
+        return [(el * c // chunks, el * (c + 1) // chunks) for c in range(chunks)]
+
+    def _chunked_experts(self, x, map_te, deltas, nsend, splits):
+        """Dispatch (side stream) and fc1/fc2 (caller's stream) chunk by chunk
+        of the local experts; see overlap_chunks. Stage events: a2a_dispatch
+        when chunk 0 is ready, fc1 after the last chunk's fc1."""
+        dev = x.device
+        main = torch.cuda.current_stream(dev)
+        if self._comm is None:
+            self._comm = torch.cuda.Stream(dev)
+            self._sms = torch.cuda.get_device_properties(dev).multi_processor_count
+        comm = self._comm
+        starts = [0]
+        for v in splits:
+            starts.append(starts[-1] + int(v))
+        # Group sizes of every chunk on the device up front, so no chunk's
+        # plan waits on a host copy between the GEMM launches.
+        sp = torch.tensor([int(v) for v in splits], dtype=torch.int32).pin_memory().to(
+            dev, non_blocking=True)
+        comm.wait_stream(main)
+        for tt in (x, map_te, deltas):
+            tt.record_stream(comm)
+        ready = []
+        with torch.cuda.stream(comm):
+            for lo, hi in self._bounds:
+                self.peer.dispatch_range(x, map_te, deltas, nsend, lo, hi, self._sms)
+                self.peer.barrier()  # every rank's rows of this chunk have landed
+                ev = torch.cuda.Event()
+                ev.record(comm)
+                ready.append(ev)
+        last = len(self._bounds) - 1
+        for c, (lo, hi) in enumerate(self._bounds):
+            main.wait_event(ready[c])
+            if c == 0:
+                self._ev("a2a_dispatch")
+            r0, r1 = starts[lo], starts[hi]
+            hm = None
+            if r1 > r0:
+                plan = self._chunk_plans[c].from_splits(sp[lo:hi])
+                hm = ops.grouped_gemm(self.peer.recv_buf[r0:r1], self.w.w1[lo:hi],
+                                      epilogue="swiglu", plan=plan)
+            if c == last:
+                self._ev("fc1")
+            if hm is not None:
+                ops.grouped_gemm(hm, self.w.w2[lo:hi], plan=plan, out=self.peer.y_buf[r0:r1])
+
+    def device_error(self) -> int:
+        """First non-zero device error word of this layer's grouped-GEMM
+        plans (0: none). Synchronises."""
+        for p in [self.plan] + self._chunk_plans:
+            v = p.device_error()
+            if v:
+                return v
+        return 0
 
     __call__ = forward
 

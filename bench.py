@@ -50,6 +50,14 @@ def resolve_transport(transport: str, world: int) -> str:
     return "fused_dedup" if world <= 4 else "fused"
 
 
+def overlap_chunks(a, world: int) -> int:
+    return a.overlap_chunks if resolve_transport(a.transport, world) == "fused" else 1
+
+
+def device_error(layer) -> int:
+    return layer.device_error() if hasattr(layer, "device_error") else layer.plan.device_error()
+
+
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -82,6 +90,10 @@ def parse_args():
                          "buffers + copy engines, or NCCL all-to-all; auto = fused_dedup up to "
                          "4 GPUs, fused at 8 (where tokens reach 6.8 of 8 ranks and the "
                          "receiver's expansion copy outweighs the saved rows)")
+    ap.add_argument("--overlap-chunks", type=int, default=1,
+                    help="EP with --transport fused: split the local experts into this many "
+                         "chunks and dispatch chunk c+1 over NVLink while chunk c's GEMMs run "
+                         "(1 = no overlap)")
     ap.add_argument("--workload", choices=["layer", "router_gemm", "backward", "wgrad"],
                     default="layer",
                     help="layer: the MoE expert-layer forward (the headline); router_gemm: the "
@@ -110,7 +122,8 @@ def config_dict(a, world):
             "topk": a.topk, "ffn": a.ffn, "routing": a.routing,
             "parallelism": f"ep{world}" if world > 1 else "single",
             **({"ep_transport": resolve_transport(a.transport, world),
-                "ep_placement": a.placement} if world > 1 else {}),
+                "ep_placement": a.placement,
+                "ep_overlap_chunks": overlap_chunks(a, world)} if world > 1 else {}),
             "l2": "no flush: every step streams >22 GB of expert weights and 0.25 GB of "
                   "activations, both larger than the 126 MB L2"}
 
@@ -344,7 +357,7 @@ def check_ep(layer, x, logits, bias, w, k, placement, world, rank, dev):
     torch.cuda.synchronize()
     same = bool(torch.equal(out, out_ep))
     chk = check_layer(out, mid, x, logits, bias, w1_all, w2_all, k, placement)
-    derr = layer.plan.device_error() + full.plan.device_error()
+    derr = device_error(layer) + full.plan.device_error()
     ok = torch.tensor([1 if (same and chk["ok"] and derr == 0) else 0], device=dev)
     dist.all_reduce(ok, op=dist.ReduceOp.MIN)
     del out, mid, full, w1_all, w2_all, out_ep
@@ -812,7 +825,7 @@ def main():
                                      dtype=torch.int32, device=dev)
         layer = MoELayerEP(w, e, topk=k, expert_bias=bias,
                            transport=resolve_transport(a.transport, world), tokens=t,
-                           placement=placement)
+                           placement=placement, overlap_chunks=overlap_chunks(a, world))
         stage_names = ["start", "local_dispatch", "a2a_dispatch", "fc1", "fc2", "a2a_combine",
                        "combine"]
 
@@ -836,7 +849,7 @@ def main():
     for _ in range(a.warmup):
         layer(x, logits)
     torch.cuda.synchronize()
-    assert layer.plan.device_error() == 0, "grouped GEMM reported a device error"
+    assert device_error(layer) == 0, "grouped GEMM reported a device error"
 
     # Host-buffer copies of the inputs for the end-to-end windows.
     pipe = None
@@ -920,7 +933,7 @@ def main():
         n0, n1 = stage_names[i - 1], stage_names[i]
         stage_ms[n1] = sum(ev[n0].elapsed_time(ev[n1]) for ev in events) / a.steps
     fc1_ms = stage_ms["fc1"]
-    fc1_rows = t * k if world == 1 else int(layer.plan._keep.sum().item())
+    fc1_rows = t * k if world == 1 else int(layer.last_recv_rows)
     fc2_ms = stage_ms["fc2"]
 
     ms_step = agree_max(dev_ms / a.steps)

@@ -295,6 +295,18 @@ int moe_ep_dispatch(const void* x, const int64_t* row_id_map_te, const int64_t* 
                     const int64_t* expert_deltas, int32_t ranks, int32_t experts_per_rank,
                     int64_t cap_rows, int64_t T, int64_t H, int64_t E, int64_t num_rows,
                     moe_stream_t stream);
+/* One chunk of the fused dispatch, for overlapping the exchange with the    */
+/* grouped GEMMs (the comm/compute overlap of the deep_ep FusedDispatch the   */
+/* reference names, kernel_cases/case22_ref_moe_permute_mask_kernel_true.py: */
+/* 3-6): as moe_ep_dispatch, restricted to the (t, e) whose local expert     */
+/* index e % experts_per_rank is in [local_lo, local_hi). The kernel is      */
+/* persistent over tokens with at most max_ctas 128-thread CTAs (0 = one per */
+/* token), small enough to run beside a grouped GEMM on another stream.      */
+int moe_ep_dispatch_range(const void* x, const int64_t* row_id_map_te, const int64_t* peer_bases,
+                          const int64_t* expert_deltas, int32_t ranks, int32_t experts_per_rank,
+                          int64_t cap_rows, int64_t T, int64_t H, int64_t E, int64_t num_rows,
+                          int32_t local_lo, int32_t local_hi, int32_t max_ctas,
+                          moe_stream_t stream);
 /* Fused combine: out[t] = bf16(sum over e ascending of probs[t,e] * row),   */
 /* each row read from rank e / experts_per_rank's buffer at map[t,e] +       */
 /* expert_deltas[e] (device array); probs null = unweighted. Same arithmetic */

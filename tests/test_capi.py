@@ -90,6 +90,15 @@ def test_invalid_arguments_are_rejected_without_launch(lib):
     assert b"multiple of 8" in lib.moe_b200_last_error()
     assert sb(17, 16, 16, 4, 16, None) == 1  # misaligned
     assert sb(None, None, None, 0, 16, None) == 0
+    # one chunk of the fused EP dispatch: the local expert range must lie in
+    # [0, experts_per_rank); an empty range launches nothing
+    dr = lib.moe_ep_dispatch_range
+    bases = (ctypes.c_int64 * 2)(256, 512)
+    assert dr(16, 16, bases, 16, 2, 4, 64, 8, 64, 8, 32, 3, 5, 0, None) == 1
+    assert b"local expert range" in lib.moe_b200_last_error()
+    assert dr(16, 16, bases, 16, 2, 4, 64, 8, 64, 8, 32, 2, 1, 0, None) == 1
+    assert dr(16, 16, bases, 16, 2, 4, 64, 8, 64, 8, 32, 0, 2, -1, None) == 1
+    assert dr(16, 16, bases, 16, 2, 4, 64, 8, 64, 8, 32, 2, 2, 0, None) == 0
 
 
 def test_ops_refuse_cpu_tensors():

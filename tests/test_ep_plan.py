@@ -101,3 +101,18 @@ def test_expert_major_layout(world, experts, seed):
                   for i in range(counts[s, d * el + j])]
         np.testing.assert_array_equal(recv[d][:lay.recv_rows[d]], np.array(expect).reshape(-1, 3))
         assert (recv[d][lay.recv_rows[d]:] == -1).all()
+
+
+@pytest.mark.parametrize("el,chunks", [(32, 2), (32, 3), (2, 2), (7, 4), (128, 1)])
+def test_overlap_chunks_cover_every_local_expert_once(el, chunks):
+    """The overlapped EP path dispatches and multiplies the local experts in
+    contiguous chunks; together they must cover each local expert once, in
+    order (so the receive rows and GEMM groups equal the unchunked ones)."""
+    from moe_b200.ep import MoELayerEP
+    bounds = MoELayerEP.chunk_bounds(el, chunks)
+    assert len(bounds) == chunks
+    assert bounds[0][0] == 0 and bounds[-1][1] == el
+    for (a, b), (c, d) in zip(bounds, bounds[1:]):
+        assert a < b and b == c
+    sizes = [b - a for a, b in bounds]
+    assert max(sizes) - min(sizes) <= 1

@@ -37,7 +37,7 @@ def _problem(world, t, h, e, f, routing):
     return x, lg, bias, w1, w2
 
 
-def _worker(rank, world, port, routing, transport, q, placed=False):
+def _worker(rank, world, port, routing, transport, q, placed=False, chunks=1):
     for p in (str(PKG), str(ROOT), str(GOLDEN)):
         if p not in sys.path:
             sys.path.insert(0, p)
@@ -63,13 +63,14 @@ def _worker(rank, world, port, routing, transport, q, placed=False):
         local = moe_b200.MoEWeights(w1[rank * el:(rank + 1) * el].to(dev).contiguous(),
                                     w2[rank * el:(rank + 1) * el].to(dev).contiguous())
         layer = MoELayerEP(local, e, topk=k, expert_bias=bias.to(dev), transport=transport,
-                           tokens=t, placement=pl.to(dev) if placed else None)
+                           tokens=t, placement=pl.to(dev) if placed else None,
+                           overlap_chunks=chunks)
         out = layer(x[sl].to(dev), lg[sl].to(dev))
         out2 = layer(x[sl].to(dev), lg[sl].to(dev))  # buffers reused across forwards
         assert torch.equal(out, out2)
         outs = [torch.empty_like(out) for _ in range(world)]
         dist.all_gather(outs, out)
-        err = layer.plan.device_error()
+        err = layer.device_error()
         ok = None
         if rank == 0:
             full = moe_b200.MoELayer(moe_b200.MoEWeights(w1.to(dev), w2.to(dev)), topk=k,
@@ -97,7 +98,11 @@ def _worker(rank, world, port, routing, transport, q, placed=False):
                                                      (2, "zipf", "fused_dedup"),
                                                      (4, "uniform", "fused_dedup"),
                                                      (4, "zipf", "fused_dedup+placed"),
-                                                     (8, "zipf", "fused_dedup+placed")])
+                                                     (8, "zipf", "fused_dedup+placed"),
+                                                     (2, "zipf", "fused+overlap2"),
+                                                     (2, "uniform", "fused+placed+overlap3"),
+                                                     (4, "zipf", "fused+placed+overlap2"),
+                                                     (8, "zipf", "fused+placed+overlap2")])
 def test_ep_equals_single_gpu(world, routing, transport):
     if not torch.cuda.is_available():
         pytest.fail("GPU test selected but no CUDA device is visible")
@@ -107,9 +112,11 @@ def test_ep_equals_single_gpu(world, routing, transport):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    placed = transport.endswith("+placed")
-    tr = transport.split("+")[0]
-    procs = [ctx.Process(target=_worker, args=(r, world, port, routing, tr, q, placed))
+    parts = transport.split("+")
+    placed = "placed" in parts
+    chunks = int(next((p[len("overlap"):] for p in parts if p.startswith("overlap")), 1))
+    tr = parts[0]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, routing, tr, q, placed, chunks))
              for r in range(world)]
     for p in procs:
         p.start()
