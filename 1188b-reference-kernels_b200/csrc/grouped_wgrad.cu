@@ -64,9 +64,13 @@ struct Params {
   const int32_t* gid;       // [Gnz] their group ids
   int32_t* err;
   __nv_bfloat16* out;  // dW [G, N, K]
-  int G, N, K;         // G = groups with rows
+  int G, N, K;         // G = groups with rows (when gnz is null)
   int m_tiles, n_tiles;
+  const int32_t* gnz;  // device count of groups with rows (built by wgrad_table_kernel), or null
 };
+
+// Groups with rows: from the device table when it was built on the device.
+MOE_DEVICE int groups_with_rows(const Params& p) { return p.gnz != nullptr ? __ldg(p.gnz) : p.G; }
 
 MOE_DEVICE void tensormap_acquire(const void* tmap) {
   asm volatile("fence.proxy.tensormap::generic.acquire.gpu [%0], 128;" ::"l"(
@@ -128,7 +132,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const long long per_g = static_cast<long long>(p.m_tiles) * p.n_tiles;
-  const long long total = per_g * p.G;
+  const long long total = per_g * groups_with_rows(p);
   // g: index into the tables (and maps); p.gid[g] is the group's id in dW.
   auto locate = [&](long long t, int& g, int& mi, int& ni) {
     g = static_cast<int>(t / per_g);
@@ -403,7 +407,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t tmem_base = *tmem_slot;
 
   const long long per_g = static_cast<long long>(p.m_tiles) * p.n_tiles;
-  const long long total = per_g * p.G;
+  const long long total = per_g * groups_with_rows(p);
   auto locate = [&](long long t, int& g, int& mi, int& ni) {
     g = static_cast<int>(t / per_g);
     const int r = static_cast<int>(t - g * per_g);
@@ -660,6 +664,144 @@ int encode_bf16(CUtensorMap* m, const void* ptr, uint64_t inner, uint64_t outer,
   return MOE_OK;
 }
 
+// ---------------------------------------------------------------------------
+// Group table built on the device, so no call waits for the stream: the host
+// encodes one tensor map over all of dy and one over all of x (templates);
+// wgrad_table_kernel compacts the groups with rows and writes, for each, a copy
+// of both templates whose global address and outer extent it replaces
+// (tensormap.replace) with the group's first row and row count. The splits
+// come from device memory or, for the host-array entry point, by value in the
+// kernel parameters (at most kHostSplitsMax groups).
+// ---------------------------------------------------------------------------
+constexpr int kHostSplitsMax = 4096;
+struct HostSplits {
+  int32_t v[kHostSplitsMax];
+};
+constexpr int kErrBadSplits = 4;  // device error word: a negative count or sum(m) > rows
+
+MOE_DEVICE int32_t split_of(const int32_t* m_dev, const HostSplits& hs, int g) {
+  return m_dev != nullptr ? __ldg(m_dev + g) : hs.v[g];
+}
+
+// Writes the template map to dst (global), then points it at `addr` with
+// `rows` rows. tensormap.replace works on the object in the generic proxy,
+// after this thread's own stores of the template.
+MOE_DEVICE void store_group_map(CUtensorMap* dst, const CUtensorMap& tmpl, uint64_t addr,
+                                uint32_t rows) {
+  const uint4* src = reinterpret_cast<const uint4*>(&tmpl);
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) d[i] = src[i];
+  asm volatile("tensormap.replace.tile.global_address.global.b1024.b64 [%0], %1;" ::"l"(dst),
+               "l"(addr)
+               : "memory");
+  asm volatile("tensormap.replace.tile.global_dim.global.b1024.b32 [%0], 1, %1;" ::"l"(dst),
+               "r"(rows)
+               : "memory");
+}
+
+__global__ void __launch_bounds__(1024) wgrad_table_kernel(
+    const int32_t* __restrict__ m_dev, const __grid_constant__ HostSplits hs, int G,
+    int64_t rows_total, const __grid_constant__ CUtensorMap tmpl_dy,
+    const __grid_constant__ CUtensorMap tmpl_x, const char* dy, const char* x, int64_t N,
+    int64_t K, int32_t* __restrict__ rows_out, int32_t* __restrict__ gid_out,
+    CUtensorMap* __restrict__ maps_out, int32_t* __restrict__ gnz_out, int32_t* __restrict__ err) {
+  __shared__ int64_t w_rows[32];
+  __shared__ int w_nz[32];
+  __shared__ int64_t carry_rows;
+  __shared__ int carry_nz;
+  __shared__ int bad;
+  const int lane = lane_id(), wid = warp_id();
+  if (threadIdx.x == 0) {
+    carry_rows = 0;
+    carry_nz = 0;
+    bad = 0;
+  }
+  __syncthreads();
+  for (int g0 = 0; g0 < G; g0 += 1024) {
+    const int g = g0 + static_cast<int>(threadIdx.x);
+    int32_t m = g < G ? split_of(m_dev, hs, g) : 0;
+    if (m < 0) {
+      bad = 1;
+      m = 0;
+    }
+    int64_t r_incl = m;
+    int nz_incl = m > 0 ? 1 : 0;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int64_t yr = __shfl_up_sync(0xffffffffu, r_incl, off);
+      const int yn = __shfl_up_sync(0xffffffffu, nz_incl, off);
+      if (lane >= off) {
+        r_incl += yr;
+        nz_incl += yn;
+      }
+    }
+    if (lane == 31) {
+      w_rows[wid] = r_incl;
+      w_nz[wid] = nz_incl;
+    }
+    __syncthreads();
+    if (wid == 0) {
+      int64_t a = w_rows[lane];
+      int b = w_nz[lane];
+      const int64_t a0 = a;
+      const int b0 = b;
+#pragma unroll
+      for (int off = 1; off < 32; off <<= 1) {
+        const int64_t ya = __shfl_up_sync(0xffffffffu, a, off);
+        const int yb = __shfl_up_sync(0xffffffffu, b, off);
+        if (lane >= off) {
+          a += ya;
+          b += yb;
+        }
+      }
+      w_rows[lane] = a - a0;  // exclusive prefix of the warps before
+      w_nz[lane] = b - b0;
+    }
+    __syncthreads();
+    const int64_t start = carry_rows + w_rows[wid] + r_incl - m;
+    const int idx = carry_nz + w_nz[wid] + nz_incl - (m > 0 ? 1 : 0);
+    if (m > 0) {
+      if (start + m > rows_total) {
+        bad = 1;  // the maps would reach past dy / x: emit nothing
+      } else {
+        rows_out[idx] = m;
+        gid_out[idx] = g;
+        store_group_map(maps_out + 2 * idx, tmpl_dy,
+                        reinterpret_cast<uint64_t>(dy) + static_cast<uint64_t>(start * N * 2),
+                        static_cast<uint32_t>(m));
+        store_group_map(maps_out + 2 * idx + 1, tmpl_x,
+                        reinterpret_cast<uint64_t>(x) + static_cast<uint64_t>(start * K * 2),
+                        static_cast<uint32_t>(m));
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 1023) {
+      carry_rows = start + m;
+      carry_nz = idx + (m > 0 ? 1 : 0);
+    }
+    __syncthreads();
+  }
+  asm volatile("fence.proxy.tensormap::generic.release.gpu;" ::: "memory");
+  if (threadIdx.x == 0) {
+    *gnz_out = bad ? 0 : carry_nz;
+    if (bad) atomicCAS(err, 0, kErrBadSplits);
+  }
+}
+
+// dW[g] = 0 for every group without rows (torch.mm over zero rows).
+__global__ void __launch_bounds__(256) wgrad_zero_empty_kernel(
+    uint4* __restrict__ dw, const int32_t* __restrict__ m_dev, const __grid_constant__ HostSplits hs,
+    int64_t slice_vec) {
+  const int g = static_cast<int>(blockIdx.y);
+  if (split_of(m_dev, hs, g) != 0) return;
+  uint4* d = dw + static_cast<int64_t>(g) * slice_vec;
+  const uint4 z = make_uint4(0u, 0u, 0u, 0u);
+  for (int64_t i = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; i < slice_vec;
+       i += static_cast<int64_t>(gridDim.x) * blockDim.x)
+    d[i] = z;
+}
+
 size_t rows_bytes(int64_t G) { return (static_cast<size_t>(G) * 4 + 255) & ~static_cast<size_t>(255); }
 size_t ws_bytes(int64_t G) {
   return 256 + 2 * rows_bytes(G) + 2 * static_cast<size_t>(G) * sizeof(CUtensorMap);
@@ -727,112 +869,91 @@ extern "C" int moe_grouped_wgrad_workspace_size(int64_t G, size_t* bytes) {
   return MOE_OK;
 }
 
-extern "C" int moe_grouped_wgrad(const void* dy, const void* x, void* dw, int64_t rows_total,
-                                 int64_t G, int64_t N, int64_t K, const int32_t* m_splits,
-                                 void* workspace, size_t workspace_bytes, moe_stream_t stream) {
-  MOE_REQUIRE(G >= 1 && G <= (1 << 20), "grouped_wgrad: G=%lld out of range", (long long)G);
-  MOE_REQUIRE(rows_total >= 0 && rows_total < (1ll << 31), "grouped_wgrad: rows=%lld out of range",
+// dW of both entry points: m_dev (device) or m_host (host array, G <= 4096,
+// passed by value), never both. Nothing here waits for the stream.
+static int grouped_wgrad_run(const void* dy, const void* x, void* dw, int64_t rows_total,
+                             int64_t G, int64_t N, int64_t K, const int32_t* m_dev,
+                             const int32_t* m_host, void* workspace, size_t workspace_bytes,
+                             moe_stream_t stream, const char* who) {
+  MOE_REQUIRE(rows_total >= 0 && rows_total < (1ll << 31), "%s: rows=%lld out of range", who,
               (long long)rows_total);
   MOE_REQUIRE(N >= 8 && N % 8 == 0 && K >= 8 && K % 8 == 0,
-              "grouped_wgrad: N=%lld and K=%lld must be positive multiples of 8", (long long)N,
+              "%s: N=%lld and K=%lld must be positive multiples of 8", who, (long long)N,
               (long long)K);
-  MOE_REQUIRE(G * N < (1ll << 31), "grouped_wgrad: G*N too large");
-  MOE_REQUIRE(m_splits != nullptr, "grouped_wgrad: null m_splits (host array of G counts)");
+  MOE_REQUIRE(G * N < (1ll << 31), "%s: G*N too large", who);
   MOE_REQUIRE(workspace != nullptr && workspace_bytes >= gw::ws_bytes(G) &&
                   (reinterpret_cast<uintptr_t>(workspace) & 255) == 0,
-              "grouped_wgrad: workspace must hold %zu bytes, 256-byte aligned", gw::ws_bytes(G));
-  MOE_REQUIRE(dy && x && dw, "grouped_wgrad: null pointer");
+              "%s: workspace must hold %zu bytes, 256-byte aligned", who, gw::ws_bytes(G));
+  MOE_REQUIRE(dy && x && dw, "%s: null pointer", who);
   MOE_REQUIRE(((reinterpret_cast<uintptr_t>(dy) | reinterpret_cast<uintptr_t>(x) |
                 reinterpret_cast<uintptr_t>(dw)) & 15) == 0,
-              "grouped_wgrad: dy, x and dw must be 16-byte aligned");
-  int64_t sum = 0;
-  for (int64_t g = 0; g < G; ++g) {
-    MOE_REQUIRE(m_splits[g] >= 0, "grouped_wgrad: m_splits[%lld] < 0", (long long)g);
-    sum += m_splits[g];
+              "%s: dy, x and dw must be 16-byte aligned", who);
+  gw::HostSplits hs{};
+  int64_t sum = rows_total;  // device splits: the rows are the estimate below
+  int64_t gnz_host = G;
+  if (m_host != nullptr) {
+    sum = 0;
+    gnz_host = 0;
+    for (int64_t g = 0; g < G; ++g) {
+      MOE_REQUIRE(m_host[g] >= 0, "%s: m_splits[%lld] < 0", who, (long long)g);
+      sum += m_host[g];
+      gnz_host += m_host[g] > 0 ? 1 : 0;
+      hs.v[g] = m_host[g];
+    }
+    MOE_REQUIRE(sum <= rows_total, "%s: sum(m_splits)=%lld exceeds rows=%lld", who,
+                (long long)sum, (long long)rows_total);
   }
-  MOE_REQUIRE(sum <= rows_total, "grouped_wgrad: sum(m_splits)=%lld exceeds rows=%lld",
-              (long long)sum, (long long)rows_total);
   int st = gw::ensure_smem_attr();
   if (st) return st;
-
-  // Host image of the workspace after the error word, for the groups with
-  // rows only: row counts, group ids, then the tensor maps (dy rows, x rows).
-  const size_t rb = gw::rows_bytes(G);
-  std::vector<int32_t> rows_nz, gid_nz;
-  std::vector<CUtensorMap> maps;
-  const char* dyb = static_cast<const char*>(dy);
-  const char* xb = static_cast<const char*>(x);
-  int64_t r0 = 0;
-  for (int64_t g = 0; g < G; ++g) {
-    const int64_t m = m_splits[g];
-    if (m > 0) {
-      CUtensorMap a, b;
-      if ((st = gw::encode_bf16(&a, dyb + r0 * N * 2, static_cast<uint64_t>(N),
-                                static_cast<uint64_t>(m), 64u, 64u, CU_TENSOR_MAP_SWIZZLE_128B)) ||
-          (st = gw::encode_bf16(&b, xb + r0 * K * 2, static_cast<uint64_t>(K),
-                                static_cast<uint64_t>(m), 64u, 64u, CU_TENSOR_MAP_SWIZZLE_128B)))
-        return st;
-      maps.push_back(a);
-      maps.push_back(b);
-      rows_nz.push_back(static_cast<int32_t>(m));
-      gid_nz.push_back(static_cast<int32_t>(g));
-    }
-    r0 += m;
-  }
-  const int64_t gnz = static_cast<int64_t>(rows_nz.size());
-  std::vector<uint8_t> host(2 * rb + maps.size() * sizeof(CUtensorMap), 0);
-  if (gnz > 0) {
-    memcpy(host.data(), rows_nz.data(), rows_nz.size() * 4);
-    memcpy(host.data() + rb, gid_nz.data(), gid_nz.size() * 4);
-    memcpy(host.data() + 2 * rb, maps.data(), maps.size() * sizeof(CUtensorMap));
-  }
-  CUtensorMap tout;
-  st = gw::encode_bf16(&tout, dw, static_cast<uint64_t>(K), static_cast<uint64_t>(G * N), 64u,
-                       32u, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (st) return st;
-
   cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
   char* ws = static_cast<char*>(workspace);
-  MOE_CUDA_CALL(cudaMemsetAsync(ws, 0, 4, s), "grouped_wgrad: clear error word");
-  // dW of the groups without rows: zeros, one memset per run of such groups.
-  const size_t slice = static_cast<size_t>(N) * static_cast<size_t>(K) * 2;
-  for (int64_t g = 0; g < G;) {
-    if (m_splits[g] > 0) {
-      ++g;
-      continue;
-    }
-    int64_t e = g;
-    while (e < G && m_splits[e] == 0) ++e;
-    MOE_CUDA_CALL(cudaMemsetAsync(static_cast<char*>(dw) + g * slice, 0, (e - g) * slice, s),
-                  "grouped_wgrad: zero empty groups");
-    g = e;
-  }
-  if (gnz == 0) return MOE_OK;
-  // From pageable memory: returns once the bytes are staged, so `host` may go.
-  MOE_CUDA_CALL(cudaMemcpyAsync(ws + 256, host.data(), host.size(), cudaMemcpyHostToDevice, s),
-                "grouped_wgrad: upload group table");
-
+  const size_t rb = gw::rows_bytes(G);
+  int32_t* err = reinterpret_cast<int32_t*>(ws);
+  int32_t* gnz = reinterpret_cast<int32_t*>(ws + 4);
+  MOE_CUDA_CALL(cudaMemsetAsync(ws, 0, 8, s), "grouped_wgrad: clear error word");
+  int dev = 0;
+  MOE_CUDA_CALL(cudaGetDevice(&dev), "cudaGetDevice");
+  // dW of the groups without rows: zeros.
+  const int64_t slice_vec = N * K * 2 / 16;
+  const unsigned zx = static_cast<unsigned>(std::min<int64_t>((slice_vec + 255) / 256, 64));
+  gw::wgrad_zero_empty_kernel<<<dim3(zx, static_cast<unsigned>(G)), 256, 0, s>>>(
+      static_cast<uint4*>(dw), m_dev, hs, slice_vec);
+  MOE_CUDA_CHECK_LAUNCH("grouped_wgrad zero launch");
+  if (rows_total == 0 || gnz_host == 0 || sum == 0) return MOE_OK;
+  CUtensorMap tdy, tx, tout;
+  if ((st = gw::encode_bf16(&tdy, dy, static_cast<uint64_t>(N), static_cast<uint64_t>(rows_total),
+                            64u, 64u, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (st = gw::encode_bf16(&tx, x, static_cast<uint64_t>(K), static_cast<uint64_t>(rows_total),
+                            64u, 64u, CU_TENSOR_MAP_SWIZZLE_128B)) ||
+      (st = gw::encode_bf16(&tout, dw, static_cast<uint64_t>(K), static_cast<uint64_t>(G * N),
+                            64u, 32u, CU_TENSOR_MAP_SWIZZLE_128B)))
+    return st;
   gw::Params p;
   p.maps = reinterpret_cast<const CUtensorMap*>(ws + 256 + 2 * rb);
   p.rows = reinterpret_cast<const int32_t*>(ws + 256);
   p.gid = reinterpret_cast<const int32_t*>(ws + 256 + rb);
-  p.err = reinterpret_cast<int32_t*>(ws);
+  p.err = err;
   p.out = static_cast<__nv_bfloat16*>(dw);
-  p.G = static_cast<int>(gnz);
+  p.G = static_cast<int>(G);  // upper bound; the kernels read the device count
+  p.gnz = gnz;
   p.N = static_cast<int>(N);
   p.K = static_cast<int>(K);
-  int dev = 0;
-  MOE_CUDA_CALL(cudaGetDevice(&dev), "cudaGetDevice");
+  gw::wgrad_table_kernel<<<1, 1024, 0, s>>>(
+      m_dev, hs, static_cast<int>(G), rows_total, tdy, tx, static_cast<const char*>(dy),
+      static_cast<const char*>(x), N, K, const_cast<int32_t*>(p.rows), const_cast<int32_t*>(p.gid),
+      reinterpret_cast<CUtensorMap*>(ws + 256 + 2 * rb), gnz, err);
+  MOE_CUDA_CHECK_LAUNCH("grouped_wgrad table launch");
   // CTA pairs when the groups are deep enough for the MMA to dominate (a
   // 256 x 256 pair tile moves two thirds of the operand bytes per SM of the
   // single-CTA tile); with a few k-blocks per tile the kernel is bound by
   // writing dW, where the single-CTA kernel measured faster (case09's ~100
-  // rows per group: 686 vs 1016 us).
+  // rows per group: 686 vs 1016 us). Host splits give the exact mean rows of
+  // the groups with rows; device splits, the mean over all G groups.
   const int clusters = gw::pair_clusters(dev);
-  if (clusters > 0 && sum >= gw::kPairMinRows * gnz) {  // 256 x 256 tiles on CTA pairs
+  if (clusters > 0 && sum >= gw::kPairMinRows * gnz_host) {  // 256 x 256 tiles on CTA pairs
     p.m_tiles = static_cast<int>((N + gw::kPairTile - 1) / gw::kPairTile);
     p.n_tiles = static_cast<int>((K + gw::kPairTile - 1) / gw::kPairTile);
-    const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles * gnz;
+    const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles * gnz_host;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(static_cast<unsigned>(2 * std::min<int64_t>(tiles, clusters)));
     cfg.blockDim = dim3(gw::kThreads);
@@ -851,9 +972,30 @@ extern "C" int moe_grouped_wgrad(const void* dy, const void* x, void* dw, int64_
   }
   p.m_tiles = static_cast<int>((N + gw::BM - 1) / gw::BM);
   p.n_tiles = static_cast<int>((K + gw::BN - 1) / gw::BN);
-  const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles * gnz;
+  const int64_t tiles = static_cast<int64_t>(p.m_tiles) * p.n_tiles * gnz_host;
   const int grid = static_cast<int>(std::min<int64_t>(tiles, num_sms(dev)));
   gw::grouped_wgrad_kernel<<<grid, gw::kThreads, gw::kSmemBytes, s>>>(tout, p);
   MOE_CUDA_CHECK_LAUNCH("grouped_wgrad launch");
   return MOE_OK;
+}
+
+extern "C" int moe_grouped_wgrad(const void* dy, const void* x, void* dw, int64_t rows_total,
+                                 int64_t G, int64_t N, int64_t K, const int32_t* m_splits,
+                                 void* workspace, size_t workspace_bytes, moe_stream_t stream) {
+  MOE_REQUIRE(G >= 1 && G <= gw::kHostSplitsMax,
+              "grouped_wgrad: G=%lld out of [1,%d] (larger G: moe_grouped_wgrad_dev)",
+              (long long)G, gw::kHostSplitsMax);
+  MOE_REQUIRE(m_splits != nullptr, "grouped_wgrad: null m_splits (host array of G counts)");
+  return grouped_wgrad_run(dy, x, dw, rows_total, G, N, K, nullptr, m_splits, workspace,
+                           workspace_bytes, stream, "grouped_wgrad");
+}
+
+extern "C" int moe_grouped_wgrad_dev(const void* dy, const void* x, void* dw, int64_t rows_total,
+                                     int64_t G, int64_t N, int64_t K, const int32_t* m_splits,
+                                     void* workspace, size_t workspace_bytes,
+                                     moe_stream_t stream) {
+  MOE_REQUIRE(G >= 1 && G <= (1 << 20), "grouped_wgrad_dev: G=%lld out of range", (long long)G);
+  MOE_REQUIRE(m_splits != nullptr, "grouped_wgrad_dev: null m_splits (device array of G counts)");
+  return grouped_wgrad_run(dy, x, dw, rows_total, G, N, K, m_splits, nullptr, workspace,
+                           workspace_bytes, stream, "grouped_wgrad_dev");
 }

@@ -9,7 +9,7 @@ The reference-style ``kernel_function`` entry points live in ``bundles/``.
 """
 from ._lib import MoeError, load as load_library
 from .ops import (GroupedGemmPlan, RouterOutput, RowIdMap, combine_backward, grouped_gemm,
-                  grouped_wgrad, permute,
+                  grouped_wgrad, grouped_wgrad_device_error, permute,
                   permute_backward, permute_trans, router_device_error, router_gemm_topk,
                   router_logits, router_topk, row_id_map, swiglu, swiglu_backward,
                   topk, unpermute, unpermute_weighted)
@@ -18,7 +18,7 @@ from .layer import HostPipeline, MoELayer, MoEWeights, moe_layer_fwd
 __all__ = [
     "MoeError", "load_library", "GroupedGemmPlan", "RouterOutput", "RowIdMap", "combine_backward",
     "grouped_gemm",
-    "grouped_wgrad",
+    "grouped_wgrad", "grouped_wgrad_device_error",
     "permute", "permute_backward", "permute_trans", "router_device_error", "router_gemm_topk",
     "router_logits", "router_topk", "row_id_map",
     "swiglu", "swiglu_backward", "topk", "unpermute", "unpermute_weighted",

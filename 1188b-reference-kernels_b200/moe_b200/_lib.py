@@ -77,6 +77,8 @@ _SIGNATURES = {
     "moe_grouped_wgrad_workspace_size": [c_int64, POINTER(c_size_t)],
     "moe_grouped_wgrad": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
                           c_void_p, c_void_p, c_size_t, c_void_p],
+    "moe_grouped_wgrad_dev": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
+                              c_void_p, c_void_p, c_size_t, c_void_p],
     "moe_grouped_gemm_nn": [c_void_p, c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64,
                          c_int64, c_int32, c_void_p, c_size_t, c_void_p],
     "moe_grouped_gemm_check": [c_void_p, c_size_t, c_void_p, POINTER(c_int32)],
@@ -111,7 +113,8 @@ _LAUNCHES = {"moe_topk_f32": 1, "moe_router_topk": 1, "moe_router_topk_placed": 
              "moe_permute_backward": 1, "moe_ep_dispatch_dedup": 1, "moe_ep_expand": 1,
              "moe_combine_backward": 1, "moe_swiglu_backward": 1,
              "moe_grouped_gemm_plan_splits": 1, "moe_grouped_gemm_plan_ep": 1,
-             "moe_grouped_gemm": 2, "moe_grouped_gemm_nn": 2, "moe_grouped_wgrad": 1,
+             "moe_grouped_gemm": 2, "moe_grouped_gemm_nn": 2, "moe_grouped_wgrad": 3,
+             "moe_grouped_wgrad_dev": 3,
              "moe_swiglu": 1}
 launch_count = 0
 

@@ -154,16 +154,15 @@ class MoELayer:
         if grad_out.shape != (t, h):
             raise ValueError(f"grad_out must be [{t},{h}]")
         # The group table of this forward's routing (another forward since may
-        # have replaced the layer's), and its row counts on the host for the
-        # wgrad tensor maps.
+        # have replaced the layer's); the wgrad takes the same device counts,
+        # so the backward never waits for the GPU.
         self.plan.from_splits(rim.counts, 1)
-        splits = rim.counts.cpu().tolist()
         dy2, grad_probs = ops.combine_backward(grad_out, ctx["y"], rim.map_te, r.probs)
         dh = ops.grouped_gemm(dy2, self.w.w2, plan=self.plan, w_layout="KN")
-        dw2 = ops.grouped_wgrad(dy2, ctx["h"], splits)
+        dw2 = ops.grouped_wgrad(dy2, ctx["h"], rim.counts)
         dy1 = ops.swiglu_backward(ctx["y1"], dh)
         dxp = ops.grouped_gemm(dy1, self.w.w1, plan=self.plan, w_layout="KN")
-        dw1 = ops.grouped_wgrad(dy1, ctx["xp"], splits)
+        dw1 = ops.grouped_wgrad(dy1, ctx["xp"], rim.counts)
         grad_x = ops.unpermute(dxp, rim.map_te, None, token_major=True)
         return grad_x, grad_probs, dw1, dw2
 

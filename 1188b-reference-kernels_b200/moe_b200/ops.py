@@ -22,7 +22,7 @@ from . import _lib
 __all__ = [
     "topk", "router_topk", "RouterOutput", "row_id_map", "RowIdMap", "permute",
     "permute_trans", "unpermute", "unpermute_weighted", "grouped_gemm", "GroupedGemmPlan",
-    "grouped_wgrad", "swiglu", "router_logits", "router_gemm_topk", "router_gemm_fusable",
+    "grouped_wgrad", "grouped_wgrad_device_error", "swiglu", "router_logits", "router_gemm_topk", "router_gemm_fusable",
     "router_device_error", "permute_backward", "combine_backward", "swiglu_backward",
 ]
 
@@ -498,20 +498,28 @@ def grouped_wgrad(dy: torch.Tensor, x: torch.Tensor,
     groups contiguous in order), fp32 accumulation; an empty group gives
     zeros. The torch.mm(dy[seg].t(), x[seg]) loop of kernel_cases/
     case05_moe_grouped_gemm_fc2_wgrad.py:49-64 / case09_moe_grouped_gemm_fc1_
-    wgrad.py:49-64. m_splits are needed on the host (a CUDA tensor is read
-    back, which synchronises): they size each group's tensor maps.
+    wgrad.py:49-64. m_splits: a CUDA int tensor (e.g. the expert counts of
+    row_id_map; used where it is, no host sync) or host counts (G <= 4096).
+    The group table and per-group tensor maps are built on the device.
     """
     for n_, t_ in (("dy", dy), ("x", x)):
         _need_cuda(n_, t_)
         _need_dtype(n_, t_, torch.bfloat16)
     if dy.dim() != 2 or x.dim() != 2 or dy.shape[0] != x.shape[0]:
         raise ValueError(f"shapes dy {tuple(dy.shape)} x {tuple(x.shape)}")
-    if isinstance(m_splits, torch.Tensor):
-        m_splits = m_splits.detach().cpu().tolist()
-    splits = [int(v) for v in m_splits]
-    if any(v < 0 for v in splits) or sum(splits) > dy.shape[0] or not splits:
-        raise ValueError("m_splits must be >= 0 and sum to at most the rows")
-    g = len(splits)
+    on_dev = isinstance(m_splits, torch.Tensor) and m_splits.is_cuda
+    if on_dev:
+        ms = m_splits.to(dtype=torch.int32).contiguous()
+        if ms.dim() != 1 or ms.numel() == 0 or ms.device != dy.device:
+            raise ValueError("device m_splits must be a 1-D tensor on dy's device")
+        g = ms.numel()
+    else:
+        if isinstance(m_splits, torch.Tensor):
+            m_splits = m_splits.tolist()
+        splits = [int(v) for v in m_splits]
+        if any(v < 0 for v in splits) or sum(splits) > dy.shape[0] or not splits:
+            raise ValueError("m_splits must be >= 0 and sum to at most the rows")
+        g = len(splits)
     dyc, xc = dy.contiguous(), x.contiguous()
     n, k = dyc.shape[1], xc.shape[1]
     dev = dyc.device
@@ -522,10 +530,34 @@ def grouped_wgrad(dy: torch.Tensor, x: torch.Tensor,
     nb = c_size_t(0)
     _lib.call("moe_grouped_wgrad_workspace_size", g, byref(nb))
     ws = _workspace(nb.value, dev)
-    host = (c_int32 * g)(*splits)
-    _lib.call("moe_grouped_wgrad", _p(dyc), _p(xc), _p(out), dyc.shape[0], g, n, k, host,
-              _p(ws), nb.value, _stream(dev))
+    if on_dev:
+        _lib.call("moe_grouped_wgrad_dev", _p(dyc), _p(xc), _p(out), dyc.shape[0], g, n, k,
+                  _p(ms), _p(ws), nb.value, _stream(dev))
+    else:
+        host = (c_int32 * g)(*splits)
+        _lib.call("moe_grouped_wgrad", _p(dyc), _p(xc), _p(out), dyc.shape[0], g, n, k, host,
+                  _p(ws), nb.value, _stream(dev))
+    _WGRAD_ERR[dev] = ws  # the error word of the last call on this device
     return out  # ws returns to torch's allocator, reused only after this stream's work
+
+
+# Workspace of the last grouped_wgrad per device (its first word is the
+# device error word, see grouped_wgrad_device_error).
+_WGRAD_ERR: dict = {}
+
+
+def grouped_wgrad_device_error(device) -> int:
+    """Error code the last grouped_wgrad on this device left (0: none;
+    4: a negative count or counts summing past the rows). Syncs."""
+    dev = torch.device(device)
+    if dev.index is None:
+        dev = torch.device(dev.type, torch.cuda.current_device())
+    ws = _WGRAD_ERR.get(dev)
+    if ws is None:
+        return 0
+    v = c_int32(0)
+    _lib.load().moe_grouped_gemm_check(_p(ws), ws.numel(), _stream(dev), byref(v))
+    return int(v.value)
 
 
 def router_logits(x: torch.Tensor, weight: torch.Tensor,

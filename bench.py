@@ -517,7 +517,6 @@ def run_backward(a):
     r = moe_b200.router_topk(logits, k, "softmax", True, zipf_bias(e, a.routing).to(dev),
                              outputs="maps")
     counts = moe_b200.row_id_map(r.routing_map, want_et=False).counts
-    splits = counts.cpu().tolist()
     rows = t * k
     w = moe_b200.MoEWeights.random(e, h, f, dev, seed=77)
     dy = torch.randn(rows, h, device=dev, generator=g).to(torch.bfloat16)
@@ -536,11 +535,11 @@ def run_backward(a):
         ev[0].record()
         moe_b200.grouped_gemm(dy, w.w2, plan=plan, out=dh, w_layout="KN")
         ev[1].record()
-        moe_b200.grouped_wgrad(dy, hm, splits, out=dw2)
+        moe_b200.grouped_wgrad(dy, hm, counts, out=dw2)
         ev[2].record()
         moe_b200.grouped_gemm(dz, w.w1, plan=plan, out=dx, w_layout="KN")
         ev[3].record()
-        moe_b200.grouped_wgrad(dz, xp, splits, out=dw1)
+        moe_b200.grouped_wgrad(dz, xp, counts, out=dw1)
         ev[4].record()
 
     sampler = ClockSampler(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0])

@@ -5,9 +5,10 @@
  * launches asynchronously on that stream and returns a moe_status. On a
  * non-zero status, moe_b200_last_error() returns a message for the calling
  * thread. Outputs are caller-allocated; inputs are only read. No entry point
- * synchronises the stream or allocates device memory; the ones that need
- * scratch take a caller-provided workspace whose size the matching
- * *_workspace_size function reports.
+ * synchronises the stream or allocates device memory (moe_grouped_gemm_check,
+ * which reads a device error word back to the host, is the one call that
+ * waits); the ones that need scratch take a caller-provided workspace whose
+ * size the matching *_workspace_size function reports.
  *
  * Each function names the reference interface it replaces. The reference
  * binds its kernels through pybind functions that take torch tensors and call
@@ -248,19 +249,28 @@ int moe_grouped_gemm_nn(const void* x, const void* w, void* out, int64_t x_rows,
 
 /* f3  Grouped weight gradient: dW[g] = dy[rows of g]^T @ x[rows of g],      */
 /* dy [rows_total, N], x [rows_total, K] bf16 row-major, groups contiguous   */
-/* in order with host-side row counts m_splits[G] (sum <= rows_total), dW    */
-/* [G, N, K] bf16 (fp32 accumulation); a group with no rows gets zeros.      */
+/* in order with row counts m_splits[G] (sum <= rows_total), dW [G, N, K]    */
+/* bf16 (fp32 accumulation); a group with no rows gets zeros.                */
 /* Replaces the torch.mm(dy[seg].t(), x[seg]) loop of kernel_cases/case05_   */
 /* moe_grouped_gemm_fc2_wgrad.py:49-64 and case09_moe_grouped_gemm_fc1_      */
-/* wgrad.py:49-64 ("TN"). The workspace (moe_grouped_wgrad_workspace_size)   */
-/* receives the group table and per-group tensor maps, uploaded on `stream`  */
-/* from host memory (the one entry point whose upload may wait for the       */
-/* stream's earlier work); its first 4 bytes are the device error word       */
-/* (read it with moe_grouped_gemm_check).                                    */
+/* wgrad.py:49-64 ("TN"). The group table and one pair of tensor maps per    */
+/* group with rows are built on the device, in the workspace                 */
+/* (moe_grouped_wgrad_workspace_size), from two host-encoded templates; its  */
+/* first 4 bytes are the device error word (read it with                     */
+/* moe_grouped_gemm_check; 4 = a negative count or sum(m_splits) beyond      */
+/* rows_total, in which case only the empty groups are written).             */
+/* moe_grouped_wgrad: m_splits is a host array, G <= 4096 (passed by value   */
+/* in the launch, so nothing waits for the stream).                          */
+/* moe_grouped_wgrad_dev: m_splits is a device array (e.g. the expert        */
+/* counts of moe_row_id_map), G <= 2^20; the CTA-pair kernel is chosen when  */
+/* rows_total / G >= 384.                                                    */
 int moe_grouped_wgrad_workspace_size(int64_t G, size_t* bytes);
 int moe_grouped_wgrad(const void* dy, const void* x, void* dw, int64_t rows_total, int64_t G,
                       int64_t N, int64_t K, const int32_t* m_splits, void* workspace,
                       size_t workspace_bytes, moe_stream_t stream);
+int moe_grouped_wgrad_dev(const void* dy, const void* x, void* dw, int64_t rows_total,
+                          int64_t G, int64_t N, int64_t K, const int32_t* m_splits,
+                          void* workspace, size_t workspace_bytes, moe_stream_t stream);
 
 /* Reads the device error word a previous moe_grouped_gemm left in the       */
 /* workspace (0 = none; blocking: synchronises the stream).                  */

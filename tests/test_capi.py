@@ -90,6 +90,13 @@ def test_invalid_arguments_are_rejected_without_launch(lib):
     assert b"multiple of 8" in lib.moe_b200_last_error()
     assert sb(17, 16, 16, 4, 16, None) == 1  # misaligned
     assert sb(None, None, None, 0, 16, None) == 0
+    # grouped wgrad: host counts travel in the launch (G <= 4096); device
+    # counts need a pointer
+    wg = lib.moe_grouped_wgrad
+    assert wg(16, 16, 16, 10, 5000, 64, 64, 16, 256, 1 << 30, None) == 1
+    assert b"4096" in lib.moe_b200_last_error()
+    assert lib.moe_grouped_wgrad_dev(16, 16, 16, 10, 8, 64, 64, None, 256, 1 << 30, None) == 1
+    assert b"device array" in lib.moe_b200_last_error()
     # one chunk of the fused EP dispatch: the local expert range must lie in
     # [0, experts_per_rank); an empty range launches nothing
     dr = lib.moe_ep_dispatch_range

@@ -244,6 +244,49 @@ def test_wgrad_ragged_vs_oracle(cuda_dev, splits, n, k):
             assert int(dw[gi].view(torch.int16).abs().sum()) == 0  # zeros, like torch.mm
 
 
+@pytest.mark.parametrize("splits,n,k", [
+    ([0, 1, 63, 64, 65, 200, 0, 128], 256, 256),
+    ([300, 77, 0, 1000], 384, 320),
+    ([600, 700, 0, 523, 640], 512, 1024),          # deep groups: rows / G >= 384, pair kernel
+])
+def test_wgrad_device_splits_equal_host_splits(cuda_dev, splits, n, k):
+    """moe_grouped_wgrad_dev (counts on the device, no host sync) gives the
+    same bits as the host-array entry point, including zeroed empty groups;
+    dW is prefilled with garbage so the zeros must be written."""
+    import moe_b200
+    g = torch.Generator().manual_seed(len(splits) + n)
+    rows = sum(splits) + 5
+    dy = _rand_bf16(g, rows, n).to(cuda_dev)
+    x = _rand_bf16(g, rows, k).to(cuda_dev)
+    host = moe_b200.grouped_wgrad(dy, x, splits)
+    out = torch.full((len(splits), n, k), 7.0, dtype=torch.bfloat16, device=cuda_dev)
+    dev = moe_b200.grouped_wgrad(dy, x, torch.tensor(splits, dtype=torch.int32, device=cuda_dev),
+                                 out=out)
+    assert moe_b200.grouped_wgrad_device_error(cuda_dev) == 0
+    assert torch.equal(dev.view(torch.int16), host.view(torch.int16))
+    assert_gemm_close(dev, _wgrad_f32(u16(dy), u16(x), splits), f"wgrad dev {splits}")
+
+
+def test_wgrad_device_splits_beyond_rows_report_an_error(cuda_dev):
+    """Device counts summing past the rows: the table builder emits no group
+    (no tensor map may reach past dy or x) and sets error word 4; the empty
+    groups are still zeroed. Host counts like that are refused up front."""
+    import moe_b200
+    from moe_b200 import MoeError
+    g = torch.Generator().manual_seed(5)
+    dy = _rand_bf16(g, 100, 128).to(cuda_dev)
+    x = _rand_bf16(g, 100, 256).to(cuda_dev)
+    out = torch.full((3, 128, 256), 7.0, dtype=torch.bfloat16, device=cuda_dev)
+    moe_b200.grouped_wgrad(dy, x, torch.tensor([60, 0, 60], dtype=torch.int32, device=cuda_dev),
+                           out=out)
+    assert moe_b200.grouped_wgrad_device_error(cuda_dev) == 4
+    assert int(out[1].view(torch.int16).abs().sum()) == 0
+    with pytest.raises(ValueError):
+        moe_b200.grouped_wgrad(dy, x, [60, 0, 60])
+    with pytest.raises(MoeError):
+        moe_b200.grouped_wgrad(dy, x, [0] * 4097)  # host counts: G <= 4096
+
+
 def test_wgrad_pair_kernel_many_tiles(cuda_dev):
     """Deep groups (the CTA-pair wgrad kernel) with more 256 x 256 tiles than
     CTA pairs, so every pair walks several tiles and groups: checked in full."""
