@@ -137,6 +137,25 @@ MOE_DEVICE void tma_load_2d(uint32_t dst, const void* tmap, int32_t x, int32_t y
       : "memory");
 }
 
+// Untiled bulk copy of `bytes` (a multiple of 16, both addresses 16-byte
+// aligned) from global memory into this CTA's shared memory; the bytes are
+// counted on the mbarrier.
+MOE_DEVICE void bulk_load(uint32_t dst_smem, const void* src, uint32_t bytes, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          dst_smem),
+      "l"(reinterpret_cast<uint64_t>(src)), "r"(bytes), "r"(bar)
+      : "memory");
+}
+// Untiled bulk copy from this CTA's shared memory to global memory, in the
+// issuing thread's current bulk async-group.
+MOE_DEVICE void bulk_store(void* dst, uint32_t src_smem, uint32_t bytes) {
+  asm volatile("cp.async.bulk.global.shared::cta.bulk_group [%0], [%1], %2;" ::"l"(
+                   reinterpret_cast<uint64_t>(dst)),
+               "r"(src_smem), "r"(bytes)
+               : "memory");
+}
+
 // TMA tile store from this CTA's shared memory (bulk async-group based).
 MOE_DEVICE void tma_store_2d(const void* tmap, int32_t x, int32_t y, uint32_t src) {
   asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(

@@ -13,6 +13,11 @@
 // kernel_cases/case22_ref_moe_permute_mask_kernel_true.py:47-69,
 // kernel_cases/case15_moe_unpermute_mask_fwd.py:58-64,
 // kernel_cases/case24_ref_moe_unpermute_mask_kernel_false.py:45-68.
+#include <stdlib.h>
+
+#include <algorithm>
+#include <mutex>
+
 #include "moe_common.cuh"
 #include "rowcopy.cuh"
 #include "swiglu.cuh"
@@ -70,6 +75,90 @@ __global__ void __launch_bounds__(kRowThreads) permute_kernel(
       if (pp != nullptr && tid == 0) pp[dd] = s_p[j];
     }
     __syncthreads();
+  }
+}
+
+// Permute through the bulk-copy (TMA) engine. A one-warp CTA walks the tokens
+// blockIdx.x, blockIdx.x + gridDim.x, ...: each token row reaches shared
+// memory with one bulk load, issued kBulkBufs - 1 tokens ahead into a ring of
+// kBulkBufs row buffers, and each destination row leaves with one bulk store,
+// issued by the lane that read that map entry. The SM executes a handful of
+// instructions per row instead of one 16-byte load or store per thread, and
+// every byte still crosses HBM once. A buffer is reloaded only after the
+// stores that read it (the previous token's) have finished reading shared
+// memory. The row wait is bounded (2 s): on a timeout the kernel records 1 in
+// g_rowcopy_err (read by moe_permute_check), waits a bounded time for its
+// loads in flight and returns.
+constexpr int kBulkBufs = 3;
+constexpr uint32_t kBulkMaxRowBytes = 32768;
+__device__ int32_t g_rowcopy_err;
+
+template <bool kTrans, typename IdxT>
+__global__ void __launch_bounds__(32) permute_bulk_kernel(
+    const char* __restrict__ x, const IdxT* __restrict__ map, const float* __restrict__ probs,
+    char* __restrict__ out, float* __restrict__ pp, int64_t T, int E, uint32_t row_bytes,
+    int64_t num_out) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const uint32_t stride = (row_bytes + 127u) & ~127u;
+  const uint32_t buf0 = smem_u32(smem);
+  const uint32_t bar0 = buf0 + kBulkBufs * stride;
+  const int lane = lane_id();
+  if (static_cast<int64_t>(blockIdx.x) >= T) return;  // CTA-uniform
+  const int64_t n_tok = (T - 1 - static_cast<int64_t>(blockIdx.x)) / gridDim.x + 1;
+  if (lane == 0) {
+    for (int b = 0; b < kBulkBufs; ++b) mbar_init(bar0 + 8u * b, 1);
+    fence_mbar_init();
+  }
+  __syncwarp();
+  auto token = [&](int64_t i) { return static_cast<int64_t>(blockIdx.x) + i * gridDim.x; };
+  auto load = [&](int64_t i) {
+    const uint32_t b = static_cast<uint32_t>(i % kBulkBufs);
+    mbar_arrive_expect_tx(bar0 + 8u * b, row_bytes);
+    bulk_load(buf0 + b * stride, x + token(i) * row_bytes, row_bytes, bar0 + 8u * b);
+  };
+  int64_t issued = n_tok < kBulkBufs - 1 ? n_tok : kBulkBufs - 1;  // loads issued: tokens [0, issued)
+  if (lane == 0)
+    for (int64_t i = 0; i < issued; ++i) load(i);
+  int64_t i = 0;
+  for (; i < n_tok; ++i) {
+    if (issued < n_tok) {
+      // Token i-1's buffer takes token i + kBulkBufs - 1 once its stores read it.
+      bulk_wait_read<0>();
+      __syncwarp();
+      if (lane == 0) load(issued);
+      ++issued;
+    }
+    const uint32_t b = static_cast<uint32_t>(i % kBulkBufs);
+    const uint32_t parity = static_cast<uint32_t>((i / kBulkBufs) & 1);
+    bool ok = mbar_try_wait(bar0 + 8u * b, parity);
+    if (!ok) {
+      const unsigned long long t0 = globaltimer_ns();
+      while (!(ok = mbar_try_wait(bar0 + 8u * b, parity)))
+        if (globaltimer_ns() - t0 > kWaitTimeoutNs) break;
+    }
+    if (!__all_sync(0xffffffffu, ok)) break;
+    const int64_t t = token(i);
+    const uint32_t src = buf0 + b * stride;
+    for (int e0 = 0; e0 < E; e0 += 32) {
+      const int e = e0 + lane;
+      int64_t d = -1;
+      if (e < E) d = load_map<IdxT, kTrans>(map, T, E, t, e);
+      if (d >= 0 && d < num_out) {
+        bulk_store(out + d * static_cast<int64_t>(row_bytes), src, row_bytes);
+        if (pp != nullptr) pp[d] = __ldg(probs + t * E + e);
+      }
+    }
+    bulk_commit();  // one (possibly empty) group per token and lane
+  }
+  bulk_wait_all();
+  if (i < n_tok && lane == 0) {  // a row never arrived: report, drain, return
+    atomicExch(&g_rowcopy_err, 1);
+    for (int64_t j = i; j < issued; ++j) {
+      const uint32_t b = static_cast<uint32_t>(j % kBulkBufs);
+      const unsigned long long t0 = globaltimer_ns();
+      while (!mbar_try_wait(bar0 + 8u * b, static_cast<uint32_t>((j / kBulkBufs) & 1)))
+        if (globaltimer_ns() - t0 > kWaitTimeoutNs) break;
+    }
   }
 }
 
@@ -300,9 +389,53 @@ int launch_unpermute_v(const void* pin, const IdxT* map, const float* probs, int
   return MOE_OK;
 }
 
+// MOE_PERMUTE_BULK=0 keeps the register-staged permute_kernel everywhere.
+bool permute_bulk_enabled() {
+  static const int v = [] {
+    const char* e = getenv("MOE_PERMUTE_BULK");
+    return (e != nullptr && e[0] == '0') ? 0 : 1;
+  }();
+  return v == 1;
+}
+
+template <bool kTrans, typename IdxT>
+int launch_permute_bulk(const void* x, const IdxT* map, const float* probs, void* out, float* pp,
+                        int64_t T, int64_t H, int64_t E, int64_t num_out, cudaStream_t s) {
+  const uint32_t row_bytes = static_cast<uint32_t>(H * 2);
+  const uint32_t stride = (row_bytes + 127u) & ~127u;
+  const size_t smem = kBulkBufs * stride + 8 * kBulkBufs;
+  int dev = 0;
+  MOE_CUDA_CALL(cudaGetDevice(&dev), "cudaGetDevice");
+  static std::mutex mu;
+  static bool attr_done[64] = {};
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    if (dev < 64 && !attr_done[dev]) {
+      MOE_CUDA_CALL(cudaFuncSetAttribute(permute_bulk_kernel<kTrans, IdxT>,
+                                         cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         static_cast<int>(kBulkBufs * kBulkMaxRowBytes + 64)),
+                    "cudaFuncSetAttribute(permute_bulk)");
+      attr_done[dev] = true;
+    }
+  }
+  // One-warp CTAs, as many per SM as shared memory allows (at most 16).
+  const int per_sm = static_cast<int>(std::min<size_t>(16, (227u * 1024u) / (smem + 1024)));
+  const unsigned grid =
+      static_cast<unsigned>(std::min<int64_t>(T, static_cast<int64_t>(num_sms(dev)) * per_sm));
+  permute_bulk_kernel<kTrans, IdxT><<<grid, 32, smem, s>>>(
+      static_cast<const char*>(x), map, probs, static_cast<char*>(out), pp, T, static_cast<int>(E),
+      row_bytes, num_out);
+  MOE_CUDA_CHECK_LAUNCH("permute_bulk launch");
+  return MOE_OK;
+}
+
 template <bool kTrans, typename IdxT>
 int launch_permute(const void* x, const IdxT* map, const float* probs, void* out, float* pp,
                    int64_t T, int64_t H, int64_t E, int64_t num_out, cudaStream_t s) {
+  // Bulk copies need 16-byte rows and addresses; rows up to 32 KB (H <= 16384).
+  if (permute_bulk_enabled() && vec_bytes(x, out, H) == 16 &&
+      static_cast<uint64_t>(H) * 2 <= kBulkMaxRowBytes)
+    return launch_permute_bulk<kTrans, IdxT>(x, map, probs, out, pp, T, H, E, num_out, s);
   switch (vec_bytes(x, out, H)) {
     case 16: return launch_permute_v<kTrans, IdxT, uint4>(x, map, probs, out, pp, T, H, E, num_out, s);
     case 4: return launch_permute_v<kTrans, IdxT, uint32_t>(x, map, probs, out, pp, T, H, E, num_out, s);
@@ -387,6 +520,25 @@ extern "C" int moe_permute_mask_map(const void* x, const int64_t* row_id_map_te,
   MOE_REQUIRE(x && out && row_id_map_te, "permute: null pointer");
   return launch_permute<false, int64_t>(x, row_id_map_te, probs, out, permuted_probs, T, H, E,
                                         num_out, reinterpret_cast<cudaStream_t>(stream));
+}
+
+extern "C" int moe_permute_check(moe_stream_t stream, int32_t* device_error) {
+  MOE_REQUIRE(device_error != nullptr, "permute_check: null output");
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  int32_t v = 0;
+  MOE_CUDA_CALL(cudaMemcpyFromSymbolAsync(&v, g_rowcopy_err, sizeof(v), 0,
+                                          cudaMemcpyDeviceToHost, s),
+                "permute_check copy");
+  MOE_CUDA_CALL(cudaStreamSynchronize(s), "permute_check sync");
+  *device_error = v;
+  if (v != 0) {
+    const int32_t zero = 0;
+    MOE_CUDA_CALL(cudaMemcpyToSymbolAsync(g_rowcopy_err, &zero, sizeof(zero), 0,
+                                          cudaMemcpyHostToDevice, s),
+                  "permute_check clear");
+    MOE_CUDA_CALL(cudaStreamSynchronize(s), "permute_check sync");
+  }
+  return v == 0 ? MOE_OK : MOE_ERR_DEVICE;
 }
 
 extern "C" int moe_permute_mask_map_trans(const void* x, const void* row_id_map_et,

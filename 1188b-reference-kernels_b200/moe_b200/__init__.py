@@ -9,7 +9,7 @@ The reference-style ``kernel_function`` entry points live in ``bundles/``.
 """
 from ._lib import MoeError, load as load_library
 from .ops import (GroupedGemmPlan, RouterOutput, RowIdMap, combine_backward, grouped_gemm,
-                  grouped_wgrad, grouped_wgrad_device_error, permute,
+                  grouped_wgrad, grouped_wgrad_device_error, permute, permute_device_error,
                   permute_backward, permute_trans, router_device_error, router_gemm_topk,
                   router_logits, router_topk, row_id_map, swiglu, swiglu_backward,
                   topk, unpermute, unpermute_weighted)
@@ -19,7 +19,7 @@ __all__ = [
     "MoeError", "load_library", "GroupedGemmPlan", "RouterOutput", "RowIdMap", "combine_backward",
     "grouped_gemm",
     "grouped_wgrad", "grouped_wgrad_device_error",
-    "permute", "permute_backward", "permute_trans", "router_device_error", "router_gemm_topk",
+    "permute", "permute_device_error", "permute_backward", "permute_trans", "router_device_error", "router_gemm_topk",
     "router_logits", "router_topk", "row_id_map",
     "swiglu", "swiglu_backward", "topk", "unpermute", "unpermute_weighted",
     "MoELayer", "MoEWeights", "HostPipeline", "moe_layer_fwd",

@@ -89,6 +89,7 @@ _SIGNATURES = {
     "moe_copy_async": [c_void_p, c_void_p, c_size_t, c_void_p],
     "moe_ep_dispatch": [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int64,
                         c_int64, c_int64, c_int64, c_int64, c_void_p],
+    "moe_permute_check": [c_void_p, POINTER(c_int32)],
     "moe_ep_dispatch_range": [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32,
                               c_int64, c_int64, c_int64, c_int64, c_int64, c_int32, c_int32,
                               c_int32, c_void_p],

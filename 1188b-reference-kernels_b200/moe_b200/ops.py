@@ -21,7 +21,7 @@ from . import _lib
 
 __all__ = [
     "topk", "router_topk", "RouterOutput", "row_id_map", "RowIdMap", "permute",
-    "permute_trans", "unpermute", "unpermute_weighted", "grouped_gemm", "GroupedGemmPlan",
+    "permute_trans", "permute_device_error", "unpermute", "unpermute_weighted", "grouped_gemm", "GroupedGemmPlan",
     "grouped_wgrad", "grouped_wgrad_device_error", "swiglu", "router_logits", "router_gemm_topk", "router_gemm_fusable",
     "router_device_error", "permute_backward", "combine_backward", "swiglu_backward",
 ]
@@ -210,6 +210,18 @@ def permute(x: torch.Tensor, row_id_map: torch.Tensor, probs: Optional[torch.Ten
     _lib.call("moe_permute_mask_map", _p(xc), _p(mc), _p(pc), _p(out), _p(pp), t, xc.shape[1], e,
               int(num_out), _stream(xc.device))
     return out, pp
+
+
+def permute_device_error(device) -> int:
+    """Error word of the bulk-copy permute on this device (0: none, 1: a row
+    load timed out), cleared after reading. Synchronises the current stream."""
+    dev = torch.device(device)
+    if dev.index is None:
+        dev = torch.device(dev.type, torch.cuda.current_device())
+    v = c_int32(0)
+    with torch.cuda.device(dev):
+        _lib.load().moe_permute_check(_stream(dev), byref(v))
+    return int(v.value)
 
 
 def permute_trans(x: torch.Tensor, row_id_map: torch.Tensor, probs: Optional[torch.Tensor] = None,

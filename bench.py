@@ -952,7 +952,7 @@ def main():
         out, mid = layer.forward(x, logits, return_intermediates=True)
         torch.cuda.synchronize()
         check = check_layer(out, mid, x, logits, bias, w.w1, w.w2, k)
-        check["device_error"] = layer.plan.device_error()
+        check["device_error"] = layer.plan.device_error() + moe_b200.permute_device_error(dev)
         check["ok"] = check["ok"] and check["device_error"] == 0
         del out, mid
     elif not a.no_check:

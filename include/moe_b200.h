@@ -5,10 +5,10 @@
  * launches asynchronously on that stream and returns a moe_status. On a
  * non-zero status, moe_b200_last_error() returns a message for the calling
  * thread. Outputs are caller-allocated; inputs are only read. No entry point
- * synchronises the stream or allocates device memory (moe_grouped_gemm_check,
- * which reads a device error word back to the host, is the one call that
- * waits); the ones that need scratch take a caller-provided workspace whose
- * size the matching *_workspace_size function reports.
+ * synchronises the stream or allocates device memory (moe_grouped_gemm_check
+ * and moe_permute_check, which read a device error word back to the host,
+ * are the calls that wait); the ones that need scratch take a caller-provided
+ * workspace whose size the matching *_workspace_size function reports.
  *
  * Each function names the reference interface it replaces. The reference
  * binds its kernels through pybind functions that take torch tensors and call
@@ -150,6 +150,14 @@ int moe_permute_mask_map(const void* x, const int64_t* row_id_map_te, const floa
 int moe_permute_mask_map_trans(const void* x, const void* row_id_map_et, int32_t idx_bits,
                                const float* probs, void* out, float* permuted_probs, int64_t T,
                                int64_t H, int64_t E, int64_t num_out, moe_stream_t stream);
+
+/* Rows with 16-byte aligned pointers and H <= 16384 (H % 8 == 0) go through  */
+/* the bulk-copy (TMA) engine: one bulk load of each token row into shared    */
+/* memory, one bulk store per destination row. Its bounded wait on a row      */
+/* load records a device error word; moe_permute_check reads it back (and     */
+/* clears it), synchronising `stream`: 0 = none, 1 = a row load timed out.    */
+/* No reference counterpart (the reference launchers return nothing).         */
+int moe_permute_check(moe_stream_t stream, int32_t* device_error);
 
 /* ------------------------------------------------------------------------ */
 /* a6/a7/a8  Unpermute (combine) with an expert-major [E,T] map:             */

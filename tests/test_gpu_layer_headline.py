@@ -44,7 +44,7 @@ def test_headline_layer_vs_oracle(cuda_dev):
     layer = moe_b200.MoELayer(w, topk=K, expert_bias=bias)
     out, mid = layer.forward(x, logits, return_intermediates=True)
     torch.cuda.synchronize()
-    assert layer.plan.device_error() == 0
+    assert layer.plan.device_error() == 0 and moe_b200.permute_device_error(cuda_dev) == 0
 
     _, _, rmap, probs = orc.router(logits.cpu().numpy(), K, bias.cpu().numpy())
     r = mid["routing"]

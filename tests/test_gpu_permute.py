@@ -112,6 +112,49 @@ def test_permute_chain_vs_oracle(cuda_dev, t, h, e, k):
     np.testing.assert_array_equal(u16(out2), ref)
 
 
+def test_permute_bulk_path_equals_register_path(cuda_dev):
+    """The default permute (rows staged in shared memory by bulk TMA loads and
+    written by bulk TMA stores) and the register-staged kernel
+    (MOE_PERMUTE_BULK=0, in a fresh process) give the same bits, for the
+    token-major map with probs and the [E,T] int32 map, with fewer tokens
+    than CTAs and with many tokens per CTA; the device error word stays 0."""
+    import os
+    import subprocess
+    import sys
+    from conftest import ROOT
+    code = r'''
+import sys, hashlib, torch
+sys.path[:0] = [sys.argv[1], sys.argv[2], sys.argv[3]]
+import moe_b200
+from moe_b200 import _lib
+from ctypes import byref, c_int32
+dev = torch.device("cuda", 0)
+out = []
+for t, h, e, k in ((3, 7168, 16, 4), (20000, 1024, 64, 8), (2500, 16384, 32, 2)):
+    g = torch.Generator().manual_seed(t)
+    x = torch.randn(t, h, generator=g).to(torch.bfloat16).to(dev)
+    lg = torch.randn(t, e, generator=g).to(dev)
+    r = moe_b200.router_topk(lg, k, "softmax", renorm=True)
+    m = moe_b200.row_id_map(r.routing_map)
+    a, pa = moe_b200.permute(x, m.map_te, r.probs, num_out=t * k)
+    b, _ = moe_b200.permute_trans(x, m.map_et.to(torch.int32), None, num_out=t * k)
+    for v in (a.view(torch.int16), pa, b.view(torch.int16)):
+        out.append(hashlib.sha256(v.cpu().numpy().tobytes()).hexdigest())
+err = c_int32(-1)
+assert _lib.load().moe_permute_check(None, byref(err)) == 0 and err.value == 0
+print(" ".join(out))
+'''
+    res = {}
+    for flag in ("1", "0"):
+        env = dict(os.environ, MOE_PERMUTE_BULK=flag)
+        r = subprocess.run([sys.executable, "-c", code, str(ROOT / "1188b-reference-kernels_b200"),
+                            str(ROOT), str(ROOT / "tests")], env=env, capture_output=True,
+                           text=True, timeout=300)
+        assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
+        res[flag] = r.stdout.split()
+    assert res["1"] == res["0"]
+
+
 # ------------------------------------------------------------------ a6-a8 unpermute
 def test_unpermute_small_exact(cuda_dev, golden):
     z = golden("case15_unpermute.npz")
