@@ -194,6 +194,84 @@ __global__ void __launch_bounds__(kRowThreads) ep_combine_kernel(
   }
 }
 
+// Backward of the fused combine for one source rank: for each routed (t, e)
+// in ascending e, with owner d = e / experts_per_rank and row rr = map[t,e] +
+// delta[e], grad_probs[t,e] = <grad_out[t], y_d[rr]> (fp32, the forward rows
+// loaded from the owner's fc2 output over NVLink) and dy_d[rr] =
+// bf16(probs[t,e] * grad_out[t]) (stored into the owner's gradient buffer
+// over NVLink). The arithmetic and the reduction order (per-thread FMA chain,
+// xor butterfly, warps in order) are those of the single-GPU
+// combine_backward_kernel, so the results are the same bits.
+template <typename V>
+__global__ void __launch_bounds__(kRowThreads) ep_combine_backward_kernel(
+    const V* __restrict__ grad_out, const int64_t* __restrict__ map_te,
+    const float* __restrict__ probs, const PeerRows pr, const PeerRows pw,
+    float* __restrict__ grad_probs, int64_t T, int E, int nvec, int64_t num_rows) {
+  constexpr int kE = VecTraits<V>::kElems;
+  __shared__ long long s_src[kEpCombineMaxE];  // forward row address (owner's fc2 output)
+  __shared__ long long s_dst[kEpCombineMaxE];  // gradient row address (owner's buffer)
+  __shared__ int s_e[kEpCombineMaxE];
+  __shared__ float s_w[kEpCombineMaxE];
+  __shared__ int s_wcnt[kRowWarps];
+  __shared__ float s_red[kRowWarps];
+  __shared__ int s_n;
+  const int64_t t = blockIdx.x;
+  const int tid = threadIdx.x;
+  if (tid == 0) s_n = 0;
+  for (int e0 = 0; e0 < E; e0 += kRowThreads) {
+    const int e = e0 + tid;
+    int64_t row = -1;
+    if (e < E) row = __ldg(map_te + t * E + e);
+    long long rb = 0, wb = 0;
+    int64_t rr = 0, wr = 0;
+    const bool valid = row >= 0 && row < num_rows && peer_row(pr, e, row, rb, rr) &&
+                       peer_row(pw, e, row, wb, wr);
+    if (e < E && !valid) grad_probs[t * E + e] = 0.f;
+    int pos;
+    const int total = compact_window(valid, s_wcnt, pos);
+    const int b = s_n;
+    if (valid) {
+      s_src[b + pos] = rb + rr * nvec * static_cast<long long>(sizeof(V));
+      s_dst[b + pos] = wb + wr * nvec * static_cast<long long>(sizeof(V));
+      s_e[b + pos] = e;
+      s_w[b + pos] = __ldg(probs + t * E + e);
+    }
+    __syncthreads();
+    if (tid == 0) s_n = b + total;
+  }
+  __syncthreads();
+  const int n = s_n;
+  const V* g_row = grad_out + t * nvec;
+  for (int j = 0; j < n; ++j) {
+    const V* yr = reinterpret_cast<const V*>(s_src[j]);
+    V* dr = reinterpret_cast<V*>(s_dst[j]);
+    const float w = s_w[j];
+    float part = 0.f;
+    for (int i = tid; i < nvec; i += kRowThreads) {
+      float g[kE], y[kE], o[kE];
+      VecTraits<V>::unpack(__ldg(g_row + i), g);
+      VecTraits<V>::unpack(yr[i], y);
+#pragma unroll
+      for (int q = 0; q < kE; ++q) {
+        o[q] = __fmul_rn(w, g[q]);
+        part = __fmaf_rn(g[q], y[q], part);
+      }
+      dr[i] = VecTraits<V>::pack(o);
+    }
+#pragma unroll
+    for (int off = 16; off > 0; off >>= 1) part += __shfl_xor_sync(0xffffffffu, part, off);
+    if (lane_id() == 0) s_red[warp_id()] = part;
+    __syncthreads();
+    if (tid == 0) {
+      float d = 0.f;
+#pragma unroll
+      for (int w2 = 0; w2 < kRowWarps; ++w2) d += s_red[w2];
+      grad_probs[t * E + s_e[j]] = d;
+    }
+    __syncthreads();
+  }
+}
+
 // ---------------------------------------------------------------------------
 // Deduplicated dispatch: a token row crosses NVLink once per destination rank
 // instead of once per (token, expert). Each rank owns a staging block per
@@ -444,6 +522,43 @@ extern "C" int moe_ep_combine(const int64_t* peer_bases, const int64_t* expert_d
                                                              (int)E, static_cast<int>(H),
                                                              num_rows);
   MOE_CUDA_CHECK_LAUNCH("ep_combine launch");
+  return MOE_OK;
+}
+
+extern "C" int moe_ep_combine_backward(const void* grad_out, const int64_t* row_id_map_te,
+                                       const float* probs, const int64_t* peer_rows,
+                                       const int64_t* peer_grad_rows,
+                                       const int64_t* expert_deltas, int32_t ranks,
+                                       int32_t experts_per_rank, int64_t cap_rows,
+                                       float* grad_probs, int64_t T, int64_t H, int64_t E,
+                                       int64_t num_rows, moe_stream_t stream) {
+  MOE_REQUIRE(T >= 0 && H >= 0 && E >= 1, "ep_combine_backward: bad shape");
+  MOE_REQUIRE(E <= kEpCombineMaxE, "ep_combine_backward: E=%lld above %d", (long long)E,
+              kEpCombineMaxE);
+  if (T == 0) return MOE_OK;
+  MOE_REQUIRE(grad_out && row_id_map_te && probs && grad_probs,
+              "ep_combine_backward: null pointer");
+  PeerRows pr, pw;
+  int vb = 16, vw = 16;
+  int st = make_peer_rows(pr, peer_rows, expert_deltas, ranks, experts_per_rank, cap_rows, E, H,
+                          vb, "ep_combine_backward");
+  if (st) return st;
+  st = make_peer_rows(pw, peer_grad_rows, expert_deltas, ranks, experts_per_rank, cap_rows, E, H,
+                      vw, "ep_combine_backward");
+  if (st) return st;
+  if (H == 0) return MOE_OK;
+  if ((reinterpret_cast<uintptr_t>(grad_out) & 15) != 0 || vw != 16) vb = 2;
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned grid = static_cast<unsigned>(T);
+  if (vb == 16)
+    ep_combine_backward_kernel<uint4><<<grid, kRowThreads, 0, s>>>(
+        static_cast<const uint4*>(grad_out), row_id_map_te, probs, pr, pw, grad_probs, T, (int)E,
+        static_cast<int>(H / 8), num_rows);
+  else
+    ep_combine_backward_kernel<uint16_t><<<grid, kRowThreads, 0, s>>>(
+        static_cast<const uint16_t*>(grad_out), row_id_map_te, probs, pr, pw, grad_probs, T,
+        (int)E, static_cast<int>(H), num_rows);
+  MOE_CUDA_CHECK_LAUNCH("ep_combine_backward launch");
   return MOE_OK;
 }
 

@@ -487,17 +487,25 @@ class MoELayerEP:
         if self.events is not None:
             self.events[name].record()
 
-    def forward(self, x: torch.Tensor, logits: torch.Tensor) -> torch.Tensor:
+    def forward(self, x: torch.Tensor, logits: torch.Tensor, save_for_backward: bool = False):
+        """One expert-parallel forward of this rank's tokens x [T,H] with router
+        logits [T,E]. save_for_backward (transports "fused" and "fused_dedup",
+        overlap_chunks 1): returns (out, ctx) for backward(); fc1 then keeps
+        its gate|up output, and the received rows are copied out of the
+        receive buffer, which the backward reuses for the fc2 gradient rows."""
         t, h = x.shape
         e = self.disp.num_experts
         if logits.shape != (t, e):
             raise ValueError(f"logits must be [{t},{e}]")
+        if save_for_backward and (not self.fused or self.chunks > 1):
+            raise ValueError("save_for_backward needs transport 'fused' or 'fused_dedup' "
+                             "with overlap_chunks=1")
         self._ev("start")
         r = ops.router_topk(logits, self.k, "softmax", self.renorm, self.bias, outputs="maps",
                             placement=self.placement)
         rim = ops.row_id_map(r.routing_map, align=1, want_et=False)
         if self.fused:
-            return self._forward_fused(x, r, rim)
+            return self._forward_fused(x, r, rim, save_for_backward)
         xp, _ = ops.permute(x, rim.map_te, None, num_out=t * self.k)
         self._ev("local_dispatch")
         if self.peer is not None:
@@ -522,7 +530,7 @@ class MoELayerEP:
         self._ev("combine")
         return out
 
-    def _forward_fused(self, x, r, rim):
+    def _forward_fused(self, x, r, rim, save=False):
         t, h = x.shape
         self._ev("local_dispatch")
         lay, host, deltas = self.peer.expert_major(rim.counts)
@@ -530,6 +538,7 @@ class MoELayerEP:
         nsend = int(sum(host[self.peer.rank]))
         nrecv = int(sum(lay.splits))
         self.last_recv_rows = nrecv
+        ctx = None
         if self.chunks > 1:
             self._chunked_experts(x, rim.map_te, deltas, nsend, lay.splits)
         else:
@@ -539,7 +548,13 @@ class MoELayerEP:
                 xr = self.peer.fused_dispatch(x, rim.map_te, deltas, nsend, nrecv)
             self._ev("a2a_dispatch")
             self.plan.from_splits(torch.tensor(lay.splits, dtype=torch.int32))
-            hmid = ops.grouped_gemm(xr, self.w.w1, epilogue="swiglu", plan=self.plan)
+            if save:
+                y1 = ops.grouped_gemm(xr, self.w.w1, plan=self.plan)
+                hmid = ops.swiglu(y1)  # the fused SwiGLU epilogue's bits
+                ctx = dict(routing=r, rim=rim, deltas=deltas, splits=list(lay.splits),
+                           nsend=nsend, xr=xr.clone(), y1=y1, h=hmid, tokens=t)
+            else:
+                hmid = ops.grouped_gemm(xr, self.w.w1, epilogue="swiglu", plan=self.plan)
             self._ev("fc1")
             ops.grouped_gemm(hmid, self.w.w2, plan=self.plan, out=self.peer.y_buf[:xr.shape[0]])
         self._ev("fc2")
@@ -547,7 +562,57 @@ class MoELayerEP:
         self._ev("a2a_combine")
         out = self.peer.fused_combine(rim.map_te, r.probs, deltas, nsend, t, h)
         self._ev("combine")
-        return out
+        return (out, ctx) if save else out
+
+    def backward(self, grad_out: torch.Tensor, ctx: dict):
+        """Backward of one forward(..., save_for_backward=True) of this rank's
+        tokens; call it on every rank, before the layer's next forward (the
+        fc2 outputs it reads stay in the peer-shared output buffers only until
+        then). Returns (grad_x [T,H] bf16, grad_probs [T,E] fp32 in slot
+        order, dw1 [E_loc,2F,H], dw2 [E_loc,H,F]) -- the gradients of this
+        rank's tokens and of this rank's experts, the same bits as
+        MoELayer.backward on all ranks' tokens with all experts.
+
+          1. combine backward over NVLink (moe_ep_combine_backward): gate
+             gradients from the owners' fc2 rows, fc2 gradient rows stored
+             into the owners' receive buffers at the forward's rows; barrier;
+          2. on the local experts, grouped by the forward's expert-major
+             receive layout: fc2 dgrad and wgrad, SwiGLU backward, fc1 dgrad
+             (written into the peer-shared output buffer) and wgrad; barrier;
+          3. permute backward: grad_x[t] = the unweighted fused combine of the
+             fc1 dgrad rows, read back from their owners."""
+        if ctx is None or "xr" not in ctx:
+            raise ValueError("ctx must come from forward(..., save_for_backward=True)")
+        t = ctx["tokens"]
+        h = self.w.hidden
+        if grad_out.shape != (t, h) or grad_out.dtype != torch.bfloat16:
+            raise ValueError(f"grad_out must be bf16 [{t},{h}]")
+        r, rim, deltas = ctx["routing"], ctx["rim"], ctx["deltas"]
+        nsend = ctx["nsend"]
+        nrecv = ctx["xr"].shape[0]
+        peer = self.peer
+        e = self.disp.num_experts
+        go = grad_out.contiguous()
+        grad_probs = torch.empty((t, e), dtype=torch.float32, device=go.device)
+        n = peer.world
+        arr = lambda v: (ctypes.c_int64 * n)(*v)  # noqa: E731
+        _lib.call("moe_ep_combine_backward", go.data_ptr(), rim.map_te.data_ptr(),
+                  r.probs.data_ptr(), arr(peer.peer_y), arr(peer.peer_recv), deltas.data_ptr(),
+                  n, self.disp.local_experts, peer.recv_cap, grad_probs.data_ptr(), t, h, e,
+                  nsend, torch.cuda.current_stream(go.device).cuda_stream)
+        peer.barrier()
+        dy2 = peer.recv_buf[:nrecv]
+        sp = torch.tensor(ctx["splits"], dtype=torch.int32).to(go.device)
+        self.plan.from_splits(sp)
+        dh = ops.grouped_gemm(dy2, self.w.w2, plan=self.plan, w_layout="KN")
+        dw2 = ops.grouped_wgrad(dy2, ctx["h"], sp)
+        dy1 = ops.swiglu_backward(ctx["y1"], dh)
+        ops.grouped_gemm(dy1, self.w.w1, plan=self.plan, w_layout="KN",
+                         out=peer.y_buf[:nrecv])
+        dw1 = ops.grouped_wgrad(dy1, ctx["xr"], sp)
+        peer.barrier()
+        grad_x = peer.fused_combine(rim.map_te, None, deltas, nsend, t, h)
+        return grad_x, grad_probs, dw1, dw2
 
     @staticmethod
     def chunk_bounds(local_experts: int, chunks: int):

@@ -334,6 +334,21 @@ int moe_ep_combine(const int64_t* peer_bases, const int64_t* expert_deltas, int3
                    const float* probs, void* out, int64_t T, int64_t H, int64_t E,
                    int64_t num_rows, moe_stream_t stream);
 
+/* f3  Backward of the fused combine for this rank's tokens: for each routed */
+/* (t, e), owner d = e / experts_per_rank, row rr = map[t,e] + deltas[e]:     */
+/* grad_probs[t,e] = <grad_out[t], rows_d[rr]> in fp32 (rows_d: rank d's fc2  */
+/* output, peer_rows[d]) and grad_rows_d[rr] = bf16(probs[t,e] * grad_out[t]) */
+/* (peer_grad_rows[d]); grad_probs [T,E] is 0 where unrouted. The same bits  */
+/* as moe_combine_backward on the single-GPU layout. The expert-parallel     */
+/* form of the deep_ep FusedCombine backward the reference names             */
+/* (kernel_cases/case24_ref_moe_unpermute_mask_kernel_false.py:3-6). E <=    */
+/* 1024.                                                                      */
+int moe_ep_combine_backward(const void* grad_out, const int64_t* row_id_map_te, const float* probs,
+                            const int64_t* peer_rows, const int64_t* peer_grad_rows,
+                            const int64_t* expert_deltas, int32_t ranks, int32_t experts_per_rank,
+                            int64_t cap_rows, float* grad_probs, int64_t T, int64_t H, int64_t E,
+                            int64_t num_rows, moe_stream_t stream);
+
 /* Deduplicated dispatch (the token-once-per-rank scheme of the deep_ep       */
 /* FusedDispatch the reference names, kernel_cases/case22_ref_moe_permute_    */
 /* mask_kernel_true.py:3-6): a token row crosses NVLink once per destination  */

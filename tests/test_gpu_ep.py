@@ -127,3 +127,78 @@ def test_ep_equals_single_gpu(world, routing, transport):
         assert r[1] != "error", r
         assert r[2] == 0, r
     assert res[0][1] is True
+
+
+def _bwd_worker(rank, world, port, transport, q):
+    for p in (str(PKG), str(ROOT), str(GOLDEN)):
+        if p not in sys.path:
+            sys.path.insert(0, p)
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+    try:
+        import torch.distributed as dist
+        import moe_b200
+        from moe_b200.ep import MoELayerEP, balanced_placement
+        dev = torch.device("cuda", rank)
+        torch.cuda.set_device(dev)
+        dist.init_process_group("nccl", rank=rank, world_size=world,
+                                timeout=timedelta(seconds=60), device_id=dev)
+        t, h, e, f, k = 256, 1024, 16, 256, 4
+        x, lg, bias, w1, w2 = _problem(world, t, h, e, f, "zipf")
+        g = torch.Generator().manual_seed(99)
+        go = torch.randn(world * t, h, generator=g).to(torch.bfloat16)
+        el = e // world
+        sl = slice(rank * t, (rank + 1) * t)
+        load = torch.bincount(torch.topk(lg + bias, k, dim=1).indices.reshape(-1), minlength=e)
+        pl = torch.tensor(balanced_placement(load.tolist(), world), dtype=torch.int32)
+        w1, w2 = w1[pl.long()], w2[pl.long()]  # slot order
+        local = moe_b200.MoEWeights(w1[rank * el:(rank + 1) * el].to(dev).contiguous(),
+                                    w2[rank * el:(rank + 1) * el].to(dev).contiguous())
+        layer = MoELayerEP(local, e, topk=k, expert_bias=bias.to(dev), transport=transport,
+                           tokens=t, placement=pl.to(dev))
+        out, ctx = layer.forward(x[sl].to(dev), lg[sl].to(dev), save_for_backward=True)
+        gx, gp, dw1, dw2 = layer.backward(go[sl].to(dev), ctx)
+        err = layer.device_error() + moe_b200.grouped_wgrad_device_error(dev)
+        full = moe_b200.MoELayer(moe_b200.MoEWeights(w1.to(dev), w2.to(dev)), topk=k,
+                                 expert_bias=bias.to(dev), placement=pl.to(dev))
+        ref_out, rctx = full.forward(x.to(dev), lg.to(dev), save_for_backward=True)
+        rgx, rgp, rdw1, rdw2 = full.backward(go.to(dev), rctx)
+        es = slice(rank * el, (rank + 1) * el)
+        same = {"out": torch.equal(out, ref_out[sl]), "grad_x": torch.equal(gx, rgx[sl]),
+                "grad_probs": torch.equal(gp, rgp[sl]),
+                "dw1": torch.equal(dw1.view(torch.int16), rdw1[es].view(torch.int16)),
+                "dw2": torch.equal(dw2.view(torch.int16), rdw2[es].view(torch.int16))}
+        layer.close()
+        dist.barrier(device_ids=[rank])
+        dist.destroy_process_group()
+        q.put((rank, same, err))
+    except Exception as exc:
+        q.put((rank, "error", f"{type(exc).__name__}: {exc}", traceback.format_exc()[-1500:]))
+
+
+@pytest.mark.parametrize("world,transport", [(2, "fused"), (2, "fused_dedup"), (4, "fused"),
+                                             (8, "fused")])
+def test_ep_backward_equals_single_gpu(world, transport):
+    """MoELayerEP.backward (combine backward over NVLink, grouped dgrad/wgrad
+    on the receive rows, permute backward as the unweighted fused combine)
+    against MoELayer.backward on all ranks' tokens with all experts (same
+    placement): output, grad_x, grad_probs and every local expert's dW1/dW2
+    bit for bit."""
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test selected but no CUDA device is visible")
+    if torch.cuda.device_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    import torch.multiprocessing as mp
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_bwd_worker, args=(r, world, port, transport, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = sorted((q.get(timeout=300) for _ in range(world)), key=lambda r: r[0])
+    for p in procs:
+        p.join(timeout=120)
+    for r in res:
+        assert r[1] != "error", r
+        assert r[2] == 0, r
+        assert all(r[1].values()), r
