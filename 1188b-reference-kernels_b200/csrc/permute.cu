@@ -389,11 +389,14 @@ int launch_unpermute_v(const void* pin, const IdxT* map, const float* probs, int
   return MOE_OK;
 }
 
-// MOE_PERMUTE_BULK=0 keeps the register-staged permute_kernel everywhere.
+// MOE_PERMUTE_BULK=1 routes eligible rows through permute_bulk_kernel. Off by
+// default: at the layer's 16384 x 7168 permute it measured 4.5 TB/s against
+// 5.2 TB/s for the register-staged kernel on the same box (the copy engine's
+// per-SM bulk-store rate, not HBM, bounds it).
 bool permute_bulk_enabled() {
   static const int v = [] {
     const char* e = getenv("MOE_PERMUTE_BULK");
-    return (e != nullptr && e[0] == '0') ? 0 : 1;
+    return (e != nullptr && e[0] == '1') ? 1 : 0;
   }();
   return v == 1;
 }

@@ -151,8 +151,9 @@ int moe_permute_mask_map_trans(const void* x, const void* row_id_map_et, int32_t
                                const float* probs, void* out, float* permuted_probs, int64_t T,
                                int64_t H, int64_t E, int64_t num_out, moe_stream_t stream);
 
-/* Rows with 16-byte aligned pointers and H <= 16384 (H % 8 == 0) go through  */
-/* the bulk-copy (TMA) engine: one bulk load of each token row into shared    */
+/* With MOE_PERMUTE_BULK=1 in the environment, rows with 16-byte aligned     */
+/* pointers and H <= 16384 (H % 8 == 0) go through the bulk-copy (TMA)        */
+/* engine instead of registers: one bulk load of each token row into shared   */
 /* memory, one bulk store per destination row. Its bounded wait on a row      */
 /* load records a device error word; moe_permute_check reads it back (and     */
 /* clears it), synchronising `stream`: 0 = none, 1 = a row load timed out.    */

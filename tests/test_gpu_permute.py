@@ -113,9 +113,9 @@ def test_permute_chain_vs_oracle(cuda_dev, t, h, e, k):
 
 
 def test_permute_bulk_path_equals_register_path(cuda_dev):
-    """The default permute (rows staged in shared memory by bulk TMA loads and
-    written by bulk TMA stores) and the register-staged kernel
-    (MOE_PERMUTE_BULK=0, in a fresh process) give the same bits, for the
+    """The bulk-copy permute (MOE_PERMUTE_BULK=1: rows staged in shared memory
+    by bulk TMA loads and written by bulk TMA stores) and the default
+    register-staged kernel, each in a fresh process, give the same bits, for the
     token-major map with probs and the [E,T] int32 map, with fewer tokens
     than CTAs and with many tokens per CTA; the device error word stays 0."""
     import os
