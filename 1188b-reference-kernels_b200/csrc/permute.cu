@@ -27,6 +27,34 @@ namespace {
 
 using namespace rowcopy;
 
+// 32-byte row vector moved by one 256-bit global load / store (sm_100): the
+// permute writes each token row k times, so halving the store instructions
+// per row matters at the power-capped clock, where the 16-byte version is
+// partly issue-bound.
+struct __align__(32) Vec32 {
+  uint4 lo, hi;
+};
+template <typename V>
+MOE_DEVICE V ld_row(const V* p) { return __ldg(p); }
+template <>
+MOE_DEVICE Vec32 ld_row<Vec32>(const Vec32* p) {
+  Vec32 v;
+  asm volatile("ld.global.nc.v8.b32 {%0, %1, %2, %3, %4, %5, %6, %7}, [%8];"
+               : "=r"(v.lo.x), "=r"(v.lo.y), "=r"(v.lo.z), "=r"(v.lo.w), "=r"(v.hi.x),
+                 "=r"(v.hi.y), "=r"(v.hi.z), "=r"(v.hi.w)
+               : "l"(p));
+  return v;
+}
+template <typename V>
+MOE_DEVICE void st_row(V* p, const V& v) { *p = v; }
+template <>
+MOE_DEVICE void st_row<Vec32>(Vec32* p, const Vec32& v) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(p), "r"(v.lo.x),
+               "r"(v.lo.y), "r"(v.lo.z), "r"(v.lo.w), "r"(v.hi.x), "r"(v.hi.y), "r"(v.hi.z),
+               "r"(v.hi.w)
+               : "memory");
+}
+
 template <int VPT, bool kTrans, typename IdxT, typename V>
 __global__ void __launch_bounds__(kRowThreads) permute_kernel(
     const V* __restrict__ x, const IdxT* __restrict__ map, const float* __restrict__ probs,
@@ -44,7 +72,7 @@ __global__ void __launch_bounds__(kRowThreads) permute_kernel(
 #pragma unroll
     for (int v = 0; v < VPT; ++v) {
       const int i = tid + v * kRowThreads;
-      if (i < nvec) r[v] = __ldg(src + i);
+      if (i < nvec) r[v] = ld_row(src + i);
     }
   }
 
@@ -67,10 +95,10 @@ __global__ void __launch_bounds__(kRowThreads) permute_kernel(
 #pragma unroll
         for (int v = 0; v < VPT; ++v) {
           const int i = tid + v * kRowThreads;
-          if (i < nvec) o[i] = r[v];
+          if (i < nvec) st_row(o + i, r[v]);
         }
       } else {
-        for (int i = tid; i < nvec; i += kRowThreads) o[i] = __ldg(src + i);
+        for (int i = tid; i < nvec; i += kRowThreads) st_row(o + i, ld_row(src + i));
       }
       if (pp != nullptr && tid == 0) pp[dd] = s_p[j];
     }
@@ -340,10 +368,16 @@ __global__ void swiglu_kernel(const uint4* __restrict__ y, uint4* __restrict__ h
   h[i] = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+template <typename V>
+constexpr int row_elems() {
+  if constexpr (sizeof(V) == 32) return 16;
+  else return VecTraits<V>::kElems;
+}
+
 template <bool kTrans, typename IdxT, typename V>
 int launch_permute_v(const void* x, const IdxT* map, const float* probs, void* out, float* pp,
                      int64_t T, int64_t H, int64_t E, int64_t num_out, cudaStream_t s) {
-  const int nvec = static_cast<int>(H / VecTraits<V>::kElems);
+  const int nvec = static_cast<int>(H / row_elems<V>());
   const int vpt = (nvec + kRowThreads - 1) / kRowThreads;
   const V* xv = static_cast<const V*>(x);
   V* ov = static_cast<V*>(out);
@@ -401,6 +435,14 @@ bool permute_bulk_enabled() {
   return v == 1;
 }
 
+bool permute_v32_enabled() {
+  static const int v = [] {
+    const char* e = getenv("MOE_PERMUTE_V32");
+    return (e != nullptr && e[0] == '0') ? 0 : 1;
+  }();
+  return v == 1;
+}
+
 template <bool kTrans, typename IdxT>
 int launch_permute_bulk(const void* x, const IdxT* map, const float* probs, void* out, float* pp,
                         int64_t T, int64_t H, int64_t E, int64_t num_out, cudaStream_t s) {
@@ -439,6 +481,11 @@ int launch_permute(const void* x, const IdxT* map, const float* probs, void* out
   if (permute_bulk_enabled() && vec_bytes(x, out, H) == 16 &&
       static_cast<uint64_t>(H) * 2 <= kBulkMaxRowBytes)
     return launch_permute_bulk<kTrans, IdxT>(x, map, probs, out, pp, T, H, E, num_out, s);
+  // 32-byte vectors when rows and both pointers allow them (MOE_PERMUTE_V32=0:
+  // 16-byte vectors at most).
+  const bool v32 = permute_v32_enabled() && H % 16 == 0 &&
+                   ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(out)) & 31) == 0;
+  if (v32) return launch_permute_v<kTrans, IdxT, Vec32>(x, map, probs, out, pp, T, H, E, num_out, s);
   switch (vec_bytes(x, out, H)) {
     case 16: return launch_permute_v<kTrans, IdxT, uint4>(x, map, probs, out, pp, T, H, E, num_out, s);
     case 4: return launch_permute_v<kTrans, IdxT, uint32_t>(x, map, probs, out, pp, T, H, E, num_out, s);

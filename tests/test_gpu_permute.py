@@ -112,10 +112,11 @@ def test_permute_chain_vs_oracle(cuda_dev, t, h, e, k):
     np.testing.assert_array_equal(u16(out2), ref)
 
 
-def test_permute_bulk_path_equals_register_path(cuda_dev):
+def test_permute_paths_give_the_same_bits(cuda_dev):
     """The bulk-copy permute (MOE_PERMUTE_BULK=1: rows staged in shared memory
-    by bulk TMA loads and written by bulk TMA stores) and the default
-    register-staged kernel, each in a fresh process, give the same bits, for the
+    by bulk TMA loads and written by bulk TMA stores), the register-staged
+    kernel with 32-byte vectors (the default) and with 16-byte vectors
+    (MOE_PERMUTE_V32=0), each in a fresh process, give the same bits, for the
     token-major map with probs and the [E,T] int32 map, with fewer tokens
     than CTAs and with many tokens per CTA; the device error word stays 0."""
     import os
@@ -145,14 +146,15 @@ assert _lib.load().moe_permute_check(None, byref(err)) == 0 and err.value == 0
 print(" ".join(out))
 '''
     res = {}
-    for flag in ("1", "0"):
-        env = dict(os.environ, MOE_PERMUTE_BULK=flag)
+    for flag, envs in (("1", {"MOE_PERMUTE_BULK": "1"}), ("0", {"MOE_PERMUTE_V32": "0"}),
+                       ("v32", {})):
+        env = dict(os.environ, **envs)
         r = subprocess.run([sys.executable, "-c", code, str(ROOT / "1188b-reference-kernels_b200"),
                             str(ROOT), str(ROOT / "tests")], env=env, capture_output=True,
                            text=True, timeout=300)
         assert r.returncode == 0, r.stdout[-2000:] + r.stderr[-2000:]
         res[flag] = r.stdout.split()
-    assert res["1"] == res["0"]
+    assert res["1"] == res["0"] == res["v32"]
 
 
 # ------------------------------------------------------------------ a6-a8 unpermute
