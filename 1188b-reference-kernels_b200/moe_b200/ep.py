@@ -489,17 +489,16 @@ class MoELayerEP:
 
     def forward(self, x: torch.Tensor, logits: torch.Tensor, save_for_backward: bool = False):
         """One expert-parallel forward of this rank's tokens x [T,H] with router
-        logits [T,E]. save_for_backward (transports "fused" and "fused_dedup",
-        overlap_chunks 1): returns (out, ctx) for backward(); fc1 then keeps
+        logits [T,E]. save_for_backward (transports "fused" and "fused_dedup"):
+        returns (out, ctx) for backward(); fc1 then keeps
         its gate|up output, and the received rows are copied out of the
         receive buffer, which the backward reuses for the fc2 gradient rows."""
         t, h = x.shape
         e = self.disp.num_experts
         if logits.shape != (t, e):
             raise ValueError(f"logits must be [{t},{e}]")
-        if save_for_backward and (not self.fused or self.chunks > 1):
-            raise ValueError("save_for_backward needs transport 'fused' or 'fused_dedup' "
-                             "with overlap_chunks=1")
+        if save_for_backward and not self.fused:
+            raise ValueError("save_for_backward needs transport 'fused' or 'fused_dedup'")
         self._ev("start")
         r = ops.router_topk(logits, self.k, "softmax", self.renorm, self.bias, outputs="maps",
                             placement=self.placement)
@@ -540,7 +539,11 @@ class MoELayerEP:
         self.last_recv_rows = nrecv
         ctx = None
         if self.chunks > 1:
-            self._chunked_experts(x, rim.map_te, deltas, nsend, lay.splits)
+            saved = self._chunked_experts(x, rim.map_te, deltas, nsend, lay.splits, save)
+            if save:
+                ctx = dict(routing=r, rim=rim, deltas=deltas, splits=list(lay.splits),
+                           nsend=nsend, xr=self.peer.recv_buf[:nrecv].clone(), y1=saved[0],
+                           h=saved[1], tokens=t)
         else:
             if self.peer.dedup:
                 xr = self.peer.fused_dispatch_dedup(x, rim.map_te, deltas, nsend, nrecv)
@@ -621,10 +624,11 @@ class MoELayerEP:
         el = int(local_experts)
         return [(el * c // chunks, el * (c + 1) // chunks) for c in range(chunks)]
 
-    def _chunked_experts(self, x, map_te, deltas, nsend, splits):
+    def _chunked_experts(self, x, map_te, deltas, nsend, splits, save=False):
         """Dispatch (side stream) and fc1/fc2 (caller's stream) chunk by chunk
         of the local experts; see overlap_chunks. Stage events: a2a_dispatch
-        when chunk 0 is ready, fc1 after the last chunk's fc1."""
+        when chunk 0 is ready, fc1 after the last chunk's fc1. With save, fc1
+        keeps its gate|up output: returns (y1 [rows,2F], h [rows,F])."""
         dev = x.device
         main = torch.cuda.current_stream(dev)
         if self._comm is None:
@@ -650,6 +654,11 @@ class MoELayerEP:
                 ev.record(comm)
                 ready.append(ev)
         last = len(self._bounds) - 1
+        y1 = h = None
+        if save:
+            f = self.w.ffn
+            y1 = torch.empty((starts[-1], 2 * f), dtype=torch.bfloat16, device=dev)
+            h = torch.empty((starts[-1], f), dtype=torch.bfloat16, device=dev)
         for c, (lo, hi) in enumerate(self._bounds):
             main.wait_event(ready[c])
             if c == 0:
@@ -658,12 +667,18 @@ class MoELayerEP:
             hm = None
             if r1 > r0:
                 plan = self._chunk_plans[c].from_splits(sp[lo:hi])
-                hm = ops.grouped_gemm(self.peer.recv_buf[r0:r1], self.w.w1[lo:hi],
-                                      epilogue="swiglu", plan=plan)
+                if save:
+                    ops.grouped_gemm(self.peer.recv_buf[r0:r1], self.w.w1[lo:hi], plan=plan,
+                                     out=y1[r0:r1])
+                    hm = ops.swiglu(y1[r0:r1], out=h[r0:r1])
+                else:
+                    hm = ops.grouped_gemm(self.peer.recv_buf[r0:r1], self.w.w1[lo:hi],
+                                          epilogue="swiglu", plan=plan)
             if c == last:
                 self._ev("fc1")
             if hm is not None:
                 ops.grouped_gemm(hm, self.w.w2[lo:hi], plan=plan, out=self.peer.y_buf[r0:r1])
+        return (y1, h) if save else None
 
     def device_error(self) -> int:
         """First non-zero device error word of this layer's grouped-GEMM

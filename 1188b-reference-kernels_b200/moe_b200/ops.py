@@ -680,14 +680,21 @@ def router_gemm_topk(x: torch.Tensor, weight: torch.Tensor, k: int, score: str =
     return (r, logits) if return_logits else r
 
 
-def swiglu(y: torch.Tensor) -> torch.Tensor:
-    """h = silu(y[:, :F]) * y[:, F:] for y [M,2F] bf16 (gate|up order)."""
+def swiglu(y: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """h = silu(y[:, :F]) * y[:, F:] for y [M,2F] bf16 (gate|up order);
+    into `out` (contiguous bf16 [M,F]) when given."""
     _need_cuda("y", y)
     _need_dtype("y", y, torch.bfloat16)
     if y.dim() != 2 or y.shape[1] % 2:
         raise ValueError("y must be [M,2F]")
     yc = y.contiguous()
     m, f2 = yc.shape
-    h = torch.empty((m, f2 // 2), dtype=yc.dtype, device=yc.device)
+    if out is None:
+        h = torch.empty((m, f2 // 2), dtype=yc.dtype, device=yc.device)
+    elif out.dtype != torch.bfloat16 or tuple(out.shape) != (m, f2 // 2) or \
+            not out.is_contiguous() or out.device != yc.device:
+        raise ValueError(f"out must be a contiguous bf16 [{m},{f2 // 2}] tensor on {yc.device}")
+    else:
+        h = out
     _lib.call("moe_swiglu", _p(yc), _p(h), m, f2 // 2, _stream(yc.device))
     return h

@@ -129,7 +129,7 @@ def test_ep_equals_single_gpu(world, routing, transport):
     assert res[0][1] is True
 
 
-def _bwd_worker(rank, world, port, transport, q):
+def _bwd_worker(rank, world, port, transport, q, chunks=1):
     for p in (str(PKG), str(ROOT), str(GOLDEN)):
         if p not in sys.path:
             sys.path.insert(0, p)
@@ -154,7 +154,7 @@ def _bwd_worker(rank, world, port, transport, q):
         local = moe_b200.MoEWeights(w1[rank * el:(rank + 1) * el].to(dev).contiguous(),
                                     w2[rank * el:(rank + 1) * el].to(dev).contiguous())
         layer = MoELayerEP(local, e, topk=k, expert_bias=bias.to(dev), transport=transport,
-                           tokens=t, placement=pl.to(dev))
+                           tokens=t, placement=pl.to(dev), overlap_chunks=chunks)
         out, ctx = layer.forward(x[sl].to(dev), lg[sl].to(dev), save_for_backward=True)
         gx, gp, dw1, dw2 = layer.backward(go[sl].to(dev), ctx)
         err = layer.device_error() + moe_b200.grouped_wgrad_device_error(dev)
@@ -176,7 +176,8 @@ def _bwd_worker(rank, world, port, transport, q):
 
 
 @pytest.mark.parametrize("world,transport", [(2, "fused"), (2, "fused_dedup"), (4, "fused"),
-                                             (8, "fused")])
+                                             (8, "fused"), (2, "fused+overlap3"),
+                                             (8, "fused+overlap2")])
 def test_ep_backward_equals_single_gpu(world, transport):
     """MoELayerEP.backward (combine backward over NVLink, grouped dgrad/wgrad
     on the receive rows, permute backward as the unweighted fused combine)
@@ -191,7 +192,8 @@ def test_ep_backward_equals_single_gpu(world, transport):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_bwd_worker, args=(r, world, port, transport, q))
+    tr, _, ov = transport.partition("+overlap")
+    procs = [ctx.Process(target=_bwd_worker, args=(r, world, port, tr, q, int(ov or 1)))
              for r in range(world)]
     for p in procs:
         p.start()
