@@ -605,7 +605,8 @@ class MoELayerEP:
                   nsend, torch.cuda.current_stream(go.device).cuda_stream)
         peer.barrier()
         dy2 = peer.recv_buf[:nrecv]
-        sp = torch.tensor(ctx["splits"], dtype=torch.int32).to(go.device)
+        sp = torch.tensor(ctx["splits"], dtype=torch.int32).pin_memory().to(go.device,
+                                                                            non_blocking=True)
         self.plan.from_splits(sp)
         dh = ops.grouped_gemm(dy2, self.w.w2, plan=self.plan, w_layout="KN")
         dw2 = ops.grouped_wgrad(dy2, ctx["h"], sp)
