@@ -313,6 +313,7 @@ class GroupedGemmPlan:
         _lib.call("moe_grouped_gemm_workspace_size", self.num_groups, byref(nb))
         self.nbytes = nb.value
         self.workspace = _workspace(self.nbytes, device)
+        self.workspace[:256].zero_()  # error word reads 0 before the first plan
         self.device = device
 
     def from_splits(self, m_splits: torch.Tensor, align: int = 1) -> "GroupedGemmPlan":

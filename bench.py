@@ -357,14 +357,20 @@ def check_ep(layer, x, logits, bias, w, k, placement, world, rank, dev):
     torch.cuda.synchronize()
     same = bool(torch.equal(out, out_ep))
     chk = check_layer(out, mid, x, logits, bias, w1_all, w2_all, k, placement)
-    derr = device_error(layer) + full.plan.device_error()
-    ok = torch.tensor([1 if (same and chk["ok"] and derr == 0) else 0], device=dev)
-    dist.all_reduce(ok, op=dist.ReduceOp.MIN)
+    derr = {"ep": device_error(layer), "single": full.plan.device_error(),
+            "permute": moe_b200.permute_device_error(dev)}
+    mine = {"rank": rank, "ep_equals_single_gpu": same, "checks_ok": bool(chk["ok"]),
+            "failed": [k for k, v in chk.items() if v is False],
+            "device_errors": {k: v for k, v in derr.items() if v}}
+    mine["ok"] = same and chk["ok"] and not mine["device_errors"]
+    every = [None] * world
+    dist.all_gather_object(every, mine)
     del out, mid, full, w1_all, w2_all, out_ep
     torch.cuda.empty_cache()
-    chk.update({"ok": bool(ok.item()), "ep_equals_single_gpu_rank0": same,
-                "scope": "every rank's tokens vs the single-GPU layer bit for bit (ok = all "
-                         "ranks); rank 0's details shown"})
+    chk.update({"ok": all(r["ok"] for r in every), "ranks": every,
+                "scope": "every rank's tokens vs the single-GPU layer bit for bit, and the "
+                         "torch reference on the single-GPU forward (ok = all ranks); rank "
+                         "0's details shown"})
     return chk
 
 
