@@ -86,6 +86,7 @@ struct Params {
   int k_rows;    // K: reduction rows of one weight matrix when b_mn
   int epilogue;  // 0 bf16 out, 1 SwiGLU -> bf16, 2 fp32 out
   int raster;   // pair kernel: pair M-tiles per raster super-row
+  int n_chunk;  // pair kernel: N-tiles per weight-slab chunk (0: super-rows of `raster`)
   int l2_mode;  // pair kernel: 0 both evict_normal, 1 B evict_first, 2 A evict_last + B evict_first,
                 //   3 A evict_first + B evict_last, 4 B evict_last
 };
@@ -133,12 +134,19 @@ struct WalkerT {
 using Walker = WalkerT<BM, kSuperRow>;
 
 // Same walk with the super-row height chosen at run time.
+// n_chunk > 0 replaces the super-rows by N-chunks: a group's tiles are walked
+// chunk by chunk of n_chunk N-tiles, and inside a chunk M-tile by M-tile
+// (every N-tile of the chunk for one M-tile, then the next M-tile). The CTA
+// pairs running at once then share one M-tile of rows and one chunk of the
+// weight slab, which is sized to stay in L2 while all of the group's M-tiles
+// stream past it; rows are read once per chunk.
 template <int kTileM>
 struct WalkerRT {
   const int32_t* rows;
   int G;
   int n_tiles;
   int raster;
+  int n_chunk;
   int g = 0;
   int mt = -1;
   long long base = 0;
@@ -154,11 +162,20 @@ struct WalkerRT {
     }
     if (g >= G) return false;
     const long long local = t - base;
+    tile.g = g;
+    if (n_chunk > 0) {
+      const long long full = static_cast<long long>(mt) * n_chunk;  // tiles of a whole chunk
+      const int ci = static_cast<int>(local / full);
+      const int rem = static_cast<int>(local - ci * full);
+      const int nc = min(n_chunk, n_tiles - ci * n_chunk);  // the last chunk may be narrower
+      tile.m_idx = rem / nc;
+      tile.n_idx = ci * n_chunk + rem % nc;
+      return true;
+    }
     const long long sr_tiles = static_cast<long long>(raster) * n_tiles;
     const int sr = static_cast<int>(local / sr_tiles);
     const int within = static_cast<int>(local - sr * sr_tiles);
     const int mg = min(raster, mt - sr * raster);
-    tile.g = g;
     tile.n_idx = within / mg;
     tile.m_idx = sr * raster + within % mg;
     return true;
@@ -530,7 +547,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
 
-  WalkerRT<pairk::kPairTileM> walker{p.rows, p.G, p.n_tiles, p.raster};
+  WalkerRT<pairk::kPairTileM> walker{p.rows, p.G, p.n_tiles, p.raster, p.n_chunk};
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -1002,6 +1019,12 @@ int pair_clusters(int dev) {
   return n;
 }
 
+// Weight bytes of one slab chunk of the N-chunk walk: about a quarter of L2,
+// so the chunk stays resident while a group's M-tiles stream past it (the
+// measured fc1 slab of 58.7 MB did not, the fc2 slab of 29.4 MB did).
+constexpr int64_t kSlabChunkBytes = 32ll << 20;
+constexpr int kNChunkDefault = 0;
+
 int env_int(const char* name, int def, int lo, int hi) {
   const char* e = getenv(name);
   if (e == nullptr || e[0] == 0) return def;
@@ -1164,6 +1187,7 @@ static int grouped_gemm_run(const void* x, const void* w, void* out, int64_t x_r
   static const int l2_mode = gg::env_int("MOE_GEMM_L2", 0, 0, 4);
   p.raster = raster;
   p.l2_mode = l2_mode;
+  p.n_chunk = 0;
 
   int dev = 0;
   MOE_CUDA_CALL(cudaGetDevice(&dev), "cudaGetDevice");
@@ -1204,6 +1228,16 @@ static int grouped_gemm_run(const void* x, const void* w, void* out, int64_t x_r
                                CU_TENSOR_MAP_SWIZZLE_128B);
         if (st) return st;
       }
+    }
+    // Weight-slab chunks: MOE_GEMM_NCHUNK=-1 picks the most N-tiles whose
+    // weight rows fit in kSlabChunkBytes, k > 0 takes k N-tiles, 0 keeps the
+    // super-rows of MOE_GEMM_RASTER.
+    static const int nchunk_env = gg::env_int("MOE_GEMM_NCHUNK", gg::kNChunkDefault, -1, 1024);
+    if (nchunk_env != 0) {
+      const int64_t ntile_bytes = (epilogue == 1 ? 256 : pb.bn) * K * 2;
+      const int64_t fit = std::max<int64_t>(1, gg::kSlabChunkBytes / ntile_bytes);
+      pb.n_chunk = static_cast<int>(
+          std::min<int64_t>(pb.n_tiles, nchunk_env > 0 ? nchunk_env : fit));
     }
     MOE_CUDA_CALL(cudaLaunchKernelEx(&cfg, gg::grouped_gemm_pair_kernel, ta, tbp, to, pb),
                   "grouped_gemm pair launch");

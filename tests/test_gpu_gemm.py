@@ -477,15 +477,22 @@ def test_bad_arguments(cuda_dev):
 
 
 @pytest.mark.parametrize("env", [{"MOE_GEMM_PAIR": "0", "MOE_WGRAD_PAIR": "0"},
-                                 {"MOE_GEMM_SPLIT": "0"}],
-                         ids=["single_cta", "pair_padded_tails"])
+                                 {"MOE_GEMM_SPLIT": "0"},
+                                 {"MOE_GEMM_NCHUNK": "1", "MOE_GEMM_FOLD": "1",
+                                  "MOE_GEMM_L2": "4"},
+                                 {"MOE_GEMM_NCHUNK": "0", "MOE_GEMM_RASTER": "3",
+                                  "MOE_GEMM_FOLD": "0"}],
+                         ids=["single_cta", "pair_padded_tails", "slab_chunks_folded",
+                              "super_rows"])
 def test_kernel_variants(cuda_dev, env):
     """The non-default kernel paths, each in a fresh process, on ragged groups
     with the bf16, SwiGLU and fp32 epilogues: the single-CTA kernel alone (used
     when CTA pairs cannot be scheduled, or with MOE_GEMM_PAIR=0; with
     MOE_WGRAD_PAIR=0 the wgrad's single-CTA kernel too), and the pair
     kernel with each group's last partial tile padded to 256 rows instead of
-    handed to the single-CTA kernel (MOE_GEMM_SPLIT=0)."""
+    handed to the single-CTA kernel (MOE_GEMM_SPLIT=0), and both pair-kernel
+    tile orders (weight-slab chunks of one N-tile with the remainders folded
+    into the pair kernel; super-rows of three M-tiles)."""
     import os
     import subprocess
     import sys
