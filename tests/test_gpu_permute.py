@@ -115,8 +115,8 @@ def test_permute_chain_vs_oracle(cuda_dev, t, h, e, k):
 def test_permute_paths_give_the_same_bits(cuda_dev):
     """The bulk-copy permute (MOE_PERMUTE_BULK=1: rows staged in shared memory
     by bulk TMA loads and written by bulk TMA stores), the register-staged
-    kernel with 32-byte vectors (the default) and with 16-byte vectors
-    (MOE_PERMUTE_V32=0), each in a fresh process, give the same bits, for the
+    kernel with 16-byte vectors (the default) and with 32-byte vectors
+    (MOE_PERMUTE_V32=1), each in a fresh process, give the same bits, for the
     token-major map with probs and the [E,T] int32 map, with fewer tokens
     than CTAs and with many tokens per CTA; the device error word stays 0."""
     import os
@@ -146,8 +146,8 @@ assert _lib.load().moe_permute_check(None, byref(err)) == 0 and err.value == 0
 print(" ".join(out))
 '''
     res = {}
-    for flag, envs in (("1", {"MOE_PERMUTE_BULK": "1"}), ("0", {"MOE_PERMUTE_V32": "0"}),
-                       ("v32", {})):
+    for flag, envs in (("1", {"MOE_PERMUTE_BULK": "1"}), ("0", {}),
+                       ("v32", {"MOE_PERMUTE_V32": "1"})):
         env = dict(os.environ, **envs)
         r = subprocess.run([sys.executable, "-c", code, str(ROOT / "1188b-reference-kernels_b200"),
                             str(ROOT), str(ROOT / "tests")], env=env, capture_output=True,
