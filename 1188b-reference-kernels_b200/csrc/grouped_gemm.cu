@@ -17,10 +17,12 @@
 // Two kernels share the group table, the raster order and the epilogues:
 //   grouped_gemm_pair_kernel (default): CTA pairs (cta_group::2, clusters of
 //     2) on 256-row tiles, epilogue through 64B-swizzled shared buffers and
-//     TMA tile stores; it takes every group's whole 256-row tiles.
-//   grouped_gemm_kernel: one CTA per SM on 128-row tiles; it takes each
-//     group's remainder (< 256 rows) after the pair kernel, or everything
-//     when CTA pairs cannot be scheduled.
+//     TMA tile stores; it takes every group of at least 256 rows, its last
+//     partial tile row-predicated. Inside a group it walks the N-tiles in
+//     chunks of at most 32 MB of weights, all M-tiles per chunk.
+//   grouped_gemm_kernel: one CTA per SM on 128-row tiles; it takes the groups
+//     of fewer than 256 rows after the pair kernel, or everything when CTA
+//     pairs cannot be scheduled.
 // Single-CTA kernel structure (one persistent CTA per SM, 192 threads):
 //   warp 0      TMA producer: 128x64 A tile + 2 x 128x64 B half-tiles per
 //               stage, 128-byte swizzle, 4-stage mbarrier ring.
@@ -1023,7 +1025,7 @@ int pair_clusters(int dev) {
 // so the chunk stays resident while a group's M-tiles stream past it (the
 // measured fc1 slab of 58.7 MB did not, the fc2 slab of 29.4 MB did).
 constexpr int64_t kSlabChunkBytes = 32ll << 20;
-constexpr int kNChunkDefault = 0;
+constexpr int kNChunkDefault = -1;
 
 int env_int(const char* name, int def, int lo, int hi) {
   const char* e = getenv(name);
@@ -1033,10 +1035,12 @@ int env_int(const char* name, int def, int lo, int hi) {
 }
 
 // Smallest group whose remainder (rows beyond its whole 256-row tiles) stays
-// on the pair kernel: MOE_GEMM_FOLD=1 folds the remainder of every group
-// that has whole tiles; 0 hands every remainder to the single-CTA kernel.
+// on the pair kernel: MOE_GEMM_FOLD=1 (default) folds the remainder of every
+// group that has whole tiles, computed right after that group's other tiles
+// while its weight slab is still in L2; 0 hands every remainder to the
+// single-CTA kernel, which then streams those slabs from HBM once more.
 int fold_min() {
-  static const int v = env_int("MOE_GEMM_FOLD", 0, 0, 1) == 1 ? pairk::kPairTileM : 0x7fffffff;
+  static const int v = env_int("MOE_GEMM_FOLD", 1, 0, 1) == 1 ? pairk::kPairTileM : 0x7fffffff;
   return v;
 }
 
