@@ -466,6 +466,56 @@ def test_full_fc1_fc2_shapes_spot_check(cuda_dev):
         assert_gemm_close(y[torch.as_tensor(rr, device=cuda_dev)], ys, f"fc2 g{gidx}")
 
 
+def test_cfg3_whole_outputs_vs_torch_fp32(cuda_dev):
+    """BASELINE cfg3 in full (T=8192 top-8 routing -> 65536 rows, E=256,
+    H=7168, F=2048): every element of fc1+SwiGLU and of fc2 against fp32
+    products that torch computes per expert on the device (TF32 off; fc1
+    rounded to bf16 before SwiGLU, fc2 fed with the kernel's own fc1 output
+    so each GEMM is checked on its own), with assert_gemm_close's bar:
+    rtol 2e-2 / atol 1e-2 everywhere, >= 99.9 % (fc2) / 99.5 % (fc1+SwiGLU)
+    of the elements within one bf16 ulp."""
+    import torch.nn.functional as F
+    import moe_b200
+    t, e, h, f, topk = 8192, 256, 7168, 2048, 8
+    gc = torch.Generator().manual_seed(3)
+    lg = torch.randn(t, e, generator=gc)
+    r = moe_b200.router_topk(lg.to(cuda_dev), topk, "softmax", renorm=True, outputs="maps")
+    m = moe_b200.row_id_map(r.routing_map)
+    counts = m.counts.cpu().tolist()
+    rows = t * topk
+    gd = torch.Generator(device=cuda_dev).manual_seed(3)
+    x = torch.randn(rows, h, device=cuda_dev, generator=gd).to(torch.bfloat16)
+    w1 = (torch.randn(e, 2 * f, h, device=cuda_dev, generator=gd) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(e, h, f, device=cuda_dev, generator=gd) * 0.02).to(torch.bfloat16)
+    plan = moe_b200.GroupedGemmPlan(e, cuda_dev).from_splits(m.counts)
+    hmid = moe_b200.grouped_gemm(x, w1, epilogue="swiglu", plan=plan)
+    y = moe_b200.grouped_gemm(hmid, w2, plan=plan)
+    assert plan.device_error() == 0
+    prev = torch.backends.cuda.matmul.allow_tf32
+    torch.backends.cuda.matmul.allow_tf32 = False
+    stats = {"fc1": [0, 0], "fc2": [0, 0]}
+
+    def check(name, got, ref):
+        d = (got.float() - ref).abs()
+        assert bool(torch.all(d <= ATOL + RTOL * ref.abs())), (name, float(d.max()))
+        stats[name][0] += int((d <= ref.abs() * 2.0 ** -7 + 1e-6).sum())
+        stats[name][1] += d.numel()
+
+    try:
+        off = 0
+        for g, c in enumerate(counts):
+            if c:
+                y1 = (x[off:off + c].float() @ w1[g].float().t()).to(torch.bfloat16).float()
+                check("fc1", hmid[off:off + c], F.silu(y1[:, :f]) * y1[:, f:])
+                check("fc2", y[off:off + c], hmid[off:off + c].float() @ w2[g].float().t())
+            off += c
+    finally:
+        torch.backends.cuda.matmul.allow_tf32 = prev
+    assert off == rows
+    assert stats["fc1"][0] / stats["fc1"][1] > 0.995, stats
+    assert stats["fc2"][0] / stats["fc2"][1] > 0.999, stats
+
+
 def test_bad_arguments(cuda_dev):
     import moe_b200
     x = torch.zeros(8, 20, dtype=torch.bfloat16, device=cuda_dev)  # K % 8 != 0
