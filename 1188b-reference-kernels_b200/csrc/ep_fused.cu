@@ -139,6 +139,100 @@ __global__ void __launch_bounds__(kRowThreads) ep_dispatch_range_kernel(
   }
 }
 
+// ---------------------------------------------------------------------------
+// Pull dispatch: the receiver loads its rows from the sources instead of the
+// sources storing them. Each source first stages its token rows and, for each
+// of its permuted (expert-major) rows, the token it comes from, in two
+// peer-shared buffers (ep_pull_stage_kernel). After a barrier every receiver
+// walks its expert-major receive rows: row rr of the group (local expert le,
+// source s) is the source's permuted row src_row0[g] + (rr - start[g]), whose
+// token the receiver reads from the source's index, then the row itself;
+// the two loads cross NVLink, the store is local. The receive rows come out
+// exactly as the push dispatch writes them.
+// ---------------------------------------------------------------------------
+constexpr int kPullMaxGroups = 1024;
+
+template <int VPT, typename V>
+__global__ void __launch_bounds__(kRowThreads) ep_pull_stage_kernel(
+    const V* __restrict__ x, const int64_t* __restrict__ map_te, int64_t T, int E, int nvec,
+    int64_t num_rows, V* __restrict__ xs, int32_t* __restrict__ inv) {
+  const int64_t t = blockIdx.x;
+  const int tid = threadIdx.x;
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int i = tid + v * kRowThreads;
+    if (i < nvec) xs[t * nvec + i] = __ldg(x + t * nvec + i);
+  }
+  for (int e = tid; e < E; e += kRowThreads) {
+    const int64_t row = __ldg(map_te + t * E + e);
+    if (row >= 0 && row < num_rows) inv[row] = static_cast<int32_t>(t);
+  }
+}
+
+struct PullSrc {
+  long long xs[kMaxRanks];   // rank s's staged token rows, this process's address
+  long long inv[kMaxRanks];  // rank s's permuted row -> token index
+  long long tok_cap;         // rows of each staging buffer
+  long long row_cap;         // entries of each index
+  int ranks;
+};
+
+template <int VPT, typename V>
+__global__ void __launch_bounds__(kRowThreads) ep_pull_kernel(
+    const PullSrc ps, const int32_t* __restrict__ table, int ng, V* __restrict__ recv,
+    int64_t nrecv, int64_t cap_rows, int nvec) {
+  __shared__ int32_t s_start[kPullMaxGroups];
+  __shared__ int32_t s_cnt[kPullMaxGroups];
+  __shared__ int32_t s_src0[kPullMaxGroups];
+  __shared__ long long s_src;
+  const int tid = threadIdx.x;
+  for (int g = tid; g < ng; g += kRowThreads) {
+    s_start[g] = __ldg(table + g);
+    s_cnt[g] = __ldg(table + ng + g);
+    s_src0[g] = __ldg(table + 2 * ng + g);
+  }
+  __syncthreads();
+  for (int64_t rr = blockIdx.x; rr < nrecv && rr < cap_rows; rr += gridDim.x) {
+    if (tid == 0) {
+      // the last group starting at or before rr (empty groups share the next
+      // group's start, so this lands on the group that holds rr)
+      int lo = 0, hi = ng - 1;
+      while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (s_start[mid] <= rr) lo = mid;
+        else hi = mid - 1;
+      }
+      const int s = lo % ps.ranks;
+      const int64_t j = rr - s_start[lo];
+      const int64_t srow = static_cast<int64_t>(s_src0[lo]) + j;
+      long long a = -1;
+      if (j >= 0 && j < s_cnt[lo] && srow >= 0 && srow < ps.row_cap) {
+        const int32_t tok = reinterpret_cast<const int32_t*>(ps.inv[s])[srow];
+        if (tok >= 0 && tok < ps.tok_cap)
+          a = ps.xs[s] + static_cast<long long>(tok) * nvec * static_cast<long long>(sizeof(V));
+      }
+      s_src = a;
+    }
+    __syncthreads();
+    const long long a = s_src;
+    if (a >= 0) {
+      const V* src = reinterpret_cast<const V*>(a);
+      V r[VPT];
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        const int i = tid + v * kRowThreads;
+        if (i < nvec) r[v] = src[i];
+      }
+#pragma unroll
+      for (int v = 0; v < VPT; ++v) {
+        const int i = tid + v * kRowThreads;
+        if (i < nvec) recv[rr * nvec + i] = r[v];
+      }
+    }
+    __syncthreads();
+  }
+}
+
 constexpr int kEpCombineMaxE = 1024;
 
 template <typename V>
@@ -492,6 +586,76 @@ extern "C" int moe_ep_dispatch_range(const void* x, const int64_t* row_id_map_te
         static_cast<const uint16_t*>(x), row_id_map_te, pr, T, (int)E, nvec, num_rows, lo, hi);
   }
   MOE_CUDA_CHECK_LAUNCH("ep_dispatch_range launch");
+  return MOE_OK;
+}
+
+extern "C" int moe_ep_pull_stage(const void* x, const int64_t* row_id_map_te, int64_t T,
+                                 int64_t H, int64_t E, int64_t num_rows, void* staged_rows,
+                                 int32_t* row_tokens, moe_stream_t stream) {
+  MOE_REQUIRE(T >= 0 && H >= 0 && E >= 1 && num_rows >= 0, "ep_pull_stage: bad shape");
+  MOE_REQUIRE(T < (1ll << 31), "ep_pull_stage: T=%lld above 2^31", (long long)T);
+  if (T == 0 || H == 0) return MOE_OK;
+  MOE_REQUIRE(x && row_id_map_te && staged_rows && row_tokens, "ep_pull_stage: null pointer");
+  MOE_REQUIRE(H % 8 == 0 && ((reinterpret_cast<uintptr_t>(x) |
+                              reinterpret_cast<uintptr_t>(staged_rows)) & 15) == 0,
+              "ep_pull_stage: rows must be 16-byte vectors (H %% 8 == 0, aligned pointers)");
+  const int nvec = static_cast<int>(H / 8);
+  const int vpt = (nvec + kRowThreads - 1) / kRowThreads;
+  MOE_REQUIRE(vpt <= 8, "ep_pull_stage: H=%lld above 8192", (long long)H);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned grid = static_cast<unsigned>(T);
+  const uint4* xv = static_cast<const uint4*>(x);
+  uint4* sv = static_cast<uint4*>(staged_rows);
+  if (vpt <= 2) ep_pull_stage_kernel<2, uint4><<<grid, kRowThreads, 0, s>>>(xv, row_id_map_te, T, (int)E, nvec, num_rows, sv, row_tokens);
+  else if (vpt <= 4) ep_pull_stage_kernel<4, uint4><<<grid, kRowThreads, 0, s>>>(xv, row_id_map_te, T, (int)E, nvec, num_rows, sv, row_tokens);
+  else ep_pull_stage_kernel<8, uint4><<<grid, kRowThreads, 0, s>>>(xv, row_id_map_te, T, (int)E, nvec, num_rows, sv, row_tokens);
+  MOE_CUDA_CHECK_LAUNCH("ep_pull_stage launch");
+  return MOE_OK;
+}
+
+extern "C" int moe_ep_dispatch_pull(const int64_t* peer_staged_rows, const int64_t* peer_row_tokens,
+                                    int32_t ranks, int64_t tokens_cap, int64_t rows_cap,
+                                    const int32_t* group_table, int32_t num_groups, void* recv,
+                                    int64_t num_recv, int64_t cap_rows, int64_t H,
+                                    moe_stream_t stream) {
+  MOE_REQUIRE(ranks >= 1 && ranks <= kMaxRanks, "ep_dispatch_pull: ranks=%d out of [1,%d]", ranks,
+              kMaxRanks);
+  MOE_REQUIRE(num_groups >= 1 && num_groups <= kPullMaxGroups && num_groups % ranks == 0,
+              "ep_dispatch_pull: num_groups=%d must be a multiple of ranks up to %d", num_groups,
+              kPullMaxGroups);
+  MOE_REQUIRE(num_recv >= 0 && cap_rows >= 0 && H >= 0 && tokens_cap >= 0 && rows_cap >= 0,
+              "ep_dispatch_pull: bad sizes");
+  if (num_recv == 0 || H == 0) return MOE_OK;
+  MOE_REQUIRE(peer_staged_rows && peer_row_tokens && group_table && recv,
+              "ep_dispatch_pull: null pointer");
+  MOE_REQUIRE(H % 8 == 0 && (reinterpret_cast<uintptr_t>(recv) & 15) == 0,
+              "ep_dispatch_pull: rows must be 16-byte vectors (H %% 8 == 0, aligned pointers)");
+  PullSrc ps;
+  for (int d = 0; d < kMaxRanks; ++d) {
+    const bool in = d < ranks;
+    MOE_REQUIRE(!in || (peer_staged_rows[d] && peer_row_tokens[d]),
+                "ep_dispatch_pull: null buffer for rank %d", d);
+    MOE_REQUIRE(!in || ((peer_staged_rows[d] & 15) == 0 && (peer_row_tokens[d] & 3) == 0),
+                "ep_dispatch_pull: misaligned buffer for rank %d", d);
+    ps.xs[d] = in ? peer_staged_rows[d] : 0;
+    ps.inv[d] = in ? peer_row_tokens[d] : 0;
+  }
+  ps.tok_cap = tokens_cap;
+  ps.row_cap = rows_cap;
+  ps.ranks = ranks;
+  const int nvec = static_cast<int>(H / 8);
+  const int vpt = (nvec + kRowThreads - 1) / kRowThreads;
+  MOE_REQUIRE(vpt <= 8, "ep_dispatch_pull: H=%lld above 8192", (long long)H);
+  int dev = 0;
+  MOE_CUDA_CALL(cudaGetDevice(&dev), "cudaGetDevice");
+  const int64_t rows = std::min<int64_t>(num_recv, cap_rows);
+  const unsigned grid = static_cast<unsigned>(std::min<int64_t>(rows, 16ll * num_sms(dev)));
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  uint4* rv = static_cast<uint4*>(recv);
+  if (vpt <= 2) ep_pull_kernel<2, uint4><<<grid, kRowThreads, 0, s>>>(ps, group_table, num_groups, rv, num_recv, cap_rows, nvec);
+  else if (vpt <= 4) ep_pull_kernel<4, uint4><<<grid, kRowThreads, 0, s>>>(ps, group_table, num_groups, rv, num_recv, cap_rows, nvec);
+  else ep_pull_kernel<8, uint4><<<grid, kRowThreads, 0, s>>>(ps, group_table, num_groups, rv, num_recv, cap_rows, nvec);
+  MOE_CUDA_CHECK_LAUNCH("ep_dispatch_pull launch");
   return MOE_OK;
 }
 

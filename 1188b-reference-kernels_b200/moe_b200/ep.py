@@ -203,6 +203,27 @@ def expert_major_layout(counts_all: Sequence[Sequence[int]], rank: int,
                              [int(v) for v in tot.sum(axis=1)])
 
 
+def pull_group_table(counts_all: Sequence[Sequence[int]], rank: int, local_experts: int):
+    """Group table of the pull dispatch on `rank` from the gathered [G, E]
+    per-expert counts: for group g = le * G + s (local expert le, source s),
+    the first receive row, the row count and the source's first permuted row
+    of that expert. The receive rows are those of expert_major_layout (the
+    push dispatch's): source s's rows of expert e land at its permuted row +
+    deltas_s[e]. Returns three lists of G * local_experts ints."""
+    import numpy as np
+    c = np.asarray(counts_all, dtype=np.int64)
+    g, e = c.shape
+    el = int(local_experts)
+    if e != g * el:
+        raise ValueError("counts do not match world size x local experts")
+    mine = c[:, rank * el:(rank + 1) * el]                        # [G sources, E_loc]
+    src_start = (np.cumsum(c, axis=1) - c)[:, rank * el:(rank + 1) * el]
+    cnt = mine.T.reshape(-1)                                       # le-major, then source
+    start = np.cumsum(cnt) - cnt
+    src0 = src_start.T.reshape(-1)
+    return [int(v) for v in start], [int(v) for v in cnt], [int(v) for v in src0]
+
+
 class EPPeerExchange:
     """Row exchange through peer-mapped buffers and the copy engines.
 
@@ -219,7 +240,7 @@ class EPPeerExchange:
 
     def __init__(self, num_experts: int, tokens: int, hidden: int, topk: int,
                  device: torch.device, group: Optional[dist.ProcessGroup] = None,
-                 fused: bool = False, dedup: bool = False):
+                 fused: bool = False, dedup: bool = False, pull: bool = False):
         """fused=False: receive + return buffers, rows moved by copy engines.
         fused=True: receive + fc2-output buffers; the dispatch kernel stores
         rows into the peers' receive buffers and the combine kernel loads the
@@ -228,6 +249,8 @@ class EPPeerExchange:
         rows, and each rank expands them into its receive buffer."""
         self.fused = fused
         self.dedup = bool(dedup and fused)
+        self.pull = bool(pull and fused and not self.dedup)
+        self.topk = int(topk)
         self.tokens = int(tokens)
         self.group = group
         self.world = dist.get_world_size(group)
@@ -250,6 +273,14 @@ class EPPeerExchange:
             self.y_buf = torch.empty((self.recv_cap, hidden), dtype=torch.bfloat16,
                                      device=self.device)
             self.peer_y = self._share(self.y_buf)
+        if self.pull:
+            # this rank's staged token rows and permuted row -> token index,
+            # read by the receivers of the pull dispatch
+            self.xs_buf = torch.empty((self.tokens, hidden), dtype=torch.bfloat16,
+                                      device=self.device)
+            self.inv_buf = torch.empty((self.rows_cap,), dtype=torch.int32, device=self.device)
+            self.peer_xs = self._share(self.xs_buf)
+            self.peer_inv = self._share(self.inv_buf)
         if self.dedup:
             rows = self.world * self.tokens
             self.stage_buf = torch.empty((rows, hidden), dtype=torch.bfloat16, device=self.device)
@@ -377,6 +408,28 @@ class EPPeerExchange:
                   self.num_experts, nsend, int(local_lo), int(local_hi), int(max_ctas),
                   torch.cuda.current_stream(self.device).cuda_stream)
 
+    def fused_dispatch_pull(self, x: torch.Tensor, map_te: torch.Tensor, counts_all,
+                            nsend: int, nrecv: int) -> torch.Tensor:
+        """Stages x and the permuted-row -> token index of this rank, barriers,
+        then loads this rank's receive rows from their sources (the rows of
+        the push dispatch, in the same places)."""
+        t, h = x.shape
+        if t > self.tokens:
+            raise ValueError(f"{t} tokens exceed the staging capacity of {self.tokens}")
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        _lib.call("moe_ep_pull_stage", x.data_ptr(), map_te.data_ptr(), t, h, self.num_experts,
+                  nsend, self.xs_buf.data_ptr(), self.inv_buf.data_ptr(), stream)
+        start, cnt, src0 = pull_group_table(counts_all, self.rank, self.local_experts)
+        table = torch.tensor(start + cnt + src0, dtype=torch.int32).pin_memory().to(
+            self.device, non_blocking=True)
+        self.barrier()  # every rank's staged rows and index are in place
+        n = self.world
+        arr = lambda v: (ctypes.c_int64 * n)(*v)  # noqa: E731
+        _lib.call("moe_ep_dispatch_pull", arr(self.peer_xs), arr(self.peer_inv), n, self.tokens,
+                  self.rows_cap, table.data_ptr(), len(start), self.recv_buf.data_ptr(), nrecv,
+                  self.recv_cap, h, stream)
+        return self.recv_buf[:nrecv]
+
     def fused_dispatch_dedup(self, x: torch.Tensor, map_te: torch.Tensor, deltas: torch.Tensor,
                              nsend: int, nrecv: int) -> torch.Tensor:
         """Token rows once per destination rank into the peers' staging rows
@@ -434,7 +487,9 @@ class MoELayerEP:
         buffers filled by copy-engine pushes; "fused": the dispatch and combine
         kernels store / load rows in the peers' buffers directly; "fused_dedup":
         as "fused", with each token row sent once per destination rank and
-        expanded there. "peer" and "fused*" need `tokens`, the per-rank T. placement (int32 [E] permutation):
+        expanded there; "fused_pull": as "fused", with each receiver loading
+        its rows from the sources' staged rows instead of the sources storing
+        them. "peer" and "fused*" need `tokens`, the per-rank T. placement (int32 [E] permutation):
         slot c is model expert placement[c]; this rank holds the weights of
         slots [rank*E_loc, (rank+1)*E_loc) (e.g. from balanced_placement).
 
@@ -450,15 +505,17 @@ class MoELayerEP:
         self.placement = placement
         self.disp = EPDispatcher(num_experts, group)
         self.peer = None
-        self.fused = transport in ("fused", "fused_dedup")
-        if transport in ("peer", "fused", "fused_dedup"):
+        self.fused = transport in ("fused", "fused_dedup", "fused_pull")
+        if transport in ("peer", "fused", "fused_dedup", "fused_pull"):
             if tokens is None:
                 raise ValueError(f"transport='{transport}' needs the per-rank token count")
             self.peer = EPPeerExchange(num_experts, tokens, local_weights.hidden, topk,
                                        local_weights.w1.device, group, fused=self.fused,
-                                       dedup=transport == "fused_dedup")
+                                       dedup=transport == "fused_dedup",
+                                       pull=transport == "fused_pull")
         elif transport != "nccl":
-            raise ValueError("transport must be 'nccl', 'peer', 'fused' or 'fused_dedup'")
+            raise ValueError("transport must be 'nccl', 'peer', 'fused', 'fused_dedup' or "
+                             "'fused_pull'")
         if local_weights.num_experts != self.disp.local_experts:
             raise ValueError("local weights do not match num_experts / world size")
         self.w = local_weights
@@ -547,6 +604,8 @@ class MoELayerEP:
         else:
             if self.peer.dedup:
                 xr = self.peer.fused_dispatch_dedup(x, rim.map_te, deltas, nsend, nrecv)
+            elif self.peer.pull:
+                xr = self.peer.fused_dispatch_pull(x, rim.map_te, host, nsend, nrecv)
             else:
                 xr = self.peer.fused_dispatch(x, rim.map_te, deltas, nsend, nrecv)
             self._ev("a2a_dispatch")

@@ -83,7 +83,8 @@ def parse_args():
     ap.add_argument("--placement", choices=["balanced", "contiguous"], default="balanced",
                     help="EP expert placement: load-balanced (E/G experts per GPU, chosen from "
                          "the routing of the benchmark's own logits) or contiguous id ranges")
-    ap.add_argument("--transport", choices=["auto", "fused", "fused_dedup", "peer", "nccl"],
+    ap.add_argument("--transport", choices=["auto", "fused", "fused_dedup", "fused_pull", "peer",
+                                            "nccl"],
                     default="auto",
                     help="EP row exchange: dispatch/combine kernels on peer memory (fused_dedup: "
                          "a token row crosses NVLink once per destination rank), IPC-mapped "

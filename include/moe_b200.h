@@ -326,6 +326,26 @@ int moe_ep_dispatch_range(const void* x, const int64_t* row_id_map_te, const int
                           int64_t cap_rows, int64_t T, int64_t H, int64_t E, int64_t num_rows,
                           int32_t local_lo, int32_t local_hi, int32_t max_ctas,
                           moe_stream_t stream);
+/* Pull form of the fused dispatch (the same receive rows, loaded by the     */
+/* receiver instead of stored by the source; the deep_ep FusedDispatch the    */
+/* reference names, kernel_cases/case22_ref_moe_permute_mask_kernel_true.py: */
+/* 3-6). Step 1, on every rank: moe_ep_pull_stage copies x [T,H] into this    */
+/* rank's peer-shared staging rows and writes row_tokens[r] = t for each      */
+/* routed (t, e) with r = map[t,e] < num_rows. Step 2, after a barrier, on    */
+/* every rank: moe_ep_dispatch_pull fills recv[0, num_recv): group g =       */
+/* le * ranks + s of group_table (int32 [3][num_groups] on the device: first  */
+/* receive row, rows, first permuted row of source s for local expert le;    */
+/* groups in that order, first rows ascending) takes its rows from source s's */
+/* staged rows, each token read from s's row_tokens. Loads outside           */
+/* tokens_cap / rows_cap are skipped. H % 8 == 0, H <= 8192; num_groups <=   */
+/* 1024.                                                                      */
+int moe_ep_pull_stage(const void* x, const int64_t* row_id_map_te, int64_t T, int64_t H, int64_t E,
+                      int64_t num_rows, void* staged_rows, int32_t* row_tokens,
+                      moe_stream_t stream);
+int moe_ep_dispatch_pull(const int64_t* peer_staged_rows, const int64_t* peer_row_tokens,
+                         int32_t ranks, int64_t tokens_cap, int64_t rows_cap,
+                         const int32_t* group_table, int32_t num_groups, void* recv,
+                         int64_t num_recv, int64_t cap_rows, int64_t H, moe_stream_t stream);
 /* Fused combine: out[t] = bf16(sum over e ascending of probs[t,e] * row),   */
 /* each row read from rank e / experts_per_rank's buffer at map[t,e] +       */
 /* expert_deltas[e] (device array); probs null = unweighted. Same arithmetic */

@@ -97,6 +97,16 @@ def test_invalid_arguments_are_rejected_without_launch(lib):
     assert b"4096" in lib.moe_b200_last_error()
     assert lib.moe_grouped_wgrad_dev(16, 16, 16, 10, 8, 64, 64, None, 256, 1 << 30, None) == 1
     assert b"device array" in lib.moe_b200_last_error()
+    # pull dispatch: groups a multiple of the ranks and at most 1024, 16-byte rows
+    pb = (ctypes.c_int64 * 2)(256, 512)
+    pd = lib.moe_ep_dispatch_pull
+    assert pd(pb, pb, 2, 64, 512, 16, 3, 256, 10, 100, 64, None) == 1
+    assert b"multiple of ranks" in lib.moe_b200_last_error()
+    assert pd(pb, pb, 2, 64, 512, 16, 2048, 256, 10, 100, 64, None) == 1
+    assert pd(pb, pb, 2, 64, 512, 16, 4, 256, 10, 100, 60, None) == 1
+    assert pd(pb, pb, 2, 64, 512, 16, 4, 256, 0, 100, 64, None) == 0  # nothing to receive
+    assert lib.moe_ep_pull_stage(16, 16, 4, 60, 8, 32, 16, 16, None) == 1
+    assert lib.moe_ep_pull_stage(None, None, 0, 64, 8, 0, None, None, None) == 0
     # one chunk of the fused EP dispatch: the local expert range must lie in
     # [0, experts_per_rank); an empty range launches nothing
     dr = lib.moe_ep_dispatch_range

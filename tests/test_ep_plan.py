@@ -9,7 +9,7 @@ sender's permuted buffer had it.
 import numpy as np
 import pytest
 
-from moe_b200.ep import ep_group_table, exchange_plan, expert_major_layout
+from moe_b200.ep import ep_group_table, exchange_plan, expert_major_layout, pull_group_table
 
 
 @pytest.mark.parametrize("world,experts", [(2, 8), (4, 16), (8, 256)])
@@ -116,3 +116,33 @@ def test_overlap_chunks_cover_every_local_expert_once(el, chunks):
         assert a < b and b == c
     sizes = [b - a for a, b in bounds]
     assert max(sizes) - min(sizes) <= 1
+
+
+@pytest.mark.parametrize("world,experts", [(2, 8), (4, 16), (8, 256)])
+@pytest.mark.parametrize("seed", [0, 1])
+def test_pull_group_table_matches_push_layout(world, experts, seed):
+    """The pull dispatch's group table sends every receive row to the source
+    permuted row that the push dispatch stores there (row + deltas_s[e])."""
+    rng = np.random.default_rng(seed)
+    counts = rng.integers(0, 40, size=(world, experts))
+    counts[:, rng.integers(0, experts, 3)] = 0  # some empty (source, expert) blocks
+    el = experts // world
+    for rank in range(world):
+        lay = expert_major_layout(counts.tolist(), rank, el)
+        n = sum(lay.splits)
+        push = np.full(n, -1)
+        pull = np.full(n, -1)
+        for s in range(world):
+            deltas = expert_major_layout(counts.tolist(), s, el).deltas
+            src_start = np.cumsum(counts[s]) - counts[s]
+            for le in range(el):
+                e = rank * el + le
+                for j in range(counts[s, e]):
+                    push[src_start[e] + j + deltas[e]] = s * 1000000 + src_start[e] + j
+        start, cnt, src0 = pull_group_table(counts.tolist(), rank, el)
+        assert start == sorted(start) and start[0] == 0
+        for g, (a, c, r0) in enumerate(zip(start, cnt, src0)):
+            s = g % world
+            for j in range(c):
+                pull[a + j] = s * 1000000 + r0 + j
+        assert np.array_equal(push, pull) and (pull >= 0).all()

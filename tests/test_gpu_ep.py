@@ -26,15 +26,16 @@ FORWARD = {
     2: [("uniform", "nccl"), ("zipf", "nccl"), ("zipf", "peer"), ("uniform", "peer"),
         ("zipf", "fused"), ("uniform", "fused"), ("zipf", "fused+placed"),
         ("zipf", "fused_dedup"), ("zipf", "fused+overlap2"),
-        ("uniform", "fused+placed+overlap3")],
+        ("uniform", "fused+placed+overlap3"), ("zipf", "fused_pull+placed"),
+        ("uniform", "fused_pull")],
     4: [("zipf", "peer"), ("uniform", "nccl"), ("zipf", "fused"), ("uniform", "fused"),
         ("zipf", "fused+placed"), ("uniform", "fused_dedup"), ("zipf", "fused_dedup+placed"),
-        ("zipf", "fused+placed+overlap2")],
+        ("zipf", "fused+placed+overlap2"), ("zipf", "fused_pull+placed")],
     8: [("zipf", "fused+placed"), ("uniform", "nccl"), ("zipf", "fused_dedup+placed"),
-        ("zipf", "fused+placed+overlap2")],
+        ("zipf", "fused+placed+overlap2"), ("zipf", "fused_pull+placed")],
 }
-BACKWARD = {2: ["fused", "fused_dedup", "fused+overlap3"], 4: ["fused"],
-            8: ["fused", "fused+overlap2"]}
+BACKWARD = {2: ["fused", "fused_dedup", "fused+overlap3", "fused_pull"], 4: ["fused", "fused_pull"],
+            8: ["fused", "fused+overlap2", "fused_pull"]}
 
 
 def _free_port() -> int:
@@ -189,8 +190,8 @@ def _need(world):
 @pytest.mark.parametrize("world", [2, 4, 8])
 def test_ep_forward_equals_single_gpu(world):
     """Every forward variant of this world size: NCCL all-to-all, copy-engine
-    peer copies, fused dispatch/combine kernels on peer memory, the
-    deduplicated dispatch, balanced placement and the chunked comm/GEMM
+    peer copies, fused dispatch/combine kernels on peer memory (push, pull
+    and deduplicated dispatch), balanced placement and the chunked comm/GEMM
     overlap, each equal to the single-GPU layer bit for bit."""
     _need(world)
     for rank, res in _results(world):
