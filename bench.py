@@ -95,12 +95,14 @@ def parse_args():
                     help="EP with --transport fused: split the local experts into this many "
                          "chunks and dispatch chunk c+1 over NVLink while chunk c's GEMMs run "
                          "(1 = no overlap)")
-    ap.add_argument("--workload", choices=["layer", "router_gemm", "backward", "wgrad"],
+    ap.add_argument("--workload", choices=["layer", "router_gemm", "backward", "wgrad",
+                                           "rowcopy"],
                     default="layer",
                     help="layer: the MoE expert-layer forward (the headline); router_gemm: the "
                          "router gate GEMM that produces its logits; backward: the layer's "
                          "grouped dgrad and wgrad GEMMs; wgrad: the grouped wgrad alone at "
-                         "--wgrad-shape (one GPU)")
+                         "--wgrad-shape; rowcopy: the layer's permute and weighted combine "
+                         "alone, with no expert weights on the device (one GPU)")
     ap.add_argument("--wgrad-shape", default="40,4096,5120,8192",
                     help="G,T,N,K of --workload wgrad (uniform groups; default: the traced "
                          "shape of kernel_cases/case09_moe_grouped_gemm_fc1_wgrad.py)")
@@ -614,6 +616,77 @@ def run_backward(a):
 
 
 # --------------------------------------------------------------------------- grouped wgrad alone
+def run_rowcopy(a):
+    """The layer's two row kernels at the bench shape without the GEMMs: the
+    permute of x [T,H] into T*k expert-major rows and the gate-weighted
+    combine of T*k rows back to [T,H], routing from the bench's own logits.
+    Only x, the permuted rows, the maps and the output are on the device
+    (about 4.3 GB), so the kernels can be profiled at the layer's size.
+    Inputs (1.9 GB of rows) are larger than L2."""
+    import torch
+    import moe_b200
+    from moe_b200 import _lib
+    t, h, e, k = a.tokens, a.hidden, a.experts, a.topk
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    moe_b200.load_library()
+    g = torch.Generator(device=dev)
+    g.manual_seed(1000)
+    x = torch.randn(t, h, device=dev, generator=g).to(torch.bfloat16)
+    logits = torch.randn(t, e, device=dev, generator=g)
+    r = moe_b200.router_topk(logits, k, "softmax", True, zipf_bias(e, a.routing).to(dev),
+                             outputs="maps")
+    rim = moe_b200.row_id_map(r.routing_map, want_et=False)
+    rows = t * k
+    xp = torch.empty(rows, h, dtype=torch.bfloat16, device=dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+
+    def step():
+        ev[0].record()
+        xp_, _ = moe_b200.permute(x, rim.map_te, None, num_out=rows)
+        ev[1].record()
+        moe_b200.unpermute(xp_, rim.map_te, r.probs, probs_mode="dense", token_major=True)
+        ev[2].record()
+        return xp_
+
+    sampler = ClockSampler(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0])
+    sampler.start()
+    for _ in range(a.warmup):
+        step()
+    torch.cuda.synchronize()
+    launches0 = _lib.launch_count
+    wall0 = time.time()
+    tp = tc = 0.0
+    for _ in range(a.steps):
+        step()
+        torch.cuda.synchronize()
+        tp += ev[0].elapsed_time(ev[1]) / 1e3
+        tc += ev[1].elapsed_time(ev[2]) / 1e3
+    sampler.mark(wall0, time.time())
+    launches = _lib.launch_count - launches0
+    clocks = sampler.stop()
+    tp, tc = tp / a.steps, tc / a.steps
+    perm_bytes = t * h * 2 + rows * h * 2 + t * e * 8
+    comb_bytes = rows * h * 2 + t * h * 2 + t * e * 8 + t * e * 4
+    peaks, peak_kind = load_peaks()
+    hbm = float(peaks.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"]))
+    pg, cg = perm_bytes / tp / 1e9, comb_bytes / tc / 1e9
+    line = {"metric": "permute + combine tokens/s", "value": t / (tp + tc), "unit": "tokens/s",
+            "n_gpus": 1, "steps": a.steps, "warmup": a.warmup, "ms_per_step": (tp + tc) * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) activations/logits, Zipf expert bias)",
+            "config": {"workload": "rowcopy", "tokens": t, "hidden": h, "experts": e, "topk": k,
+                       "routing": a.routing, "l2": "no flush: rows (1.9 GB) exceed L2"},
+            "roofline": {"bound": "hbm", "kernel": "permute_kernel", "achieved": round(pg, 1),
+                         "peak": hbm, "unit": "GB/s", "frac": round(pg / hbm, 4),
+                         "traffic": None},
+            "permute_ms": round(tp * 1e3, 4), "combine_ms": round(tc * 1e3, 4),
+            "permute_gbs": round(pg, 1), "combine_gbs": round(cg, 1),
+            "combine_frac": round(cg / hbm, 4), "peak_kind": f"hbm copy, of {peak_kind}",
+            "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 def run_wgrad(a):
     """dW[g] = dy[seg]^T @ x[seg] over G uniform groups of T rows (N(0,1)
     inputs), timed over --steps calls of the public op."""
@@ -820,6 +893,10 @@ def main():
     if a.workload == "wgrad":
         if rank == 0 and a.impl != "reference":
             run_wgrad(a)
+        return
+    if a.workload == "rowcopy":
+        if rank == 0 and a.impl != "reference":
+            run_rowcopy(a)
         return
     if a.impl == "reference":
         run_reference_arm(a, world, rank)
