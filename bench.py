@@ -638,7 +638,6 @@ def run_rowcopy(a):
                              outputs="maps")
     rim = moe_b200.row_id_map(r.routing_map, want_et=False)
     rows = t * k
-    xp = torch.empty(rows, h, dtype=torch.bfloat16, device=dev)
     ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
 
     def step():
