@@ -188,6 +188,51 @@ __global__ void __launch_bounds__(32) permute_bulk_kernel(
   }
 }
 
+// Permute driven by the router's expert list: experts[t, j] (j < k) names the
+// experts token t goes to, so thread j reads its destination row straight
+// from map[t, experts[t, j]] -- k scattered 8-byte loads per token instead of
+// the whole E-entry map row and its ballot compaction. The copy is the same
+// as permute_kernel's (a destination row is the same whatever order the
+// experts come in). Entries naming an expert outside [0, E) or a row outside
+// [0, num_out) are skipped.
+constexpr int kListMaxK = 32;
+
+template <int VPT, typename V>
+__global__ void __launch_bounds__(kRowThreads) permute_list_kernel(
+    const V* __restrict__ x, const int64_t* __restrict__ map_te,
+    const int64_t* __restrict__ experts, int k, const float* __restrict__ probs,
+    V* __restrict__ out, float* __restrict__ pp, int64_t T, int E, int nvec, int64_t num_out) {
+  __shared__ int64_t s_dst[kListMaxK];
+  const int64_t t = blockIdx.x;
+  const int tid = threadIdx.x;
+  const V* src = x + t * nvec;
+  V r[VPT];
+#pragma unroll
+  for (int v = 0; v < VPT; ++v) {
+    const int i = tid + v * kRowThreads;
+    if (i < nvec) r[v] = __ldg(src + i);
+  }
+  if (tid < k) {
+    const int64_t e = __ldg(experts + t * k + tid);
+    int64_t d = -1;
+    if (e >= 0 && e < E) d = __ldg(map_te + t * E + e);
+    if (d >= num_out) d = -1;
+    s_dst[tid] = d;
+    if (d >= 0 && pp != nullptr) pp[d] = __ldg(probs + t * E + e);
+  }
+  __syncthreads();
+  for (int j = 0; j < k; ++j) {
+    const int64_t dd = s_dst[j];
+    if (dd < 0) continue;  // block-uniform
+    V* o = out + dd * nvec;
+#pragma unroll
+    for (int v = 0; v < VPT; ++v) {
+      const int i = tid + v * kRowThreads;
+      if (i < nvec) o[i] = r[v];
+    }
+  }
+}
+
 // probs_mode: -1 unweighted, 0 probs[t*E+e], 1 probs[src row].
 // gp_out (optional, [T,E] fp32): the permute backward's prob gradient,
 // gp_out[t,e] = pgrad[src row] for a routed (t,e), else 0.
@@ -558,6 +603,42 @@ int check_row_args(const char* op, const void* a, const void* b, int64_t T, int6
 }  // namespace moe
 
 using namespace moe;
+
+extern "C" int moe_permute_topk(const void* x, const int64_t* row_id_map_te,
+                                const int64_t* topk_experts, int32_t k, const float* probs,
+                                void* out, float* permuted_probs, int64_t T, int64_t H, int64_t E,
+                                int64_t num_out, moe_stream_t stream) {
+  int st = check_row_args("permute_topk", x, out, T, H, E);
+  if (st) return st;
+  MOE_REQUIRE(k >= 1 && k <= kListMaxK, "permute_topk: k=%d out of [1,%d]", k, kListMaxK);
+  MOE_REQUIRE(num_out >= 0, "permute_topk: num_out=%lld < 0", (long long)num_out);
+  if (T == 0 || H == 0 || num_out == 0) return MOE_OK;
+  MOE_REQUIRE((probs == nullptr) == (permuted_probs == nullptr),
+              "permute_topk: probs and permuted_probs must both be given or both be null");
+  MOE_REQUIRE(x && out && row_id_map_te && topk_experts, "permute_topk: null pointer");
+  MOE_REQUIRE(vec_bytes(x, out, H) == 16,
+              "permute_topk: rows must be 16-byte vectors (H %% 8 == 0, aligned pointers)");
+  const int nvec = static_cast<int>(H / 8);
+  const int vpt = (nvec + kRowThreads - 1) / kRowThreads;
+  MOE_REQUIRE(vpt <= 8, "permute_topk: H=%lld above 8192", (long long)H);
+  cudaStream_t s = reinterpret_cast<cudaStream_t>(stream);
+  const unsigned grid = static_cast<unsigned>(T);
+  const uint4* xv = static_cast<const uint4*>(x);
+  uint4* ov = static_cast<uint4*>(out);
+  const int e = static_cast<int>(E);
+#define MOE_PERMUTE_LIST_CASE(VP)                                                           \
+  permute_list_kernel<VP, uint4><<<grid, kRowThreads, 0, s>>>(xv, row_id_map_te, topk_experts, \
+                                                               k, probs, ov, permuted_probs, T, e, \
+                                                               nvec, num_out)
+  if (vpt <= 1) MOE_PERMUTE_LIST_CASE(1);
+  else if (vpt <= 2) MOE_PERMUTE_LIST_CASE(2);
+  else if (vpt <= 4) MOE_PERMUTE_LIST_CASE(4);
+  else if (vpt <= 7) MOE_PERMUTE_LIST_CASE(7);
+  else MOE_PERMUTE_LIST_CASE(8);
+#undef MOE_PERMUTE_LIST_CASE
+  MOE_CUDA_CHECK_LAUNCH("permute_topk launch");
+  return MOE_OK;
+}
 
 extern "C" int moe_permute_mask_map(const void* x, const int64_t* row_id_map_te, const float* probs,
                                     void* out, float* permuted_probs, int64_t T, int64_t H,

@@ -90,6 +90,8 @@ _SIGNATURES = {
     "moe_ep_dispatch": [c_void_p, c_void_p, c_void_p, c_void_p, c_int32, c_int32, c_int64,
                         c_int64, c_int64, c_int64, c_int64, c_void_p],
     "moe_permute_check": [c_void_p, POINTER(c_int32)],
+    "moe_permute_topk": [c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_void_p,
+                         c_int64, c_int64, c_int64, c_int64, c_void_p],
     "moe_ep_pull_stage": [c_void_p, c_void_p, c_int64, c_int64, c_int64, c_int64, c_void_p,
                           c_void_p, c_void_p],
     "moe_ep_dispatch_pull": [c_void_p, c_void_p, c_int32, c_int64, c_int64, c_void_p, c_int32,
@@ -118,7 +120,7 @@ _LAUNCHES = {"moe_topk_f32": 1, "moe_router_topk": 1, "moe_router_topk_placed": 
              "moe_permute_mask_map": 1, "moe_permute_mask_map_trans": 1, "moe_unpermute_mask": 1,
              "moe_unpermute_mask_token_major": 1, "moe_ep_dispatch": 1, "moe_ep_combine": 1,
              "moe_ep_dispatch_range": 1, "moe_ep_combine_backward": 1,
-             "moe_ep_pull_stage": 1, "moe_ep_dispatch_pull": 1,
+             "moe_ep_pull_stage": 1, "moe_ep_dispatch_pull": 1, "moe_permute_topk": 1,
              "moe_permute_backward": 1, "moe_ep_dispatch_dedup": 1, "moe_ep_expand": 1,
              "moe_combine_backward": 1, "moe_swiglu_backward": 1,
              "moe_grouped_gemm_plan_splits": 1, "moe_grouped_gemm_plan_ep": 1,

@@ -179,12 +179,15 @@ def _permute_outputs(x, probs, num_out, dense):
 
 
 def permute(x: torch.Tensor, row_id_map: torch.Tensor, probs: Optional[torch.Tensor] = None,
-            num_out: Optional[int] = None):
+            num_out: Optional[int] = None, experts: Optional[torch.Tensor] = None):
     """out[row_id_map[t,e]] = x[t]; permuted_probs[row_id_map[t,e]] = probs[t,e].
 
     row_id_map is the token-major [T,E] int64 map (case17). When num_out is
     None it is max(row_id_map)+1, found with one host sync as the reference
     binding does (kernel_results/case17_moe_permute_with_mask_map/binding.cpp:24).
+    experts (optional [T,k] int64, e.g. RouterOutput.topk_idx): the experts of
+    each token; the kernel then reads only those k map entries per token
+    (moe_permute_topk), with the same result.
     Returns (out [num_out,H], permuted_probs [num_out] or None).
     """
     for n_, t_ in (("x", x), ("row_id_map", row_id_map), ("probs", probs)):
@@ -207,6 +210,15 @@ def permute(x: torch.Tensor, row_id_map: torch.Tensor, probs: Optional[torch.Ten
         num_out, nvalid = _map_stats(mc) if mc.numel() else (0, 0)
         dense = nvalid >= num_out
     out, pp = _permute_outputs(xc, pc, int(num_out), dense)
+    if experts is not None and xc.shape[1] % 8 == 0 and (xc.data_ptr() | out.data_ptr()) % 16 == 0:
+        _need_cuda("experts", experts)
+        _need_dtype("experts", experts, torch.int64)
+        if experts.dim() != 2 or experts.shape[0] != t:
+            raise ValueError(f"experts must be [{t},k]")
+        ec = experts.contiguous()
+        _lib.call("moe_permute_topk", _p(xc), _p(mc), _p(ec), ec.shape[1], _p(pc), _p(out),
+                  _p(pp), t, xc.shape[1], e, int(num_out), _stream(xc.device))
+        return out, pp
     _lib.call("moe_permute_mask_map", _p(xc), _p(mc), _p(pc), _p(out), _p(pp), t, xc.shape[1], e,
               int(num_out), _stream(xc.device))
     return out, pp

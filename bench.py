@@ -635,10 +635,10 @@ def run_rowcopy(a):
     x = torch.randn(t, h, device=dev, generator=g).to(torch.bfloat16)
     logits = torch.randn(t, e, device=dev, generator=g)
     r = moe_b200.router_topk(logits, k, "softmax", True, zipf_bias(e, a.routing).to(dev),
-                             outputs="maps")
+                             outputs="all")
     rim = moe_b200.row_id_map(r.routing_map, want_et=False)
     rows = t * k
-    ev = [torch.cuda.Event(enable_timing=True) for _ in range(3)]
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
 
     def step():
         ev[0].record()
@@ -646,7 +646,9 @@ def run_rowcopy(a):
         ev[1].record()
         moe_b200.unpermute(xp_, rim.map_te, r.probs, probs_mode="dense", token_major=True)
         ev[2].record()
-        return xp_
+        xl, _ = moe_b200.permute(x, rim.map_te, None, num_out=rows, experts=r.topk_idx)
+        ev[3].record()
+        return xp_, xl
 
     sampler = ClockSampler(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0])
     sampler.start()
@@ -655,16 +657,18 @@ def run_rowcopy(a):
     torch.cuda.synchronize()
     launches0 = _lib.launch_count
     wall0 = time.time()
-    tp = tc = 0.0
+    tp = tc = tl = 0.0
     for _ in range(a.steps):
-        step()
+        xa, xb = step()
         torch.cuda.synchronize()
         tp += ev[0].elapsed_time(ev[1]) / 1e3
         tc += ev[1].elapsed_time(ev[2]) / 1e3
+        tl += ev[2].elapsed_time(ev[3]) / 1e3
+    same = bool(torch.equal(xa, xb))
     sampler.mark(wall0, time.time())
     launches = _lib.launch_count - launches0
     clocks = sampler.stop()
-    tp, tc = tp / a.steps, tc / a.steps
+    tp, tc, tl = tp / a.steps, tc / a.steps, tl / a.steps
     perm_bytes = t * h * 2 + rows * h * 2 + t * e * 8
     comb_bytes = rows * h * 2 + t * h * 2 + t * e * 8 + t * e * 4
     peaks, peak_kind = load_peaks()
@@ -680,6 +684,10 @@ def run_rowcopy(a):
                          "peak": hbm, "unit": "GB/s", "frac": round(pg / hbm, 4),
                          "traffic": None},
             "permute_ms": round(tp * 1e3, 4), "combine_ms": round(tc * 1e3, 4),
+            "permute_from_expert_list": {"ms": round(tl * 1e3, 4),
+                                         "gbs": round(perm_bytes / tl / 1e9, 1),
+                                         "frac": round(perm_bytes / tl / 1e9 / hbm, 4),
+                                         "same_rows": same},
             "permute_gbs": round(pg, 1), "combine_gbs": round(cg, 1),
             "combine_frac": round(cg / hbm, 4), "peak_kind": f"hbm copy, of {peak_kind}",
             "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clocks}

@@ -143,6 +143,15 @@ int moe_permute_mask_map(const void* x, const int64_t* row_id_map_te, const floa
                          void* out, float* permuted_probs, int64_t T, int64_t H, int64_t E,
                          int64_t num_out, moe_stream_t stream);
 
+/* a4  Same permute driven by the router's expert list topk_experts [T,k]    */
+/* int64 (k <= 32, any order): the destination of (t, j) is                  */
+/* map[t, topk_experts[t,j]], so the kernel reads k map entries per token    */
+/* instead of the whole E-entry row. Same output as moe_permute_mask_map;    */
+/* 16-byte rows (H % 8 == 0, aligned pointers), H <= 8192.                   */
+int moe_permute_topk(const void* x, const int64_t* row_id_map_te, const int64_t* topk_experts,
+                     int32_t k, const float* probs, void* out, float* permuted_probs, int64_t T,
+                     int64_t H, int64_t E, int64_t num_out, moe_stream_t stream);
+
 /* a5  Same with an expert-major [E,T] map of int64 (idx_bits 64) or int32   */
 /* (idx_bits 32): kernel_cases/case22_ref_moe_permute_mask_kernel_true.py:   */
 /* 47-69, case21_ref_permute_with_mask_map_trans.py:52-68,                   */

@@ -97,6 +97,11 @@ def test_invalid_arguments_are_rejected_without_launch(lib):
     assert b"4096" in lib.moe_b200_last_error()
     assert lib.moe_grouped_wgrad_dev(16, 16, 16, 10, 8, 64, 64, None, 256, 1 << 30, None) == 1
     assert b"device array" in lib.moe_b200_last_error()
+    # permute from the expert list: 1 <= k <= 32, 16-byte rows
+    pt = lib.moe_permute_topk
+    assert pt(16, 16, 16, 33, None, 16, None, 4, 64, 8, 32, None) == 1
+    assert pt(16, 16, 16, 4, None, 16, None, 4, 60, 8, 32, None) == 1
+    assert pt(None, None, None, 4, None, None, None, 0, 64, 8, 0, None) == 0
     # pull dispatch: groups a multiple of the ranks and at most 1024, 16-byte rows
     pb = (ctypes.c_int64 * 2)(256, 512)
     pd = lib.moe_ep_dispatch_pull

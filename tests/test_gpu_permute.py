@@ -157,6 +157,28 @@ print(" ".join(out))
     assert res["1"] == res["0"] == res["v32"]
 
 
+@pytest.mark.parametrize("t,h,e,k", [(4096, 7168, 256, 8), (333, 1024, 64, 4), (7, 8, 16, 2)])
+def test_permute_from_expert_list_equals_map_permute(cuda_dev, t, h, e, k):
+    """moe_permute_topk (destinations read from the router's [T,k] expert list,
+    in selection order or shuffled) gives the same rows and permuted probs as
+    the map-scanning permute, and both equal the oracle."""
+    import moe_b200
+    g = torch.Generator().manual_seed(t + k)
+    x = torch.randn(t, h, generator=g).to(torch.bfloat16).to(cuda_dev)
+    lg = torch.randn(t, e, generator=g).to(cuda_dev)
+    r = moe_b200.router_topk(lg, k, "softmax", renorm=True, outputs="all")
+    m = moe_b200.row_id_map(r.routing_map)
+    a, pa = moe_b200.permute(x, m.map_te, r.probs, num_out=t * k)
+    b, pb = moe_b200.permute(x, m.map_te, r.probs, num_out=t * k, experts=r.topk_idx)
+    perm = torch.argsort(torch.rand(t, k, generator=g), dim=1).to(cuda_dev)
+    c, pc = moe_b200.permute(x, m.map_te, r.probs, num_out=t * k,
+                             experts=torch.gather(r.topk_idx, 1, perm))
+    assert torch.equal(a, b) and torch.equal(a, c)
+    assert torch.equal(pa, pb) and torch.equal(pa, pc)
+    ref, _ = orc.permute(u16(x), m.map_te.cpu().numpy(), None, t * k)
+    np.testing.assert_array_equal(u16(b), ref)
+
+
 # ------------------------------------------------------------------ a6-a8 unpermute
 def test_unpermute_small_exact(cuda_dev, golden):
     z = golden("case15_unpermute.npz")
