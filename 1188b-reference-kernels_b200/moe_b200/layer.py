@@ -102,19 +102,21 @@ class MoELayer:
         elif logits.shape != (t, e):
             raise ValueError(f"logits must be [{t},{e}]")
         self._ev("start")
+        # outputs="all": the [T,k] expert list lets the permute read k map
+        # entries per token instead of scanning the whole map row
         if logits is None and self.placement is None and ops.router_gemm_fusable(
                 x, router_weight, self.k):
             r = ops.router_gemm_topk(x, router_weight, self.k, "softmax", self.renorm, self.bias,
-                                     outputs="maps")
+                                     outputs="all")
         else:
             if logits is None:
                 logits = ops.router_logits(x, router_weight)
-            r = ops.router_topk(logits, self.k, "softmax", self.renorm, self.bias, outputs="maps",
+            r = ops.router_topk(logits, self.k, "softmax", self.renorm, self.bias, outputs="all",
                                 placement=self.placement)
         rim = ops.row_id_map(r.routing_map, align=1, want_et=False)
         self._ev("routing")
         rows = t * self.k
-        xp, _ = ops.permute(x, rim.map_te, None, num_out=rows)
+        xp, _ = ops.permute(x, rim.map_te, None, num_out=rows, experts=r.topk_idx)
         self._ev("permute")
         self.plan.from_splits(rim.counts, 1)
         y1 = None
