@@ -495,24 +495,37 @@ constexpr uint32_t kPairStageBytes = kPairABytes + kPairBBytes;   // 32 KB
 constexpr uint32_t kEpiBoxBytes = 32 * 32 * 2;            // 32 rows x 32 bf16 columns
 constexpr uint32_t kEpiBytes = 4 * 2 * kEpiBoxBytes;        // 4 warps x 2 buffers = 16 KB
 constexpr size_t kPairSmemBytes = 1024 + kPairStages * kPairStageBytes + 1024 + kEpiBytes;
+// Wide tiles: 256 rows x 512 columns per pair (two N=256 MMAs per K step that
+// share the A tile), one 128x512 fp32 accumulator per CTA (all 512 TMEM
+// columns, so the epilogue does not overlap the next tile's mainloop), and a
+// quarter fewer operand bytes per flop than the 256x256 tile.
+constexpr int kWideStages = 4;
+constexpr int kWideOverlap = 2;  // k-blocks issued half by half at each end of a tile
+constexpr uint32_t kWideBBytes = 256 * BK * 2;                     // 32 KB: this CTA's 256 B rows
+constexpr uint32_t kWideStageBytes = kPairABytes + kWideBBytes;    // 48 KB
+constexpr size_t kWideSmemBytes = 1024 + kWideStages * kWideStageBytes + 1024 + kEpiBytes;
+static_assert(kPairSmemBytes <= 232448 && kWideSmemBytes <= 232448, "shared memory per CTA");
 }  // namespace pairk
 
+template <bool kWide>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmap_a,
                              const __grid_constant__ CUtensorMap tmap_b,
                              const __grid_constant__ CUtensorMap tmap_out, const Params p) {
+  constexpr int kS = kWide ? pairk::kWideStages : pairk::kPairStages;
+  constexpr uint32_t kSB = kWide ? pairk::kWideStageBytes : pairk::kPairStageBytes;
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw_addr = smem_u32(smem_raw);
   const uint32_t base = (raw_addr + 1023u) & ~1023u;
   uint8_t* base_ptr = smem_raw + (base - raw_addr);
-  uint64_t* bars = reinterpret_cast<uint64_t*>(base_ptr + pairk::kPairStages * pairk::kPairStageBytes);
+  uint64_t* bars = reinterpret_cast<uint64_t*>(base_ptr + kS * kSB);
   const uint32_t bar0 = smem_u32(bars);
   auto full_bar = [&](int s) { return bar0 + 8u * s; };
-  auto empty_bar = [&](int s) { return bar0 + 8u * (pairk::kPairStages + s); };
-  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * pairk::kPairStages + a); };
-  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * pairk::kPairStages + 2 + a); };
-  const uint32_t drain_bar = bar0 + 8u * (2 * pairk::kPairStages + 4);
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * pairk::kPairStages + 5);
+  auto empty_bar = [&](int s) { return bar0 + 8u * (kS + s); };
+  auto tfull_bar = [&](int a) { return bar0 + 8u * (2 * kS + a); };
+  auto tempty_bar = [&](int a) { return bar0 + 8u * (2 * kS + 2 + a); };
+  const uint32_t drain_bar = bar0 + 8u * (2 * kS + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * kS + 5);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
 
   const uint32_t rank = cluster_ctarank();
@@ -523,7 +536,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = lane_id();
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < pairk::kPairStages; ++s) {
+    for (int s = 0; s < kS; ++s) {
       mbar_init(full_bar(s), 1);
       mbar_init(empty_bar(s), 1);
     }
@@ -568,9 +581,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                                : l2_policy_evict_normal();
       int stage = 0;
       uint32_t phase = 0;
-      int issued[pairk::kPairStages];
+      int issued[kS];
 #pragma unroll
-      for (int s = 0; s < pairk::kPairStages; ++s) issued[s] = -1;
+      for (int s = 0; s < kS; ++s) issued[s] = -1;
       bool ok = true;
       // Coordinates of this CTA's A rows and B rows for a tile.
       auto coords = [&](const Tile& tl, int& ra, int& rb) {
@@ -580,11 +593,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           return;
         }
         const int wb = p.widx[tl.g] * p.n_w;
-        rb = (p.epilogue == 1) ? wb + tl.n_idx * 128 + static_cast<int>(rank) * p.f_half
-                               : wb + tl.n_idx * p.bn + static_cast<int>(rank) * (p.bn / 2);
+        if (kWide)  // SwiGLU: 256 gate rows (rank 0) / 256 up rows (rank 1); else 256 of 512 rows
+          rb = (p.epilogue == 1) ? wb + tl.n_idx * 256 + static_cast<int>(rank) * p.f_half
+                                 : wb + tl.n_idx * 512 + static_cast<int>(rank) * 256;
+        else
+          rb = (p.epilogue == 1) ? wb + tl.n_idx * 128 + static_cast<int>(rank) * p.f_half
+                                 : wb + tl.n_idx * p.bn + static_cast<int>(rank) * (p.bn / 2);
       };
       // Both CTAs' bytes per stage: 128 A rows each, bn/2 B rows each.
-      const uint32_t tx = 2u * (pairk::kPairABytes + static_cast<uint32_t>(p.bn / 2) * (BK * 2));
+      const uint32_t tx =
+          kWide ? 2u * (pairk::kPairABytes + pairk::kWideBBytes)
+                : 2u * (pairk::kPairABytes + static_cast<uint32_t>(p.bn / 2) * (BK * 2));
       for (long long t = cid; ok; t += ncl) {
         Tile tile;
         if (!walker.locate(t, tile)) break;
@@ -596,7 +615,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          const uint32_t sa = base + stage * pairk::kPairStageBytes;
+          const uint32_t sa = base + stage * kSB;
           const uint32_t sb = sa + pairk::kPairABytes;
           const uint32_t leader_full = map_to_rank(full_bar(stage), 0);
           if (leader) mbar_arrive_expect_tx(full_bar(stage), tx);
@@ -610,7 +629,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_2d_pair(sb, &tmap_b, kb * BK, b0, leader_full, pol_b);
           }
           issued[stage] = static_cast<int>(phase);
-          if (++stage == pairk::kPairStages) {
+          if (++stage == kS) {
             stage = 0;
             phase ^= 1u;
           }
@@ -619,12 +638,12 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (ok) {
         // The pair's MMA releases every stage with a commit that lands in this
         // CTA's shared memory; wait for the last ones before exiting.
-        for (int s = 0; s < pairk::kPairStages; ++s)
+        for (int s = 0; s < kS; ++s)
           if (issued[s] >= 0) wait_drain(empty_bar(s), static_cast<uint32_t>(issued[s]));
       } else {
         raise_abort(abort_flag, p.err, kErrTimeoutProducer);
         if (leader) {
-          for (int s = 0; s < pairk::kPairStages; ++s)
+          for (int s = 0; s < kS; ++s)
             if (issued[s] >= 0) wait_drain(full_bar(s), static_cast<uint32_t>(issued[s]));
         } else {
           // Copies count on the leader's barrier; give them a bounded time to land.
@@ -638,14 +657,108 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else if (warp == 1) {
     // ------------------------------------------------------------ MMA issuer (leader)
     if (leader && lane == 0) {
-      const uint32_t idesc =
-          umma_idesc_bf16_f32(pairk::kPairTileM, p.bn) | (p.b_mn ? kIdescBMajorMN : 0u);
+      const uint32_t idesc = umma_idesc_bf16_f32(pairk::kPairTileM, kWide ? 256 : p.bn) |
+                             (p.b_mn ? kIdescBMajorMN : 0u);
       int stage = 0;
       uint32_t phase = 0;
       int it = 0;
       bool ok = true;
       bool issued_any = false;
-      for (long long t = cid; ok; t += ncl) {
+      if (kWide) {
+        // One accumulator of two 256-column halves, handed to the epilogue
+        // half by half: the last kWideOverlap k-blocks of a tile are issued
+        // for half 0 first (its epilogue then runs while half 1 finishes), and
+        // the first kWideOverlap k-blocks of the next tile for half 0 first
+        // (while the epilogue drains half 1). A stage is released once both
+        // halves have read it. Barriers tfull/tempty(h) belong to half h.
+        long long q0 = 0;  // k-blocks consumed before this tile
+        const int nkb = p.num_kb;
+        const int h_end = min(pairk::kWideOverlap, nkb);
+        const int t_beg = max(h_end, nkb - pairk::kWideOverlap);
+        auto slot = [&](int kb, int& s, uint32_t& ph) {
+          const long long q = q0 + kb;
+          s = static_cast<int>(q % kS);
+          ph = static_cast<uint32_t>((q / kS) & 1);
+        };
+        auto wait_full = [&](int kb) {
+          int s;
+          uint32_t ph;
+          slot(kb, s, ph);
+          if (!mbar_wait_cluster(full_bar(s), ph, abort_flag)) return false;
+          tc_fence_after();
+          return true;
+        };
+        auto mma = [&](int kb, int h0, int h1) {  // halves h0..h1 of k-block kb
+          int s;
+          uint32_t ph;
+          slot(kb, s, ph);
+          const uint32_t sa = base + static_cast<uint32_t>(s) * kSB;
+          const uint32_t sb = sa + pairk::kPairABytes;
+          const uint64_t ad = umma_desc_k_sw128(sa);
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint32_t accum = (kb | k) != 0 ? 1u : 0u;
+            for (int h = h0; h <= h1; ++h)
+              umma_bf16_pair(tmem_base + static_cast<uint32_t>(h * 256),
+                             ad + 2ull * k, umma_desc_k_sw128(sb + h * 16384u) + 2ull * k,
+                             idesc, accum);
+          }
+          issued_any = true;
+        };
+        auto release = [&](int kb) {
+          int s;
+          uint32_t ph;
+          slot(kb, s, ph);
+          umma_commit_pair(empty_bar(s), 0x3);
+        };
+        for (long long t = cid; ok; t += ncl) {
+          Tile tile;
+          if (!walker.locate(t, tile)) break;
+          const uint32_t tph = static_cast<uint32_t>(it & 1);
+          // head: k-blocks [0, h_end), half 0 then half 1
+          ok = mbar_wait_cluster(tempty_bar(0), tph ^ 1u, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          for (int kb = 0; kb < h_end && ok; ++kb) {
+            ok = wait_full(kb);
+            if (ok) mma(kb, 0, 0);
+          }
+          if (!ok) break;
+          if (h_end == nkb) umma_commit_pair(tfull_bar(0), 0x3);
+          ok = mbar_wait_cluster(tempty_bar(1), tph ^ 1u, abort_flag);
+          if (!ok) break;
+          tc_fence_after();
+          for (int kb = 0; kb < h_end; ++kb) {
+            mma(kb, 1, 1);
+            release(kb);
+          }
+          // body: both halves per k-block
+          for (int kb = h_end; kb < t_beg && ok; ++kb) {
+            ok = wait_full(kb);
+            if (!ok) break;
+            mma(kb, 0, 1);
+            release(kb);
+          }
+          if (!ok) break;
+          // tail: k-blocks [t_beg, nkb), half 0 then half 1
+          if (t_beg < nkb) {
+            for (int kb = t_beg; kb < nkb && ok; ++kb) {
+              ok = wait_full(kb);
+              if (ok) mma(kb, 0, 0);
+            }
+            if (!ok) break;
+            umma_commit_pair(tfull_bar(0), 0x3);
+            for (int kb = t_beg; kb < nkb; ++kb) {
+              mma(kb, 1, 1);
+              release(kb);
+            }
+          }
+          umma_commit_pair(tfull_bar(1), 0x3);
+          q0 += nkb;
+          ++it;
+        }
+      }
+      for (long long t = cid; ok && !kWide; t += ncl) {
         Tile tile;
         if (!walker.locate(t, tile)) break;
         const int acc = it & 1;
@@ -662,7 +775,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             break;
           }
           tc_fence_after();
-          const uint32_t sa = base + stage * pairk::kPairStageBytes;
+          const uint32_t sa = base + stage * kSB;
           const uint32_t sb = sa + pairk::kPairABytes;
           const uint64_t ad = umma_desc_k_sw128(sa);
           const uint64_t bd = p.b_mn ? umma_desc_mn_sw128(sb, 8192u) : umma_desc_k_sw128(sb);
@@ -672,7 +785,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             umma_bf16_pair(d_tmem, ad + 2ull * k, bd + bstep * k, idesc, (kb | k) != 0 ? 1u : 0u);
           issued_any = true;
           umma_commit_pair(empty_bar(stage), 0x3);
-          if (++stage == pairk::kPairStages) {
+          if (++stage == kS) {
             stage = 0;
             phase ^= 1u;
           }
@@ -742,13 +855,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (long long t = cid;; t += ncl) {
       Tile tile;
       if (!walker.locate(t, tile)) break;
-      const int acc = it & 1;
+      const int acc = kWide ? 0 : (it & 1);
       const uint32_t aph = static_cast<uint32_t>((it >> 1) & 1);
-      if (!mbar_wait_cluster(tfull_bar(acc), aph, abort_flag)) {
-        ok = false;
-        break;
+      if (!kWide) {
+        if (!mbar_wait_cluster(tfull_bar(acc), aph, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
       }
-      tc_fence_after();
       const int m_local = tile.m_idx * pairk::kPairTileM + static_cast<int>(rank) * 128 + r_in_cta;
       const int64_t row = static_cast<int64_t>(p.row_start[tile.g]) + m_local;
       const bool rvalid = m_local < p.rows[tile.g] && row < p.x_rows;
@@ -757,6 +872,72 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t tbase =
           tmem_base + (static_cast<uint32_t>(quad * 32) << 16) + static_cast<uint32_t>(acc * BN);
       char* orow = static_cast<char*>(p.out) + row * p.n_out * elem_bytes;
+      // Wide tiles, plain epilogue: accumulator columns h*256 + [0,128) hold
+      // output columns n0 + h*128 + [0,128) (rank 0's B rows), h*256 +
+      // [128,256) hold n0 + 256 + h*128 + [0,128) (rank 1's B rows).
+      auto wide_plain_half = [&](int h) {
+        const int n0 = tile.n_idx * 512;
+#pragma unroll 1
+        for (int q8 = 0; q8 < 8; ++q8) {
+          const int col = n0 + ((q8 >> 2) << 8) + h * 128 + (q8 & 3) * 32;
+          if (col >= p.n_out) continue;  // warp-uniform
+          uint32_t r[32];
+          tmem_ld_32x32b_x32(tbase + h * 256 + q8 * 32, r);
+          tmem_ld_wait();
+          uint32_t o[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q)
+            o[q] = pack_bf16x2(__uint_as_float(r[2 * q]), __uint_as_float(r[2 * q + 1]));
+          emit(o, tma, row, col, warp_row0, orow, rvalid);
+        }
+      };
+      // Wide tiles, SwiGLU: accumulator columns h*256 + [0,128) are gate and
+      // h*256 + [128,256) up of output columns n0 + h*128 + [0,128).
+      auto wide_swiglu_half = [&](int h) {
+        const int n0 = tile.n_idx * 256;
+#pragma unroll 1
+        for (int q4 = 0; q4 < 4; ++q4) {
+          const int col = n0 + h * 128 + q4 * 32;
+          if (col >= p.n_out) continue;  // warp-uniform
+          uint32_t gr[32], ur[32];
+          tmem_ld_32x32b_x32(tbase + h * 256 + q4 * 32, gr);
+          tmem_ld_32x32b_x32(tbase + h * 256 + 128 + q4 * 32, ur);
+          tmem_ld_wait();
+          uint32_t o[16];
+#pragma unroll
+          for (int q = 0; q < 16; ++q) {
+            const float h0 = swiglu_f32(round_bf16(__uint_as_float(gr[2 * q])),
+                                        round_bf16(__uint_as_float(ur[2 * q])));
+            const float h1 = swiglu_f32(round_bf16(__uint_as_float(gr[2 * q + 1])),
+                                        round_bf16(__uint_as_float(ur[2 * q + 1])));
+            o[q] = pack_bf16x2(h0, h1);
+          }
+          emit(o, tma, row, col, warp_row0, orow, rvalid);
+        }
+      };
+      if (kWide) {
+        // Half h of the accumulator (columns h*256 ..) as soon as the MMA
+        // hands it over; its columns are free for the next tile once this
+        // CTA's four warps and the partner's have arrived.
+        const uint32_t tph = static_cast<uint32_t>(it & 1);
+        for (int h = 0; h < 2; ++h) {
+          if (!mbar_wait_cluster(tfull_bar(h), tph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          if (p.epilogue == 0)
+            wide_plain_half(h);
+          else
+            wide_swiglu_half(h);
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive_cluster(h == 0 ? leader_tempty0 : leader_tempty1);
+        }
+        if (!ok) break;
+        ++it;
+        continue;
+      }
       if (p.epilogue == 2) {
         const int n0 = tile.n_idx * p.bn;
 #pragma unroll 1
@@ -998,8 +1179,12 @@ int pair_clusters(int dev) {
   std::lock_guard<std::mutex> lock(mu);
   if (dev >= 0 && dev < 64 && init[dev]) return cache[dev];
   int n = 0;
-  if (cudaFuncSetAttribute(grouped_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           static_cast<int>(pairk::kPairSmemBytes)) == cudaSuccess) {
+  if (cudaFuncSetAttribute(grouped_gemm_pair_kernel<false>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(pairk::kPairSmemBytes)) == cudaSuccess &&
+      cudaFuncSetAttribute(grouped_gemm_pair_kernel<true>,
+                           cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           static_cast<int>(pairk::kWideSmemBytes)) == cudaSuccess) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(2 * 74);
     cfg.blockDim = dim3(kThreads);
@@ -1011,7 +1196,11 @@ int pair_clusters(int dev) {
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    if (cudaOccupancyMaxActiveClusters(&n, grouped_gemm_pair_kernel, &cfg) != cudaSuccess) n = 0;
+    int nw = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, grouped_gemm_pair_kernel<false>, &cfg) != cudaSuccess ||
+        cudaOccupancyMaxActiveClusters(&nw, grouped_gemm_pair_kernel<true>, &cfg) != cudaSuccess)
+      n = 0;
+    n = std::min(n, nw);
   }
   cudaGetLastError();  // clear a non-sticky error from an unsupported query
   if (dev >= 0 && dev < 64) {
@@ -1026,6 +1215,13 @@ int pair_clusters(int dev) {
 // measured fc1 slab of 58.7 MB did not, the fc2 slab of 29.4 MB did).
 constexpr int64_t kSlabChunkBytes = 32ll << 20;
 constexpr int kNChunkDefault = -1;
+// Wide pair tiles (256x512) against square ones (256x256), measured in the
+// layer at the 1 kW cap, interleaved in one process: fc1 (K=7168) 6.82-6.86
+// against 7.28 ms, fc2 (K=2048) 3.78 against 3.55-3.73 ms. With a single
+// accumulator the epilogue overlaps only the first and last k-blocks of a
+// tile, which hides it when the reduction is long.
+constexpr int kWideDefault = 1;
+constexpr int64_t kWideMinK = 4096;
 
 int env_int(const char* name, int def, int lo, int hi) {
   const char* e = getenv(name);
@@ -1233,18 +1429,36 @@ static int grouped_gemm_run(const void* x, const void* w, void* out, int64_t x_r
         if (st) return st;
       }
     }
+    // Wide 256x512 tiles where N (or F for SwiGLU) is a whole number of them
+    // and the reduction is deep enough to hide most of their epilogue:
+    // MOE_GEMM_WIDE=1 (default) for K >= kWideMinK, 2 for every K, 0 never.
+    static const int wide_env = gg::env_int("MOE_GEMM_WIDE", gg::kWideDefault, 0, 2);
+    const bool wide = wide_env != 0 && !b_mn && (wide_env == 2 || K >= gg::kWideMinK) &&
+                      ((epilogue == 0 && N % 512 == 0) || (epilogue == 1 && p.f_half % 256 == 0));
+    if (wide) {
+      st = gg::make_tmap_box(&tbp, w, static_cast<uint64_t>(K), static_cast<uint64_t>(num_w * N),
+                             static_cast<uint32_t>(gg::BK), 256u, CU_TENSOR_MAP_SWIZZLE_128B);
+      if (st) return st;
+      pb.bn = 512;
+      pb.n_tiles = epilogue == 1 ? p.f_half / 256 : static_cast<int>(N / 512);
+      cfg.dynamicSmemBytes = gg::pairk::kWideSmemBytes;
+    }
     // Weight-slab chunks: MOE_GEMM_NCHUNK=-1 picks the most N-tiles whose
     // weight rows fit in kSlabChunkBytes, k > 0 takes k N-tiles, 0 keeps the
     // super-rows of MOE_GEMM_RASTER.
     static const int nchunk_env = gg::env_int("MOE_GEMM_NCHUNK", gg::kNChunkDefault, -1, 1024);
     if (nchunk_env != 0) {
-      const int64_t ntile_bytes = (epilogue == 1 ? 256 : pb.bn) * K * 2;
+      const int64_t ntile_bytes = (wide ? 512 : epilogue == 1 ? 256 : pb.bn) * K * 2;
       const int64_t fit = std::max<int64_t>(1, gg::kSlabChunkBytes / ntile_bytes);
       pb.n_chunk = static_cast<int>(
           std::min<int64_t>(pb.n_tiles, nchunk_env > 0 ? nchunk_env : fit));
     }
-    MOE_CUDA_CALL(cudaLaunchKernelEx(&cfg, gg::grouped_gemm_pair_kernel, ta, tbp, to, pb),
-                  "grouped_gemm pair launch");
+    if (wide)
+      MOE_CUDA_CALL(cudaLaunchKernelEx(&cfg, gg::grouped_gemm_pair_kernel<true>, ta, tbp, to, pb),
+                    "grouped_gemm wide pair launch");
+    else
+      MOE_CUDA_CALL(cudaLaunchKernelEx(&cfg, gg::grouped_gemm_pair_kernel<false>, ta, tbp, to, pb),
+                    "grouped_gemm pair launch");
     if (!split) return MOE_OK;
     // Remainders of every group (< 256 rows) on 128-row single-CTA tiles.
     gg::Params pt = p;

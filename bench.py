@@ -96,13 +96,15 @@ def parse_args():
                          "chunks and dispatch chunk c+1 over NVLink while chunk c's GEMMs run "
                          "(1 = no overlap)")
     ap.add_argument("--workload", choices=["layer", "router_gemm", "backward", "wgrad",
-                                           "rowcopy"],
+                                           "rowcopy", "dense_gemm"],
                     default="layer",
                     help="layer: the MoE expert-layer forward (the headline); router_gemm: the "
                          "router gate GEMM that produces its logits; backward: the layer's "
                          "grouped dgrad and wgrad GEMMs; wgrad: the grouped wgrad alone at "
                          "--wgrad-shape; rowcopy: the layer's permute and weighted combine "
-                         "alone, with no expert weights on the device (one GPU)")
+                         "alone, with no expert weights on the device (one GPU); dense_gemm: "
+                         "the expert GEMMs on one dense group of tokens*topk rows against "
+                         "cuBLAS (torch.matmul) on the same operands (one GPU)")
     ap.add_argument("--wgrad-shape", default="40,4096,5120,8192",
                     help="G,T,N,K of --workload wgrad (uniform groups; default: the traced "
                          "shape of kernel_cases/case09_moe_grouped_gemm_fc1_wgrad.py)")
@@ -746,6 +748,98 @@ def run_wgrad(a):
     print(json.dumps(line), flush=True)
 
 
+def run_dense_gemm(a):
+    """The expert GEMMs' kernel against cuBLAS on the same dense problems: one
+    group of T*k rows through moe_b200.grouped_gemm (fc1 [rows,H]x[2F,H]^T
+    with the SwiGLU and the plain epilogue, fc2 [rows,F]x[H,F]^T) and
+    torch.matmul on the same operands (cuBLAS), in interleaved windows so both
+    see the same power-capped clock. Per arm: median ms per call, TFLOP/s,
+    median SM clock of its windows and flops per SM cycle; the outputs of the
+    plain fc1 and fc2 are compared bit for bit with cuBLAS's."""
+    import statistics
+    import torch
+    import moe_b200
+    from moe_b200 import _lib, ops
+    t, h, f, k = a.tokens, a.hidden, a.ffn, a.topk
+    rows = t * k
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    moe_b200.load_library()
+    g = torch.Generator(device=dev)
+    g.manual_seed(5)
+    x = torch.randn(rows, h, device=dev, generator=g).to(torch.bfloat16)
+    w1 = (torch.randn(1, 2 * f, h, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(1, h, f, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+    hm = torch.randn(rows, f, device=dev, generator=g).to(torch.bfloat16)
+    plan = ops.GroupedGemmPlan(1, dev).from_splits(torch.tensor([rows], dtype=torch.int32))
+    o_sw = torch.empty(rows, f, dtype=torch.bfloat16, device=dev)
+    o1, c1 = (torch.empty(rows, 2 * f, dtype=torch.bfloat16, device=dev) for _ in range(2))
+    o2, c2 = (torch.empty(rows, h, dtype=torch.bfloat16, device=dev) for _ in range(2))
+    arms = {
+        "fc1_swiglu": lambda: ops.grouped_gemm(x, w1, epilogue="swiglu", plan=plan, out=o_sw),
+        "fc1": lambda: ops.grouped_gemm(x, w1, plan=plan, out=o1),
+        "fc1_cublas": lambda: torch.matmul(x, w1[0].t(), out=c1),
+        "fc2": lambda: ops.grouped_gemm(hm, w2, plan=plan, out=o2),
+        "fc2_cublas": lambda: torch.matmul(hm, w2[0].t(), out=c2),
+    }
+    flops = {"fc1_swiglu": 2.0 * rows * 2 * f * h, "fc1": 2.0 * rows * 2 * f * h,
+             "fc1_cublas": 2.0 * rows * 2 * f * h, "fc2": 2.0 * rows * h * f,
+             "fc2_cublas": 2.0 * rows * h * f}
+    sampler = ClockSampler(os.environ.get("CUDA_VISIBLE_DEVICES", "0").split(",")[0])
+    sampler.start()
+    for _ in range(a.warmup):
+        for fn in arms.values():
+            fn()
+    t_end = time.time() + a.settle_s  # run into the power-capped clock first
+    while time.time() < t_end:
+        for fn in arms.values():
+            fn()
+        torch.cuda.synchronize()
+    times = {n: [] for n in arms}
+    launches0 = _lib.launch_count
+    per = max(1, a.steps // 4)
+    for _ in range(4):
+        for n, fn in arms.items():
+            evs = [torch.cuda.Event(enable_timing=True) for _ in range(per + 1)]
+            torch.cuda.synchronize()
+            w0 = time.time()
+            evs[0].record()
+            for i in range(per):
+                fn()
+                evs[i + 1].record()
+            torch.cuda.synchronize()
+            sampler.mark(w0, time.time(), n)
+            times[n] += [evs[i].elapsed_time(evs[i + 1]) for i in range(per)]
+    launches = _lib.launch_count - launches0
+    clocks = sampler.stop() or {}
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    res = {}
+    for n in arms:
+        ms = statistics.median(times[n])
+        mhz = clocks.get("windows", {}).get(n, {}).get("sm_mhz")
+        tf = flops[n] / (ms / 1e3) / 1e12
+        res[n] = {"ms": round(ms, 4), "tflops": round(tf, 1), "sm_mhz": mhz,
+                  "flop_per_sm_cycle": round(tf * 1e12 / (mhz * 1e6) / sms) if mhz else None}
+    same = {"fc1": bool(torch.equal(o1, c1)), "fc2": bool(torch.equal(o2, c2))}
+    peaks, peak_kind = load_peaks()
+    peak = float(peaks.get("bf16_tflops_sustained", FALLBACK_PEAKS["bf16_tflops_sustained"]))
+    line = {"metric": "dense expert GEMM TFLOP/s (fc1 with SwiGLU)", "value": res["fc1_swiglu"]["tflops"],
+            "unit": "TFLOP/s", "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,
+            "ms_per_step": res["fc1_swiglu"]["ms"], "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (N(0,1))",
+            "config": {"workload": "dense_gemm", "rows": rows, "hidden": h, "ffn": f,
+                       "l2": "no flush: operands larger than L2"},
+            "arms": res, "vs_cublas": {"fc1": round(res["fc1_cublas"]["ms"] / res["fc1"]["ms"], 4),
+                                       "fc2": round(res["fc2_cublas"]["ms"] / res["fc2"]["ms"], 4)},
+            "bit_equal_to_cublas": same,
+            "roofline": {"bound": "tensor", "kernel": "grouped_gemm_pair_kernel (fc1, SwiGLU)",
+                         "achieved": res["fc1_swiglu"]["tflops"], "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(res["fc1_swiglu"]["tflops"] / peak, 4), "traffic": None},
+            "peak_kind": f"sustained bf16, of {peak_kind}",
+            "cpu_baseline": None, "e2e": None, "gpu_launches": launches, "clocks": clocks}
+    print(json.dumps(line), flush=True)
+
+
 # --------------------------------------------------------------------------- GPU arm
 def read_traffic():
     p = ROOT / "profiles" / "grouped_gemm_fc1_layer.txt"
@@ -904,6 +998,10 @@ def main():
     if a.workload == "rowcopy":
         if rank == 0 and a.impl != "reference":
             run_rowcopy(a)
+        return
+    if a.workload == "dense_gemm":
+        if rank == 0 and a.impl != "reference":
+            run_dense_gemm(a)
         return
     if a.impl == "reference":
         run_reference_arm(a, world, rank)

@@ -391,6 +391,39 @@ def test_standalone_swiglu_golden(cuda_dev, golden):
     np.testing.assert_array_equal(u16(h), orc.swiglu(z["swiglu_y"]))
 
 
+def test_swiglu_accuracy_wide_range(cuda_dev):
+    """The device SwiGLU (hardware exp2 with the product's rounding error
+    carried by an FMA, rcp with one Newton step) against silu(g)*u computed
+    in float64 and rounded once to bf16, on 2M (gate, up) pairs with gates
+    over [-30, 30] plus zeros, +-1e-3 and the clamp edges: every output
+    within one bf16 ulp of the float64 rounding, at least 99.9 % equal to it,
+    and at least as often equal to it as the float32 numpy restatement
+    (exp, IEEE division) is."""
+    import moe_b200
+    g = torch.Generator().manual_seed(21)
+    n = 1 << 20
+    gate = torch.cat([torch.rand(n, generator=g) * 60 - 30, torch.randn(n - 8, generator=g),
+                      torch.tensor([0.0, -0.0, 1e-3, -1e-3, 87.0, -87.0, 100.0, -86.0])])
+    up = torch.randn(2 * n, generator=g)
+    y = torch.stack([gate, up]).to(torch.bfloat16)  # [2, 2n]: y.chunk(2, -1) per row
+    y = torch.cat([y[0].view(-1, 1024), y[1].view(-1, 1024)], dim=1)  # [rows, 2048]
+    h = u16(moe_b200.swiglu(y.to(cuda_dev)))
+    yu = u16(y)
+    gf = orc.bf16_to_f32(yu[:, :1024]).astype(np.float64)
+    uf = orc.bf16_to_f32(yu[:, 1024:]).astype(np.float64)
+    exact = orc.f32_to_bf16((gf / (1.0 + np.exp(-gf)) * uf).astype(np.float32))
+    # ulp distance in bf16 bit patterns of the same sign (zeros compare equal)
+    def dist(a, b):
+        sa = np.where(a & 0x8000, -(a.astype(np.int32) & 0x7FFF), a.astype(np.int32) & 0x7FFF)
+        sb = np.where(b & 0x8000, -(b.astype(np.int32) & 0x7FFF), b.astype(np.int32) & 0x7FFF)
+        return np.abs(sa - sb)
+    d_dev = dist(h, exact)
+    d_np = dist(orc.swiglu(yu), exact)
+    assert d_dev.max() <= 1, int(d_dev.max())
+    assert (d_dev == 0).mean() >= 0.999, float((d_dev == 0).mean())
+    assert (d_dev == 0).mean() >= (d_np == 0).mean() - 1e-4, ((d_dev == 0).mean(), (d_np == 0).mean())
+
+
 def test_aligned_segments(cuda_dev):
     """Groups starting on 128-row boundaries (padded permute layout)."""
     import moe_b200
@@ -577,3 +610,61 @@ print("OK")
                         str(ROOT), str(ROOT / "tests")], env=env, capture_output=True, text=True,
                        timeout=300)
     assert r.returncode == 0 and "OK" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
+
+
+_WIDE_CODE = r'''
+import sys, hashlib, numpy as np, torch
+sys.path[:0] = [sys.argv[1], sys.argv[2], sys.argv[3]]
+import moe_b200
+from test_gpu_gemm import fp32_ref, assert_gemm_close, _rand_bf16
+from conftest import u16
+dev = torch.device("cuda", 0)
+g = torch.Generator().manual_seed(3)
+out = []
+# ragged groups: empty, single-row, around the 256-row pair tile, large
+splits = [0, 1, 255, 256, 257, 600, 0, 5, 1000]
+x = _rand_bf16(g, sum(splits), 256)
+w = _rand_bf16(g, len(splits), 1024, 256, std=0.05)
+y = moe_b200.grouped_gemm(x.to(dev), w.to(dev), splits)
+assert_gemm_close(y, fp32_ref(u16(x), u16(w), splits), "plain N=1024")
+h = moe_b200.grouped_gemm(x.to(dev), w.to(dev), splits, epilogue="swiglu")
+assert_gemm_close(h, fp32_ref(u16(x), u16(w), splits, swiglu=True), "swiglu F=512", ulp_frac=0.995)
+out += [y, h]
+# the layer's fc2 and fc1 shapes (K=2048, N=7168; K=7168, N=2F=4096) on two experts
+s2 = [700, 300]
+x2 = _rand_bf16(g, sum(s2), 2048)
+w2 = _rand_bf16(g, 2, 7168, 2048, std=0.02)
+out.append(moe_b200.grouped_gemm(x2.to(dev), w2.to(dev), s2))
+x1 = _rand_bf16(g, sum(s2), 7168)
+w1 = _rand_bf16(g, 2, 4096, 7168, std=0.02)
+out.append(moe_b200.grouped_gemm(x1.to(dev), w1.to(dev), s2, epilogue="swiglu"))
+torch.cuda.synchronize()
+print("SHA", hashlib.sha256(b"".join(t.cpu().view(torch.int16).numpy().tobytes() for t in out)).hexdigest())
+'''
+
+
+def test_wide_tiles_equal_square_tiles():
+    """The pair kernel's 256x512 tiles (MOE_GEMM_WIDE=2, every K: two N=256
+    MMAs per K step sharing the A tile, one accumulator per CTA handed to the
+    epilogue half by half) against its 256x256 tiles (MOE_GEMM_WIDE=0), each
+    in a fresh process: ragged groups with the
+    bf16 and SwiGLU epilogues within the GEMM tolerance of the fp32 reference,
+    and every output bit for bit equal between the two tile shapes (each
+    output element is accumulated over K in the same order), at a small shape
+    and at the layer's fc1/fc2 shapes."""
+    import os
+    import subprocess
+    import sys
+    from conftest import ROOT
+    if not torch.cuda.is_available():
+        pytest.fail("GPU test selected but no CUDA device is visible")
+    sha = {}
+    for wide in ("0", "1"):
+        env = dict(os.environ, MOE_GEMM_WIDE="2" if wide == "1" else "0")
+        r = subprocess.run([sys.executable, "-c", _WIDE_CODE,
+                            str(ROOT / "1188b-reference-kernels_b200"), str(ROOT),
+                            str(ROOT / "tests")], env=env, capture_output=True, text=True,
+                           timeout=300)
+        assert r.returncode == 0 and "SHA" in r.stdout, r.stdout[-2000:] + r.stderr[-2000:]
+        sha[wide] = r.stdout.split("SHA")[1].split()[0]
+    assert sha["0"] == sha["1"], sha
