@@ -19,7 +19,11 @@
 //     2) on 256-row tiles, epilogue through 64B-swizzled shared buffers and
 //     TMA tile stores; it takes every group of at least 256 rows, its last
 //     partial tile row-predicated. Inside a group it walks the N-tiles in
-//     chunks of at most 32 MB of weights, all M-tiles per chunk.
+//     chunks of at most 32 MB of weights, all M-tiles per chunk. Its tiles
+//     are 256 columns wide with two alternating accumulators, or, for deep
+//     reductions (K >= 4096), 512 columns wide (two MMAs per K step sharing
+//     the A tile, a quarter fewer operand bytes per flop) with one
+//     accumulator that is handed to the epilogue half by half.
 //   grouped_gemm_kernel: one CTA per SM on 128-row tiles; it takes the groups
 //     of fewer than 256 rows after the pair kernel, or everything when CTA
 //     pairs cannot be scheduled.
