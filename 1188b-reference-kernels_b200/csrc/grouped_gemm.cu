@@ -593,7 +593,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       auto coords = [&](const Tile& tl, int& ra, int& rb) {
         ra = p.row_start[tl.g] + tl.m_idx * pairk::kPairTileM + static_cast<int>(rank) * 128;
         if (p.b_mn) {  // first output column of this CTA's half; rows follow kb
-          rb = tl.n_idx * p.bn + static_cast<int>(rank) * (p.bn / 2);
+          rb = kWide ? tl.n_idx * 512 + static_cast<int>(rank) * 256
+                     : tl.n_idx * p.bn + static_cast<int>(rank) * (p.bn / 2);
           return;
         }
         const int wb = p.widx[tl.g] * p.n_w;
@@ -626,8 +627,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           tma_load_2d_pair(sa, &tmap_a, kb * BK, row0, leader_full, pol_a);
           if (p.b_mn) {
             const int wrow = wrow0 + kb * BK;
+            // this CTA's 128 (wide: 256) columns as 64-column boxes
 #pragma unroll
-            for (int j = 0; j < 2; ++j)  // this CTA's 128 columns as two 64-column boxes
+            for (int j = 0; j < (kWide ? 4 : 2); ++j)
               tma_load_2d_pair(sb + j * 8192u, &tmap_b, b0 + j * 64, wrow, leader_full, pol_b);
           } else {
             tma_load_2d_pair(sb, &tmap_b, kb * BK, b0, leader_full, pol_b);
@@ -699,13 +701,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t sa = base + static_cast<uint32_t>(s) * kSB;
           const uint32_t sb = sa + pairk::kPairABytes;
           const uint64_t ad = umma_desc_k_sw128(sa);
+          // half h reads this CTA's B rows (or MN-major columns) h*128.. at +16 KB
+          const uint64_t bstep = p.b_mn ? 128ull : 2ull;
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k) {
             const uint32_t accum = (kb | k) != 0 ? 1u : 0u;
-            for (int h = h0; h <= h1; ++h)
-              umma_bf16_pair(tmem_base + static_cast<uint32_t>(h * 256),
-                             ad + 2ull * k, umma_desc_k_sw128(sb + h * 16384u) + 2ull * k,
-                             idesc, accum);
+            for (int h = h0; h <= h1; ++h) {
+              const uint32_t sbh = sb + static_cast<uint32_t>(h) * 16384u;
+              const uint64_t bd = p.b_mn ? umma_desc_mn_sw128(sbh, 8192u) : umma_desc_k_sw128(sbh);
+              umma_bf16_pair(tmem_base + static_cast<uint32_t>(h * 256), ad + 2ull * k,
+                             bd + bstep * k, idesc, accum);
+            }
           }
           issued_any = true;
         };
@@ -1437,12 +1443,15 @@ static int grouped_gemm_run(const void* x, const void* w, void* out, int64_t x_r
     // and the reduction is deep enough to hide most of their epilogue:
     // MOE_GEMM_WIDE=1 (default) for K >= kWideMinK, 2 for every K, 0 never.
     static const int wide_env = gg::env_int("MOE_GEMM_WIDE", gg::kWideDefault, 0, 2);
-    const bool wide = wide_env != 0 && !b_mn && (wide_env == 2 || K >= gg::kWideMinK) &&
-                      ((epilogue == 0 && N % 512 == 0) || (epilogue == 1 && p.f_half % 256 == 0));
-    if (wide) {
+    const bool wide = wide_env != 0 && (wide_env == 2 || K >= gg::kWideMinK) &&
+                      ((epilogue == 0 && N % 512 == 0) ||
+                       (epilogue == 1 && !b_mn && p.f_half % 256 == 0));
+    if (wide && !b_mn) {  // one 256-row box per CTA; MN-major B keeps its 64x64 boxes
       st = gg::make_tmap_box(&tbp, w, static_cast<uint64_t>(K), static_cast<uint64_t>(num_w * N),
                              static_cast<uint32_t>(gg::BK), 256u, CU_TENSOR_MAP_SWIZZLE_128B);
       if (st) return st;
+    }
+    if (wide) {
       pb.bn = 512;
       pb.n_tiles = epilogue == 1 ? p.f_half / 256 : static_cast<int>(N / 512);
       cfg.dynamicSmemBytes = gg::pairk::kWideSmemBytes;

@@ -638,6 +638,14 @@ out.append(moe_b200.grouped_gemm(x2.to(dev), w2.to(dev), s2))
 x1 = _rand_bf16(g, sum(s2), 7168)
 w1 = _rand_bf16(g, 2, 4096, 7168, std=0.02)
 out.append(moe_b200.grouped_gemm(x1.to(dev), w1.to(dev), s2, epilogue="swiglu"))
+# the dgrad form (x @ w[g] with w [G,K,N], B staged MN-major): ragged, and the
+# layer's fc1 dgrad shape (K=2F=4096, N=H=7168)
+wk = _rand_bf16(g, len(splits), 256, 1024, std=0.05)
+d = moe_b200.grouped_gemm(x.to(dev), wk.to(dev), splits, w_layout="KN")
+assert_gemm_close(d, fp32_ref(u16(x), u16(wk), splits, w_layout="KN"), "KN N=1024")
+out.append(d)
+xd = _rand_bf16(g, sum(s2), 4096)
+out.append(moe_b200.grouped_gemm(xd.to(dev), w1.to(dev), s2, w_layout="KN"))
 torch.cuda.synchronize()
 print("SHA", hashlib.sha256(b"".join(t.cpu().view(torch.int16).numpy().tobytes() for t in out)).hexdigest())
 '''
@@ -647,11 +655,11 @@ def test_wide_tiles_equal_square_tiles():
     """The pair kernel's 256x512 tiles (MOE_GEMM_WIDE=2, every K: two N=256
     MMAs per K step sharing the A tile, one accumulator per CTA handed to the
     epilogue half by half) against its 256x256 tiles (MOE_GEMM_WIDE=0), each
-    in a fresh process: ragged groups with the
-    bf16 and SwiGLU epilogues within the GEMM tolerance of the fp32 reference,
-    and every output bit for bit equal between the two tile shapes (each
-    output element is accumulated over K in the same order), at a small shape
-    and at the layer's fc1/fc2 shapes."""
+    in a fresh process: ragged groups with the bf16 and SwiGLU epilogues and
+    the dgrad form (weight staged MN-major) within the GEMM tolerance of the
+    fp32 reference, and every output bit for bit equal between the two tile
+    shapes (each output element is accumulated over K in the same order), at
+    small shapes and at the layer's fc1/fc2/fc1-dgrad shapes."""
     import os
     import subprocess
     import sys
