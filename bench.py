@@ -489,6 +489,15 @@ def run_router_gemm(a):
         fused["unfused_router_us"] = round(timed(lambda: moe_b200.router_topk(
             moe_b200.router_logits(x, w, out=out), 8, "softmax", True, outputs="maps")), 2)
         fused["device_error"] = moe_b200.router_device_error(dev)
+    # cuBLAS on the same operands (torch.matmul, bf16 out; fp32 out where
+    # this torch build offers it), for the GEMM alone
+    cb = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    fused["cublas_bf16_out_us"] = round(timed(lambda: torch.matmul(x, w.t(), out=cb)), 2)
+    try:
+        fused["cublas_fp32_out_us"] = round(timed(
+            lambda: torch.mm(x, w.t(), out_dtype=torch.float32)), 2)
+    except (TypeError, RuntimeError):
+        pass
     clocks = sampler.stop()
     peaks, peak_kind = load_peaks()
     peak = float(peaks.get("bf16_tflops", FALLBACK_PEAKS["bf16_tflops"]))
