@@ -447,11 +447,12 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
                   const int j = v * 8 + 2 * q;
-                  const float h0 = swiglu_f32(round_bf16(__uint_as_float(gr[j])),
-                                              round_bf16(__uint_as_float(ur[j])));
-                  const float h1 = swiglu_f32(round_bf16(__uint_as_float(gr[j + 1])),
-                                              round_bf16(__uint_as_float(ur[j + 1])));
-                  o[q] = pack_bf16x2(h0, h1);
+                  const float2 h = swiglu2_f32(
+                      make_float2(round_bf16(__uint_as_float(gr[j])),
+                                  round_bf16(__uint_as_float(gr[j + 1]))),
+                      make_float2(round_bf16(__uint_as_float(ur[j])),
+                                  round_bf16(__uint_as_float(ur[j + 1]))));
+                  o[q] = pack_bf16x2(h.x, h.y);
                 }
                 *reinterpret_cast<uint4*>(orow + col) = make_uint4(o[0], o[1], o[2], o[3]);
               }
@@ -916,11 +917,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t o[16];
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
-            const float h0 = swiglu_f32(round_bf16(__uint_as_float(gr[2 * q])),
-                                        round_bf16(__uint_as_float(ur[2 * q])));
-            const float h1 = swiglu_f32(round_bf16(__uint_as_float(gr[2 * q + 1])),
-                                        round_bf16(__uint_as_float(ur[2 * q + 1])));
-            o[q] = pack_bf16x2(h0, h1);
+            const float2 h = swiglu2_f32(
+                make_float2(round_bf16(__uint_as_float(gr[2 * q])),
+                            round_bf16(__uint_as_float(gr[2 * q + 1]))),
+                make_float2(round_bf16(__uint_as_float(ur[2 * q])),
+                            round_bf16(__uint_as_float(ur[2 * q + 1]))));
+            o[q] = pack_bf16x2(h.x, h.y);
           }
           emit(o, tma, row, col, warp_row0, orow, rvalid);
         }
@@ -995,11 +997,12 @@ __global__ void __launch_bounds__(kThreads, 1)
           uint32_t o[16];
 #pragma unroll
           for (int q = 0; q < 16; ++q) {
-            const float h0 = swiglu_f32(round_bf16(__uint_as_float(gr[2 * q])),
-                                        round_bf16(__uint_as_float(ur[2 * q])));
-            const float h1 = swiglu_f32(round_bf16(__uint_as_float(gr[2 * q + 1])),
-                                        round_bf16(__uint_as_float(ur[2 * q + 1])));
-            o[q] = pack_bf16x2(h0, h1);
+            const float2 h = swiglu2_f32(
+                make_float2(round_bf16(__uint_as_float(gr[2 * q])),
+                            round_bf16(__uint_as_float(gr[2 * q + 1]))),
+                make_float2(round_bf16(__uint_as_float(ur[2 * q])),
+                            round_bf16(__uint_as_float(ur[2 * q + 1]))));
+            o[q] = pack_bf16x2(h.x, h.y);
           }
           emit(o, tma, row, col, warp_row0, orow, rvalid);
         }

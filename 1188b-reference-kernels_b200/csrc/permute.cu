@@ -405,9 +405,11 @@ __global__ void swiglu_kernel(const uint4* __restrict__ y, uint4* __restrict__ h
   const uint32_t gg[4] = {g.x, g.y, g.z, g.w}, uu[4] = {u.x, u.y, u.z, u.w};
   uint32_t o[4];
 #pragma unroll
-  for (int k = 0; k < 4; ++k)
-    o[k] = pack_bf16x2(swiglu_f32(bf16_lo(gg[k]), bf16_lo(uu[k])),
-                       swiglu_f32(bf16_hi(gg[k]), bf16_hi(uu[k])));
+  for (int k = 0; k < 4; ++k) {
+    const float2 hh = swiglu2_f32(make_float2(bf16_lo(gg[k]), bf16_hi(gg[k])),
+                                  make_float2(bf16_lo(uu[k]), bf16_hi(uu[k])));
+    o[k] = pack_bf16x2(hh.x, hh.y);
+  }
   h[i] = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
